@@ -1,0 +1,236 @@
+/* ============================================================================
+ *  tinygnn_b200.h -- the C ABI of the B200 GNN inference engine.
+ *
+ *  Every entry point is extern "C", takes plain pointers and sizes, and
+ *  returns a tg_status; on failure tg_last_error_message() gives the text,
+ *  worded like the TinyGNN exception it stands for.  No C++ or torch type
+ *  crosses this boundary.
+ *
+ *  Two levels:
+ *   1. Device-pointer entry points (tg_spmm_f32, tg_gemm_f32, ...).  Every
+ *      pointer is device memory; nothing is synchronised unless stated; work
+ *      is queued on `stream` (a cudaStream_t, NULL = legacy default stream).
+ *      Dense matrices are row-major with an explicit leading dimension (ld,
+ *      in elements, >= the logical column count).  Results match the
+ *      TinyGNN CPU library bit for bit where the entry point says "exact".
+ *   2. Handle entry points (tg_tensor_*, tg_model_*), the surface TinyGNN's
+ *      own binding (python/tinygnn_ext.cpp) exposes: tensors built from host
+ *      arrays, layers/Model, forward on host inputs.
+ *
+ *  References are to TinyGNN source files, path:line.
+ * ========================================================================== */
+#ifndef TINYGNN_B200_H
+#define TINYGNN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define TG_API __attribute__((visibility("default")))
+#else
+#define TG_API
+#endif
+
+/* Error model: TinyGNN throws std::invalid_argument for shape/format/bounds
+ * violations (src/ops.cpp:73-98, src/tensor.cpp:46-86), std::out_of_range
+ * for Tensor::at (src/tensor.cpp:137) and std::runtime_error for I/O and an
+ * empty Model (src/model.cpp:52,262,361). */
+typedef enum tg_status {
+    TG_OK = 0,
+    TG_ERR_INVALID_ARGUMENT = 1, /* std::invalid_argument */
+    TG_ERR_OUT_OF_RANGE = 2,     /* std::out_of_range */
+    TG_ERR_RUNTIME = 3,          /* std::runtime_error */
+    TG_ERR_CUDA = 4,             /* a CUDA runtime call failed */
+    TG_ERR_NCCL = 5,             /* a collective failed */
+    TG_ERR_TIMEOUT = 6,          /* a bounded device or host wait ran out */
+    TG_ERR_DEVICE_CHECK = 7,     /* an in-kernel input check failed */
+    TG_ERR_NO_DEVICE = 8         /* no CUDA device (the library has no CPU path) */
+} tg_status;
+
+/* Activations applied in kernel epilogues and by tg_activation_f32
+ * (src/ops.cpp:328 relu, 355 leaky_relu, 380 elu, 411 sigmoid, 441 tanh,
+ * 469 gelu). */
+typedef enum tg_activation {
+    TG_ACT_NONE = 0,
+    TG_ACT_RELU = 1,
+    TG_ACT_ELU = 2,
+    TG_ACT_LEAKY_RELU = 3,
+    TG_ACT_SIGMOID = 4,
+    TG_ACT_TANH = 5,
+    TG_ACT_GELU = 6
+} tg_activation;
+
+/* SAGE aggregators (include/tinygnn/layers.hpp SAGELayer::Aggregator). */
+typedef enum tg_aggregator { TG_AGG_MEAN = 0, TG_AGG_MAX = 1 } tg_aggregator;
+
+/* Execution modes.
+ *  TG_MODE_EXACT: the reference's arithmetic order (bit-identical results
+ *                 for spmm/matmul/GCN/SAGE-mean aggregate-first).
+ *  TG_MODE_FAST:  the byte- or flop-minimal dataflow, results within the
+ *                 fp32 tolerance |d| <= 1e-5 + 1e-4 |ref| (SAGE
+ *                 transform-first when F_in > F_out, split long rows). */
+typedef enum tg_mode { TG_MODE_EXACT = 0, TG_MODE_FAST = 1 } tg_mode;
+
+/* ── library ─────────────────────────────────────────────────────────────── */
+TG_API const char* tg_last_error_message(void); /* thread-local */
+TG_API const char* tg_version(void);
+TG_API int32_t tg_abi_version(void);
+/* Number of CUDA devices; 0 means every compute call returns TG_ERR_NO_DEVICE. */
+TG_API int32_t tg_device_count(void);
+/* How many kernels this library has launched in this process (all devices);
+ * used by benchmarks to count their own launches. */
+TG_API uint64_t tg_kernel_launch_count(void);
+
+/* ── dense ops (level 1) ─────────────────────────────────────────────────── */
+
+/* C[M,N] = A[M,K] . B[K,N]  (TinyGNN matmul, src/ops.cpp:70-162).
+ * EXACT: every C[i][j] is one fused multiply-add chain over k = 0..K-1,
+ * the reference's order -> bit-identical.  Optional epilogue: + bias[N]
+ * (add_bias, src/ops.cpp:622) then activation `act` with parameter alpha. */
+TG_API tg_status tg_gemm_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+                             const float* B, int64_t ldb, float* C, int64_t ldc,
+                             const float* bias, int32_t act, float alpha, int32_t mode,
+                             void* stream);
+
+/* C = A1 . B1 and A2 . B2 interleaved per k (the fused dual GEMV of
+ * SAGELayer::forward, src/layers.cpp:639-669): for k = 0..K-1,
+ * acc = fma(A1[i][k], B1[k][j], acc); acc = fma(A2[i][k], B2[k][j], acc).
+ * Columns j >= 8*floor(N/8) follow the reference's scalar tail
+ * acc = acc + fma(A1, B1, A2*B2).  Then + bias, activation. */
+TG_API tg_status tg_gemm_dual_f32(int64_t M, int64_t N, int64_t K, const float* A1,
+                                  int64_t lda1, const float* A2, int64_t lda2,
+                                  const float* B1, const float* B2, int64_t ldb, float* C,
+                                  int64_t ldc, const float* bias, int32_t act, float alpha,
+                                  void* stream);
+
+/* In-place activation on a rows x cols matrix (src/ops.cpp:328-482). */
+TG_API tg_status tg_activation_f32(int32_t act, float alpha, float* X, int64_t rows,
+                                   int64_t cols, int64_t ld, void* stream);
+/* Row-wise softmax / log_softmax in place (src/ops.cpp:506, 565);
+ * cols == 0 is rejected like the reference. */
+TG_API tg_status tg_softmax_rows_f32(float* X, int64_t rows, int64_t cols, int64_t ld,
+                                     void* stream);
+TG_API tg_status tg_log_softmax_rows_f32(float* X, int64_t rows, int64_t cols, int64_t ld,
+                                         void* stream);
+/* X[i][j] += bias[j]  (src/ops.cpp:622-661). */
+TG_API tg_status tg_add_bias_f32(float* X, int64_t rows, int64_t cols, int64_t ld,
+                                 const float* bias, void* stream);
+
+/* ── sparse ops ──────────────────────────────────────────────────────────── */
+
+/* C[M,F] = A . B for CSR A (M x K, int32 row_ptr[M+1] / col_ind[nnz], fp32
+ * values[nnz]) and dense B (K x F)  (TinyGNN spmm, src/ops.cpp:198-297).
+ * EXACT: one fused multiply-add chain per output element over the row's
+ * entries in stored order -> bit-identical.  row_order (nullable) lists the
+ * rows in the order to schedule them (e.g. tg_csr_degree_order); it changes
+ * speed only.  Optional fused epilogue + bias[F], activation. */
+TG_API tg_status tg_spmm_f32(int64_t M, int64_t K, int64_t nnz, const int32_t* row_ptr,
+                             const int32_t* col_ind, const float* values, const float* B,
+                             int64_t F, int64_t ldb, float* C, int64_t ldc, const float* bias,
+                             int32_t act, float alpha, const int32_t* row_order, int32_t mode,
+                             void* stream);
+
+/* Rows sorted by decreasing stored length (ties by row id) into
+ * order_out[M]: a schedule that starts the longest rows first. */
+TG_API tg_status tg_csr_degree_order(int64_t M, const int32_t* row_ptr, int32_t* order_out,
+                                     void* stream);
+
+/* Neighbour aggregation for SAGE (src/layers.cpp:588-637 mean, 674-700 max):
+ * out[i] = mean_j H[j] (plain adds in stored order, then * (1/deg)), or the
+ * element-wise max (-inf start, empty rows 0).  CSR values are ignored. */
+TG_API tg_status tg_sage_aggregate_f32(int64_t M, int64_t K, int64_t nnz,
+                                       const int32_t* row_ptr, const int32_t* col_ind,
+                                       const float* H, int64_t F, int64_t ldh, float* out,
+                                       int64_t ldo, int32_t aggregator, void* stream);
+
+/* sage_max_aggregate (src/layers.cpp:359-435), exact. */
+TG_API tg_status tg_sage_max_aggregate_f32(int64_t M, int64_t K, int64_t nnz,
+                                           const int32_t* row_ptr, const int32_t* col_ind,
+                                           const float* H, int64_t F, int64_t ldh, float* out,
+                                           int64_t ldo, void* stream);
+
+/* edge_softmax (src/layers.cpp:768-822): per-row softmax of CSR values into
+ * values_out[nnz]; empty rows produce nothing. */
+TG_API tg_status tg_edge_softmax_f32(int64_t M, int64_t nnz, const int32_t* row_ptr,
+                                     const float* values, float* values_out, void* stream);
+
+/* ── graph construction (bit-exact) ──────────────────────────────────────── */
+
+/* GraphLoader::edge_list_to_csr (src/graph_loader.cpp:211-281): COO edges
+ * (src[E], dst[E]) -> CSR with rows = src, each row's columns sorted
+ * ascending, values 1.0, no de-duplication.  Endpoints outside
+ * [0, num_nodes) are rejected with the reference's message.  Outputs:
+ * row_ptr[num_nodes+1], col_ind[E], values[E].  Synchronises `stream`. */
+TG_API tg_status tg_edge_list_to_csr(int64_t num_nodes, int64_t E, const int32_t* src,
+                                     const int32_t* dst, int32_t* row_ptr_out,
+                                     int32_t* col_ind_out, float* values_out, void* stream);
+
+/* add_self_loops (src/layers.cpp:71-144): capacity of col_ind_out/values_out
+ * must be >= nnz + N; *nnz_out receives the result's nnz (host pointer).
+ * Synchronises `stream`. */
+TG_API tg_status tg_add_self_loops_f32(int64_t N, int64_t nnz, const int32_t* row_ptr,
+                                       const int32_t* col_ind, const float* values,
+                                       int32_t* row_ptr_out, int32_t* col_ind_out,
+                                       float* values_out, int64_t* nnz_out, void* stream);
+
+/* gcn_norm (src/layers.cpp:158-208): D^-1/2 (A + I) D^-1/2 with the
+ * reference's float degree sum, 1/sqrtf and (v*dis_i)*dis_j rounding.
+ * Same output contract as tg_add_self_loops_f32. */
+TG_API tg_status tg_gcn_norm_f32(int64_t N, int64_t nnz, const int32_t* row_ptr,
+                                 const int32_t* col_ind, const float* values,
+                                 int32_t* row_ptr_out, int32_t* col_ind_out, float* values_out,
+                                 int64_t* nnz_out, void* stream);
+
+/* Tensor::sparse_csr validation (src/tensor.cpp:46-86) on device arrays:
+ * row_ptr[rows] == nnz, row_ptr non-decreasing, 0 <= col_ind < cols.
+ * Synchronises `stream`; errors carry the reference's message. */
+TG_API tg_status tg_csr_validate(int64_t rows, int64_t cols, int64_t nnz,
+                                 const int32_t* row_ptr, const int32_t* col_ind, void* stream);
+
+/* ── layers ──────────────────────────────────────────────────────────────── */
+
+/* GCNLayer::forward (src/layers.cpp:286-339): out = act(A_norm . (H . W) + b)
+ * with A_norm an N x N CSR (e.g. from tg_gcn_norm_f32).  W is F_in x F_out,
+ * bias nullable.  EXACT -> bit-identical.  Allocates an N x F_out scratch. */
+TG_API tg_status tg_gcn_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr,
+                                  const int32_t* col_ind, const float* values, const float* H,
+                                  int64_t ldh, int64_t F_in, int64_t F_out, const float* W,
+                                  const float* bias, int32_t act, float* out, int64_t ldo,
+                                  const int32_t* row_order, int32_t mode, void* stream);
+
+/* SAGELayer::forward (src/layers.cpp:538-752) on the raw adjacency (no
+ * self-loops): out = act(AGG_j H[j] . Wn + H[i] . Ws + b).  EXACT computes
+ * the aggregate first and the interleaved dual product (bit-identical for
+ * mean); FAST transforms first when F_in > F_out (mean only). */
+TG_API tg_status tg_sage_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr,
+                                   const int32_t* col_ind, const float* H, int64_t ldh,
+                                   int64_t F_in, int64_t F_out, const float* W_neigh,
+                                   const float* W_self, const float* bias, int32_t aggregator,
+                                   int32_t act, float* out, int64_t ldo,
+                                   const int32_t* row_order, int32_t mode, void* stream);
+
+/* Multi-head GATLayer::forward (src/layers.cpp:945-1129) plus the head
+ * concat/average of Model::forward (src/model.cpp:403-422), in one pass over
+ * the graph.  A is the self-looped adjacency.  W is F_in x (heads*F_out):
+ * head h's weight occupies columns [h*F_out, (h+1)*F_out).  a_left, a_right,
+ * bias are heads x F_out (bias nullable).  Per head: e_ij = LeakyReLU(
+ * a_left.Wh_i + a_right.Wh_j), softmax over the row, out_i = sum a_ij Wh_j
+ * + b, activation `act`; then heads are concatenated (out is N x heads*F_out)
+ * or averaged (N x F_out).  The E x heads score tensor is never stored. */
+TG_API tg_status tg_gat_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr,
+                                  const int32_t* col_ind, const float* H, int64_t ldh,
+                                  int64_t F_in, int64_t heads, int64_t F_out, const float* W,
+                                  const float* a_left, const float* a_right, const float* bias,
+                                  float negative_slope, int32_t concat, int32_t act,
+                                  float* out, int64_t ldo, const int32_t* row_order,
+                                  void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* TINYGNN_B200_H */

@@ -387,6 +387,54 @@ class RefModel:
             pass
 
 
+def model_forward(impl, spec, weights, rp, ci, v, X):
+    """Model::forward (src/model.cpp:359-439) composed from ``impl``'s layers.
+
+    gcn_norm(A) for GCN layers and add_self_loops(A) for GAT layers are built
+    once per call (365-381); layers run in order; a multi-head GAT layer runs
+    each head and concatenates (312-332) or averages (335-354) them; then the
+    post activation (426-435).  ``spec``/``weights`` as in :class:`RefModel`.
+    """
+    need_gcn = any(L["type"] == "gcn" for L in spec)
+    need_sl = any(L["type"] == "gat" for L in spec)
+    A_gcn = impl.gcn_norm(rp, ci, v) if need_gcn else None
+    A_sl = impl.add_self_loops(rp, ci, v) if need_sl else None
+    H = _f(X)
+    for li, L in enumerate(spec):
+        pre = f"layer{li}"
+        relu = L.get("act") == "relu"
+        bias = L.get("bias", True)
+        if L["type"] == "gcn":
+            H = impl.gcn_layer(*A_gcn, H, weights[f"{pre}.weight"],
+                               weights[f"{pre}.bias"] if bias else None, relu)
+        elif L["type"] == "sage":
+            H = impl.sage_layer(rp, ci, v, H, weights[f"{pre}.weight_neigh"], weights[f"{pre}.weight_self"],
+                                weights[f"{pre}.bias"] if bias else None, L.get("agg", "mean"), relu)
+        else:
+            heads = []
+            for h in range(L.get("heads", 1)):
+                hp = f"{pre}.head{h}"
+                heads.append(impl.gat_layer(*A_sl, H, weights[f"{hp}.weight"], weights[f"{hp}.attn_left"],
+                                            weights[f"{hp}.attn_right"],
+                                            weights[f"{hp}.bias"] if bias else None,
+                                            L.get("slope", 0.2), relu))
+            if len(heads) == 1:
+                H = heads[0]
+            elif L.get("concat", True):
+                H = np.ascontiguousarray(np.concatenate(heads, axis=1))
+            else:
+                acc = np.zeros_like(heads[0])
+                for t in heads:
+                    acc = (acc + t).astype(np.float32)
+                H = (acc * np.float32(1.0 / len(heads))).astype(np.float32)
+        post = L.get("post")
+        if post == "relu":
+            H = impl.activation("relu", H)
+        elif post == "elu":
+            H = impl.activation("elu", H, 1.0)
+    return H
+
+
 def _load(cls, path):
     return cls(path) if os.path.exists(path) else None
 

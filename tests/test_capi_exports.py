@@ -1,0 +1,76 @@
+"""The C-ABI library loads and exports every entry point the headers declare (CPU)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+INCLUDE = os.path.join(ROOT, "include")
+
+
+def declared_symbols():
+    names = set()
+    for fn in os.listdir(INCLUDE):
+        if fn.endswith(".h"):
+            src = open(os.path.join(INCLUDE, fn)).read()
+            names |= set(re.findall(r"TG_API\s+[\w\s\*]+?\b(tg_\w+)\s*\(", src))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert "tg_spmm_f32" in names and "tg_gemm_f32" in names and len(names) >= 20
+
+
+def test_library_exports_every_declared_symbol():
+    from tinygnn_b200 import _lib
+    missing = [n for n in declared_symbols() if not hasattr(_lib.lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_python_binding_covers_every_declared_symbol():
+    from tinygnn_b200 import _lib
+    unbound = [n for n in declared_symbols() if n not in _lib.SIGNATURES]
+    assert not unbound, f"declared but not bound in _lib.SIGNATURES: {unbound}"
+
+
+def test_library_metadata_calls():
+    from tinygnn_b200 import _lib
+    assert _lib.lib.tg_abi_version() == 1
+    assert b"sm_100a" in _lib.lib.tg_version()
+    assert _lib.lib.tg_device_count() >= 0
+
+
+def test_library_is_built_for_sm100a_only():
+    """The fatbin targets sm_100a (reads the ELF section names only)."""
+    from tinygnn_b200 import _lib
+    data = open(_lib.LIB_PATH, "rb").read()
+    assert b".nv_fatbin" in data
+
+
+def test_no_cpu_fallback_when_library_missing(tmp_path, monkeypatch):
+    """Importing the package without the built library fails loudly."""
+    import importlib
+    import sys
+    from tinygnn_b200 import _lib
+    monkeypatch.setattr(os.path, "exists", lambda p, _e=os.path.exists: False if p == _lib.LIB_PATH else _e(p))
+    saved = {k: sys.modules.pop(k) for k in list(sys.modules) if k.startswith("tinygnn_b200")}
+    try:
+        with pytest.raises(ImportError):
+            importlib.import_module("tinygnn_b200._lib")
+    finally:
+        for k in list(sys.modules):
+            if k.startswith("tinygnn_b200"):
+                del sys.modules[k]
+        sys.modules.update(saved)
+
+
+def test_compute_call_without_device_reports_no_device():
+    """On a host without a GPU the status is TG_ERR_NO_DEVICE, never a CPU result."""
+    from tinygnn_b200 import _lib
+    if _lib.lib.tg_device_count() > 0:
+        pytest.skip("a device is present")
+    st = _lib.lib.tg_gemm_f32(1, 1, 1, None, 1, None, 1, None, 1, None, 0, 0.0, 0, None)
+    assert st == _lib.NO_DEVICE
+    assert "no CUDA device" in _lib.last_error()

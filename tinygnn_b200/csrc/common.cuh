@@ -1,0 +1,122 @@
+// ============================================================================
+//  tinygnn_b200/csrc/common.cuh -- shared helpers for the sm_100a kernels and
+//  the C-ABI layer: error capture, activation functors, launch geometry.
+// ============================================================================
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#include "tinygnn_b200.h"
+
+namespace tg {
+
+// ── Errors ──────────────────────────────────────────────────────────────────
+// Internal code throws tg::Error; every extern "C" entry point converts it to
+// a tg_status and stores the message for tg_last_error_message().
+struct Error : std::runtime_error {
+    tg_status status;
+    Error(tg_status s, const std::string& m) : std::runtime_error(m), status(s) {}
+};
+
+[[noreturn]] inline void fail(tg_status s, const std::string& m) { throw Error(s, m); }
+[[noreturn]] inline void invalid(const std::string& m) { fail(TG_ERR_INVALID_ARGUMENT, m); }
+
+void set_last_error(const std::string& m);
+
+inline void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess)
+        fail(TG_ERR_CUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                              cudaGetErrorString(e) + ")");
+}
+#define TG_CUDA(call) ::tg::cuda_check((call), #call)
+#define TG_LAUNCH_CHECK(name) ::tg::cuda_check(cudaGetLastError(), name)
+
+// Runs f and maps any exception to a status (the C-ABI boundary).
+template <class F>
+tg_status guard(F&& f) noexcept {
+    try {
+        f();
+        return TG_OK;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return e.status;
+    } catch (const std::invalid_argument& e) {
+        set_last_error(e.what());
+        return TG_ERR_INVALID_ARGUMENT;
+    } catch (const std::out_of_range& e) {
+        set_last_error(e.what());
+        return TG_ERR_OUT_OF_RANGE;
+    } catch (const std::bad_alloc&) {
+        set_last_error("out of host memory");
+        return TG_ERR_RUNTIME;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return TG_ERR_RUNTIME;
+    } catch (...) {
+        set_last_error("unknown error");
+        return TG_ERR_RUNTIME;
+    }
+}
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Number of SMs of the current device (cached per device).
+int num_sms();
+
+// ── Stream-ordered scratch ────────────────────────────────────────────────
+// Scratch buffers come from the device's default memory pool with a high
+// release threshold, so repeated calls reuse the same pages.
+void* scratch_alloc(size_t bytes, cudaStream_t s);
+void scratch_free(void* p, cudaStream_t s);
+
+template <class T>
+struct Scratch {
+    T* p = nullptr;
+    cudaStream_t s = nullptr;
+    Scratch(size_t n, cudaStream_t st) : s(st) {
+        p = static_cast<T*>(scratch_alloc((n ? n : 1) * sizeof(T), st));
+    }
+    ~Scratch() {
+        if (p) scratch_free(p, s);
+    }
+    Scratch(const Scratch&) = delete;
+    Scratch& operator=(const Scratch&) = delete;
+};
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// ── Activations (reference src/ops.cpp:328-482) ──────────────────────────
+// Device versions of the in-place activations; relu/leaky/elu/sigmoid keep the
+// reference's branch structure so their results match it exactly apart from
+// the last bits of exp/tanh.
+__device__ __forceinline__ float apply_act(int act, float x, float alpha) {
+    switch (act) {
+        case TG_ACT_RELU:
+            return x > 0.0f ? x : 0.0f;  // std::max(0.0f, x)
+        case TG_ACT_LEAKY_RELU:
+            return x >= 0.0f ? x : __fmul_rn(alpha, x);
+        case TG_ACT_ELU:
+            return x < 0.0f ? __fmul_rn(alpha, __fsub_rn(expf(x), 1.0f)) : x;
+        case TG_ACT_SIGMOID:
+            if (x >= 0.0f) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+            else {
+                const float ex = expf(x);
+                return __fdiv_rn(ex, __fadd_rn(1.0f, ex));
+            }
+        case TG_ACT_TANH:
+            return tanhf(x);
+        case TG_ACT_GELU: {
+            const float inner = __fmul_rn(0.7978845608f, fmaf(__fmul_rn(__fmul_rn(0.044715f, x), x), x, x));
+            return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+        }
+        default:
+            return x;
+    }
+}
+
+}  // namespace tg

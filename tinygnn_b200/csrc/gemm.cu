@@ -1,0 +1,235 @@
+// ============================================================================
+//  gemm.cu -- dense products on the hot path.
+//
+//  gemm_exact: C = A . B with every C[i][j] one fused multiply-add chain over
+//  k = 0..K-1 in order -- the arithmetic of TinyGNN's matmul (i, k, j loop
+//  with AVX2 FMA, src/ops.cpp:120-159) -- so results are bit-identical.
+//  Register-tiled SIMT kernel: a CTA of 256 threads owns a BM x BN output
+//  tile, stages BK-deep slabs of A (transposed) and B in shared memory,
+//  double-buffered through registers, and each thread keeps a TM x TN
+//  accumulator block.  The shapes on the path are tall-skinny
+//  (N = 7..256), so BN is picked from N and A is read once.
+//
+//  The DUAL form interleaves two products per k (SAGE's fused dual GEMV,
+//  src/layers.cpp:639-669).
+// ============================================================================
+#include "launch.cuh"
+
+namespace tg {
+
+namespace {
+
+struct GemmArgs {
+    int64_t M, N, K;
+    const float* A1; int64_t lda1;
+    const float* A2; int64_t lda2;   // DUAL only
+    const float* B1; const float* B2; int64_t ldb;
+    float* C; int64_t ldc;
+    const float* bias;
+    int act; float alpha;
+    int64_t n_fma_cols;  // DUAL: columns < this use the 8-wide body order
+};
+
+template <int BM, int BN, int BK, int TM, int TN, bool DUAL>
+__global__ void __launch_bounds__(256) gemm_exact_kernel(const GemmArgs g) {
+    static_assert((BM / TM) * (BN / TN) == 256, "256 threads");
+    constexpr int NA = (BM * BK + 255) / 256;  // A elements per thread per slab
+    constexpr int NB = (BK * BN + 255) / 256;  // B elements per thread per slab
+    constexpr int NOPS = DUAL ? 2 : 1;
+
+    __shared__ __align__(16) float As[NOPS][BK][BM];
+    __shared__ __align__(16) float Bs[NOPS][BK][BN];
+
+    const int tid = threadIdx.x;
+    const int tx = tid % (BN / TN);
+    const int ty = tid / (BN / TN);
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
+
+    // Loader mapping: A slab is BM rows x BK k (k fastest), B slab BK x BN.
+    float ra[NOPS][NA], rb[NOPS][NB];
+    auto load_slab = [&](int64_t k0) {
+#pragma unroll
+        for (int o = 0; o < NOPS; ++o) {
+            const float* A = o ? g.A2 : g.A1;
+            const int64_t lda = o ? g.lda2 : g.lda1;
+            const float* B = o ? g.B2 : g.B1;
+#pragma unroll
+            for (int q = 0; q < NA; ++q) {
+                const int e = tid + q * 256;
+                const int r = e / BK, c = e % BK;
+                const int64_t gm = m0 + r, gk = k0 + c;
+                ra[o][q] = (e < BM * BK && gm < g.M && gk < g.K) ? __ldg(A + gm * lda + gk) : 0.0f;
+            }
+#pragma unroll
+            for (int q = 0; q < NB; ++q) {
+                const int e = tid + q * 256;
+                const int r = e / BN, c = e % BN;
+                const int64_t gk = k0 + r, gn = n0 + c;
+                rb[o][q] = (e < BK * BN && gk < g.K && gn < g.N) ? __ldg(B + gk * g.ldb + gn) : 0.0f;
+            }
+        }
+    };
+    auto store_slab = [&]() {
+#pragma unroll
+        for (int o = 0; o < NOPS; ++o) {
+#pragma unroll
+            for (int q = 0; q < NA; ++q) {
+                const int e = tid + q * 256;
+                if (e < BM * BK) As[o][e % BK][e / BK] = ra[o][q];
+            }
+#pragma unroll
+            for (int q = 0; q < NB; ++q) {
+                const int e = tid + q * 256;
+                if (e < BK * BN) Bs[o][e / BN][e % BN] = rb[o][q];
+            }
+        }
+    };
+
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
+
+    bool body[TN];  // DUAL: column inside the reference's 8-wide body
+#pragma unroll
+    for (int j = 0; j < TN; ++j) body[j] = (n0 + tx * TN + j) < g.n_fma_cols;
+
+    load_slab(0);
+    for (int64_t k0 = 0; k0 < g.K; k0 += BK) {
+        __syncthreads();
+        store_slab();
+        __syncthreads();
+        if (k0 + BK < g.K) load_slab(k0 + BK);  // next slab in flight during compute
+        const int kn = (g.K - k0 < BK) ? static_cast<int>(g.K - k0) : BK;
+        for (int kk = 0; kk < kn; ++kk) {
+            float a[NOPS][TM], b[NOPS][TN];
+#pragma unroll
+            for (int o = 0; o < NOPS; ++o) {
+#pragma unroll
+                for (int i = 0; i < TM; i += 4) {
+                    const float4 t = *reinterpret_cast<const float4*>(&As[o][kk][ty * TM + i]);
+                    a[o][i] = t.x; a[o][i + 1] = t.y; a[o][i + 2] = t.z; a[o][i + 3] = t.w;
+                }
+                if constexpr (TN % 4 == 0) {
+#pragma unroll
+                    for (int j = 0; j < TN; j += 4) {
+                        const float4 t = *reinterpret_cast<const float4*>(&Bs[o][kk][tx * TN + j]);
+                        b[o][j] = t.x; b[o][j + 1] = t.y; b[o][j + 2] = t.z; b[o][j + 3] = t.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < TN; ++j) b[o][j] = Bs[o][kk][tx * TN + j];
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) {
+                    if constexpr (DUAL) {
+                        acc[i][j] = body[j]
+                                        ? fmaf(a[1][i], b[1][j], fmaf(a[0][i], b[0][j], acc[i][j]))
+                                        : __fadd_rn(acc[i][j], fmaf(a[0][i], b[0][j], __fmul_rn(a[1][i], b[1][j])));
+                    } else {
+                        acc[i][j] = fmaf(a[0][i], b[0][j], acc[i][j]);
+                    }
+                }
+        }
+    }
+
+    // Epilogue: + bias (one rounding), activation, masked store.
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const int64_t m = m0 + ty * TM + i;
+        if (m >= g.M) break;
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+            const int64_t n = n0 + tx * TN + j;
+            if (n < g.N) {
+                float v = acc[i][j];
+                if (g.bias) v = __fadd_rn(v, __ldg(g.bias + n));
+                g.C[m * g.ldc + n] = apply_act(g.act, v, g.alpha);
+            }
+        }
+    }
+}
+
+template <int BM, int BN, int BK, int TM, int TN, bool DUAL>
+void launch_gemm(const GemmArgs& g, cudaStream_t s) {
+    dim3 grid(static_cast<unsigned>(ceil_div(g.N, BN)), static_cast<unsigned>(ceil_div(g.M, BM)));
+    launch("gemm_exact", gemm_exact_kernel<BM, BN, BK, TM, TN, DUAL>, grid, dim3(256), 0, s, g);
+}
+
+template <bool DUAL>
+void dispatch_gemm(const GemmArgs& g, cudaStream_t s) {
+    if (g.N <= 8) launch_gemm<256, 8, 8, 8, 1, DUAL>(g, s);
+    else if (g.N <= 16) launch_gemm<256, 16, 8, 4, 4, DUAL>(g, s);
+    else if (g.N <= 32) launch_gemm<128, 32, 8, 4, 4, DUAL>(g, s);
+    else if (g.N <= 64) launch_gemm<128, 64, 8, 8, 4, DUAL>(g, s);
+    else launch_gemm<128, 128, 8, 8, 8, DUAL>(g, s);
+}
+
+}  // namespace
+
+void gemm_exact(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B,
+                int64_t ldb, float* C, int64_t ldc, const float* bias, int act, float alpha,
+                cudaStream_t s) {
+    if (M == 0 || N == 0) return;
+    // K == 0 runs no k step: C = act(0 + bias), like the zero-initialised
+    // reference output.
+    GemmArgs g{M, N, K, A, lda, nullptr, 0, B, nullptr, ldb, C, ldc, bias, act, alpha, 0};
+    dispatch_gemm<false>(g, s);
+}
+
+void gemm_dual_exact(int64_t M, int64_t N, int64_t K, const float* A1, int64_t lda1,
+                     const float* A2, int64_t lda2, const float* B1, const float* B2, int64_t ldb,
+                     float* C, int64_t ldc, const float* bias, int act, float alpha,
+                     cudaStream_t s) {
+    if (M == 0 || N == 0) return;
+    GemmArgs g{M, N, K, A1, lda1, A2, lda2, B1, B2, ldb, C, ldc, bias, act, alpha, (N / 8) * 8};
+    dispatch_gemm<true>(g, s);
+}
+
+}  // namespace tg
+
+using namespace tg;
+
+extern "C" {
+
+TG_API tg_status tg_gemm_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+                             const float* B, int64_t ldb, float* C, int64_t ldc,
+                             const float* bias, int32_t act, float alpha, int32_t mode,
+                             void* stream) {
+    return guard([&] {
+        require_device();
+        if (M < 0 || N < 0 || K < 0) invalid("matmul: negative size");
+        check_ld("matmul", "A", lda, K);
+        check_ld("matmul", "B", ldb, N);
+        check_ld("matmul", "C", ldc, N);
+        check_ptr("matmul", "A", A, M > 0 && K > 0);
+        check_ptr("matmul", "B", B, K > 0 && N > 0);
+        check_ptr("matmul", "C", C, M > 0 && N > 0);
+        (void)mode;
+        gemm_exact(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_gemm_dual_f32(int64_t M, int64_t N, int64_t K, const float* A1,
+                                  int64_t lda1, const float* A2, int64_t lda2,
+                                  const float* B1, const float* B2, int64_t ldb, float* C,
+                                  int64_t ldc, const float* bias, int32_t act, float alpha,
+                                  void* stream) {
+    return guard([&] {
+        require_device();
+        if (M < 0 || N < 0 || K < 0) invalid("gemm_dual: negative size");
+        check_ld("gemm_dual", "A1", lda1, K);
+        check_ld("gemm_dual", "A2", lda2, K);
+        check_ld("gemm_dual", "B", ldb, N);
+        check_ld("gemm_dual", "C", ldc, N);
+        gemm_dual_exact(M, N, K, A1, lda1, A2, lda2, B1, B2, ldb, C, ldc, bias, act, alpha,
+                        as_stream(stream));
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,319 @@
+"""Torch-tensor front end of the C ABI (device-pointer level).
+
+Every function here calls one ``tg_*`` entry point of
+libtinygnn_b200.so on torch's current CUDA stream; torch only provides the
+device memory.  Dense operands are 2-D float32 CUDA tensors with unit column
+stride (any row stride); CSR operands are :class:`CSR`.
+
+Names and semantics follow TinyGNN's operator API (include/tinygnn/ops.hpp,
+include/tinygnn/layers.hpp, include/tinygnn/graph_loader.hpp).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+ACT = {None: _lib.ACT_NONE, "none": _lib.ACT_NONE, "relu": _lib.ACT_RELU, "elu": _lib.ACT_ELU,
+       "leaky_relu": _lib.ACT_LEAKY_RELU, "sigmoid": _lib.ACT_SIGMOID, "tanh": _lib.ACT_TANH,
+       "gelu": _lib.ACT_GELU}
+MODE = {"exact": _lib.MODE_EXACT, "fast": _lib.MODE_FAST}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _dense(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dim() != 2 or t.dtype != torch.float32 or not t.is_cuda:
+        raise ValueError(f"{name} must be a 2-D float32 CUDA tensor")
+    if t.stride(1) != 1 and t.numel() > 0:
+        t = t.contiguous()
+    return t
+
+
+def _ld(t: torch.Tensor) -> int:
+    return max(t.stride(0), t.shape[1]) if t.dim() == 2 else 1
+
+
+def _vec(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    if t is None:
+        return None
+    return t.reshape(-1).to(torch.float32).contiguous()
+
+
+@dataclass
+class CSR:
+    """Device CSR matrix: int32 row_ptr[n_rows+1], col_ind[nnz], float32 values[nnz]."""
+
+    n_rows: int
+    n_cols: int
+    row_ptr: torch.Tensor
+    col_ind: torch.Tensor
+    values: torch.Tensor
+
+    @property
+    def nnz(self) -> int:
+        return int(self.col_ind.numel())
+
+    @classmethod
+    def from_numpy(cls, row_ptr, col_ind, values=None, n_cols=None, device="cuda") -> "CSR":
+        rp = torch.as_tensor(np.ascontiguousarray(row_ptr, dtype=np.int32), device=device)
+        ci = torch.as_tensor(np.ascontiguousarray(col_ind, dtype=np.int32), device=device)
+        if values is None:
+            v = torch.ones(ci.numel(), dtype=torch.float32, device=device)
+        else:
+            v = torch.as_tensor(np.ascontiguousarray(values, dtype=np.float32), device=device)
+        n = rp.numel() - 1
+        return cls(n, n if n_cols is None else int(n_cols), rp, ci, v)
+
+    def numpy(self):
+        return (self.row_ptr.cpu().numpy(), self.col_ind.cpu().numpy(), self.values.cpu().numpy())
+
+
+# ── dense ops ────────────────────────────────────────────────────────────────
+def matmul(A: torch.Tensor, B: torch.Tensor, bias=None, act=None, alpha: float = 0.0,
+           out: Optional[torch.Tensor] = None, mode: str = "exact") -> torch.Tensor:
+    """C = act(A . B + bias)  (TinyGNN matmul, src/ops.cpp:70)."""
+    A, B = _dense(A, "A"), _dense(B, "B")
+    if A.shape[1] != B.shape[0]:
+        raise _lib.InvalidArgument(
+            _lib.INVALID_ARGUMENT,
+            f"matmul: dimension mismatch — A is ({A.shape[0]}×{A.shape[1]}) but B is "
+            f"({B.shape[0]}×{B.shape[1]}). Required: A.cols() == B.rows() (both = {A.shape[1]} vs {B.shape[0]}).")
+    M, K = A.shape
+    N = B.shape[1]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    b = _vec(bias)
+    check(lib.tg_gemm_f32(M, N, K, _p(A), _ld(A), _p(B), _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha,
+                          MODE[mode], _stream()))
+    return out
+
+
+def gemm_dual(A1, A2, B1, B2, bias=None, act=None, out=None) -> torch.Tensor:
+    """C = interleaved A1.B1 + A2.B2 (SAGE's fused dual GEMV order)."""
+    A1, A2, B1, B2 = _dense(A1, "A1"), _dense(A2, "A2"), _dense(B1, "B1"), _dense(B2, "B2")
+    M, K = A1.shape
+    N = B1.shape[1]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=A1.device)
+    b = _vec(bias)
+    check(lib.tg_gemm_dual_f32(M, N, K, _p(A1), _ld(A1), _p(A2), _ld(A2), _p(B1), _p(B2), _ld(B1), _p(out),
+                               _ld(out), _p(b), ACT[act], 0.0, _stream()))
+    return out
+
+
+def activation_(X: torch.Tensor, kind: str, alpha: float = 0.0) -> torch.Tensor:
+    """In-place activation (src/ops.cpp:328-482)."""
+    X = _dense(X, "X")
+    check(lib.tg_activation_f32(ACT[kind], alpha, _p(X), X.shape[0], X.shape[1], _ld(X), _stream()))
+    return X
+
+
+def relu_(X):
+    return activation_(X, "relu")
+
+
+def leaky_relu_(X, alpha: float = 0.01):
+    return activation_(X, "leaky_relu", alpha)
+
+
+def elu_(X, alpha: float = 1.0):
+    return activation_(X, "elu", alpha)
+
+
+def sigmoid_(X):
+    return activation_(X, "sigmoid")
+
+
+def tanh_(X):
+    return activation_(X, "tanh")
+
+
+def gelu_(X):
+    return activation_(X, "gelu")
+
+
+def softmax_(X: torch.Tensor) -> torch.Tensor:
+    X = _dense(X, "X")
+    check(lib.tg_softmax_rows_f32(_p(X), X.shape[0], X.shape[1], _ld(X), _stream()))
+    return X
+
+
+def log_softmax_(X: torch.Tensor) -> torch.Tensor:
+    X = _dense(X, "X")
+    check(lib.tg_log_softmax_rows_f32(_p(X), X.shape[0], X.shape[1], _ld(X), _stream()))
+    return X
+
+
+def add_bias_(X: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    X = _dense(X, "X")
+    b = _vec(bias)
+    if b.numel() != X.shape[1]:
+        raise _lib.InvalidArgument(
+            _lib.INVALID_ARGUMENT,
+            f"add_bias: bias must be shape (1×{X.shape[1]}) to match X columns, but got (1×{b.numel()}).")
+    check(lib.tg_add_bias_f32(_p(X), X.shape[0], X.shape[1], _ld(X), _p(b), _stream()))
+    return X
+
+
+# ── sparse ops ───────────────────────────────────────────────────────────────
+def spmm(A: CSR, B: torch.Tensor, bias=None, act=None, alpha: float = 0.0, row_order=None,
+         out: Optional[torch.Tensor] = None, mode: str = "exact") -> torch.Tensor:
+    """C = act(A . B + bias)  (TinyGNN spmm, src/ops.cpp:198)."""
+    B = _dense(B, "B")
+    if A.n_cols != B.shape[0]:
+        raise _lib.InvalidArgument(
+            _lib.INVALID_ARGUMENT,
+            f"spmm: dimension mismatch — A is ({A.n_rows}×{A.n_cols}, SparseCSR) but B is "
+            f"({B.shape[0]}×{B.shape[1]}, Dense). Required: A.cols() == B.rows() ({A.n_cols} vs {B.shape[0]}).")
+    F = B.shape[1]
+    if out is None:
+        out = torch.empty((A.n_rows, F), dtype=torch.float32, device=B.device)
+    b = _vec(bias)
+    check(lib.tg_spmm_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(B), F,
+                          _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha, _p(row_order), MODE[mode],
+                          _stream()))
+    return out
+
+
+def degree_order(A: CSR) -> torch.Tensor:
+    """Rows by decreasing stored length (a schedule for the gather kernels)."""
+    out = torch.empty(A.n_rows, dtype=torch.int32, device=A.row_ptr.device)
+    check(lib.tg_csr_degree_order(A.n_rows, _p(A.row_ptr), _p(out), _stream()))
+    return out
+
+
+def sage_aggregate(A: CSR, H: torch.Tensor, aggregator: str = "mean") -> torch.Tensor:
+    H = _dense(H, "H")
+    out = torch.empty((A.n_rows, H.shape[1]), dtype=torch.float32, device=H.device)
+    check(lib.tg_sage_aggregate_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(H), H.shape[1],
+                                    _ld(H), _p(out), _ld(out), _lib.AGG_MAX if aggregator == "max" else
+                                    _lib.AGG_MEAN, _stream()))
+    return out
+
+
+def sage_max_aggregate(A: CSR, H: torch.Tensor) -> torch.Tensor:
+    """sage_max_aggregate (src/layers.cpp:359)."""
+    H = _dense(H, "H")
+    if A.n_cols != H.shape[0]:
+        raise _lib.InvalidArgument(_lib.INVALID_ARGUMENT,
+                                   f"sage_max_aggregate: A.cols() ({A.n_cols}) != H.rows() ({H.shape[0]}).")
+    out = torch.empty((A.n_rows, H.shape[1]), dtype=torch.float32, device=H.device)
+    check(lib.tg_sage_max_aggregate_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(H),
+                                        H.shape[1], _ld(H), _p(out), _ld(out), _stream()))
+    return out
+
+
+def edge_softmax(A: CSR) -> CSR:
+    """edge_softmax (src/layers.cpp:768): same structure, row-softmaxed values."""
+    v = torch.zeros_like(A.values)
+    check(lib.tg_edge_softmax_f32(A.n_rows, A.nnz, _p(A.row_ptr), _p(A.values), _p(v), _stream()))
+    return CSR(A.n_rows, A.n_cols, A.row_ptr.clone(), A.col_ind.clone(), v)
+
+
+# ── graph construction ───────────────────────────────────────────────────────
+def edge_list_to_csr(src: torch.Tensor, dst: torch.Tensor, num_nodes: int) -> CSR:
+    """GraphLoader::edge_list_to_csr (src/graph_loader.cpp:211)."""
+    src = src.to(torch.int32).contiguous()
+    dst = dst.to(torch.int32).contiguous()
+    E = src.numel()
+    dev = src.device
+    rp = torch.empty(num_nodes + 1, dtype=torch.int32, device=dev)
+    ci = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
+    v = torch.empty(max(E, 1), dtype=torch.float32, device=dev)
+    check(lib.tg_edge_list_to_csr(num_nodes, E, _p(src), _p(dst), _p(rp), _p(ci), _p(v), _stream()))
+    return CSR(num_nodes, num_nodes, rp, ci[:E], v[:E])
+
+
+def _csr_expand(fn, A: CSR) -> CSR:
+    N = A.n_rows
+    if A.n_rows != A.n_cols:
+        name = "gcn_norm" if fn is lib.tg_gcn_norm_f32 else "add_self_loops"
+        raise _lib.InvalidArgument(_lib.INVALID_ARGUMENT,
+                                   f"{name}: A must be square — got ({A.n_rows}×{A.n_cols}).")
+    cap = A.nnz + N
+    dev = A.row_ptr.device
+    rp = torch.empty(N + 1, dtype=torch.int32, device=dev)
+    ci = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+    v = torch.empty(max(cap, 1), dtype=torch.float32, device=dev)
+    nnz = C.c_int64(0)
+    check(fn(N, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(rp), _p(ci), _p(v), C.byref(nnz),
+             _stream()))
+    return CSR(N, N, rp, ci[:nnz.value], v[:nnz.value])
+
+
+def add_self_loops(A: CSR) -> CSR:
+    """add_self_loops (src/layers.cpp:71)."""
+    return _csr_expand(lib.tg_add_self_loops_f32, A)
+
+
+def gcn_norm(A: CSR) -> CSR:
+    """gcn_norm (src/layers.cpp:158): D^-1/2 (A + I) D^-1/2."""
+    return _csr_expand(lib.tg_gcn_norm_f32, A)
+
+
+def csr_validate(A: CSR) -> None:
+    """Tensor::sparse_csr's checks (src/tensor.cpp:46-86) on device arrays."""
+    check(lib.tg_csr_validate(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _stream()))
+
+
+# ── layers ───────────────────────────────────────────────────────────────────
+def gcn_layer(A_norm: CSR, H: torch.Tensor, W: torch.Tensor, bias=None, act="relu", row_order=None,
+              out=None, mode: str = "exact") -> torch.Tensor:
+    """GCNLayer::forward (src/layers.cpp:286)."""
+    H, W = _dense(H, "H"), _dense(W, "W").contiguous()
+    N, F_out = A_norm.n_rows, W.shape[1]
+    if out is None:
+        out = torch.empty((N, F_out), dtype=torch.float32, device=H.device)
+    b = _vec(bias)
+    check(lib.tg_gcn_layer_f32(N, A_norm.nnz, _p(A_norm.row_ptr), _p(A_norm.col_ind), _p(A_norm.values), _p(H),
+                               _ld(H), W.shape[0], F_out, _p(W), _p(b), ACT[act], _p(out), _ld(out),
+                               _p(row_order), MODE[mode], _stream()))
+    return out
+
+
+def sage_layer(A: CSR, H: torch.Tensor, W_neigh: torch.Tensor, W_self: torch.Tensor, bias=None,
+               aggregator: str = "mean", act="relu", row_order=None, out=None, mode: str = "exact"):
+    """SAGELayer::forward (src/layers.cpp:538)."""
+    H = _dense(H, "H")
+    Wn, Ws = _dense(W_neigh, "W_neigh").contiguous(), _dense(W_self, "W_self").contiguous()
+    N, F_out = A.n_rows, Wn.shape[1]
+    if out is None:
+        out = torch.empty((N, F_out), dtype=torch.float32, device=H.device)
+    b = _vec(bias)
+    check(lib.tg_sage_layer_f32(N, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(H), _ld(H), Wn.shape[0], F_out,
+                                _p(Wn), _p(Ws), _p(b), _lib.AGG_MAX if aggregator == "max" else _lib.AGG_MEAN,
+                                ACT[act], _p(out), _ld(out), _p(row_order), MODE[mode], _stream()))
+    return out
+
+
+def gat_layer(A_sl: CSR, H: torch.Tensor, W: torch.Tensor, a_left: torch.Tensor, a_right: torch.Tensor,
+              heads: int = 1, bias=None, negative_slope: float = 0.2, concat: bool = True, act=None,
+              row_order=None, out=None) -> torch.Tensor:
+    """Multi-head GATLayer::forward + head concat/average (src/layers.cpp:945, src/model.cpp:403).
+
+    W is F_in x (heads*F_out) with head h in columns [h*F_out, (h+1)*F_out);
+    a_left / a_right / bias are heads x F_out.
+    """
+    H, W = _dense(H, "H"), _dense(W, "W").contiguous()
+    F_out = W.shape[1] // heads
+    al, ar, b = _vec(a_left), _vec(a_right), _vec(bias)
+    N = A_sl.n_rows
+    if out is None:
+        out = torch.empty((N, heads * F_out if concat else F_out), dtype=torch.float32, device=H.device)
+    check(lib.tg_gat_layer_f32(N, A_sl.nnz, _p(A_sl.row_ptr), _p(A_sl.col_ind), _p(H), _ld(H), W.shape[0], heads,
+                               F_out, _p(W), _p(al), _p(ar), _p(b), negative_slope, int(concat), ACT[act],
+                               _p(out), _ld(out), _p(row_order), _stream()))
+    return out
