@@ -1,0 +1,456 @@
+"""Benchmark: 2-layer GCN (or SAGE-mean) forward on the Reddit-shaped graph.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload gcn|sage] [--small]
+
+Workload (the configuration the headline metric is quoted
+on at 1/2/4/8 GPUs): seeded Chung-Lu graph of 232,965 nodes and
+114,615,892 directed edges (mean degree ~492, heavy tail), 602-wide N(0,1)
+features, 602 -> 128 (ReLU) -> 41, log_softmax; Glorot weights, zero bias.
+A step is one forward of the whole graph.  For N > 1 (torchrun, one process
+per GPU) rows are split in equal blocks and each layer all-gathers its
+transformed rows over NCCL (tinygnn_b200/dist.py).
+
+Reported (rank 0, one JSON line):
+  value   edges/s = nnz(A_norm) / forward time, inputs resident in HBM,
+          normalised adjacency cached (max over ranks of CUDA-event time);
+  e2e     the same metric through the public path with host inputs: every
+          step uploads the raw CSR rows + feature rows from pinned memory,
+          runs gcn_norm, the forward and log_softmax, and reads the logits
+          back;
+  roofline  the layer-1 gather (SpMM, F=128): algorithmic bytes
+          nnz*(8+4F) + rows*(4+4F) + 4 per launch / its CUDA-event time,
+          against the measured HBM copy bandwidth (MEASURED_PEAKS.json);
+  cpu_baseline  the reference library (oracle/_ref) Model::forward on the
+          same graph on this host's cores (rank 0, N = 1).
+--impl reference times that reference forward alone (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+NODES, EDGES, FEATS, HIDDEN, CLASSES = 232_965, 114_615_892, 602, 128, 41
+SMALL = (20_000, 2_000_000)
+GRAPH_SEED, FEAT_SEED, WEIGHT_SEED = 9, 10, 10
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["gcn", "sage"], default="gcn")
+    ap.add_argument("--small", action="store_true", help="a 20k-node graph (quick functional run)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    return ap.parse_args()
+
+
+# ── workload ─────────────────────────────────────────────────────────────────
+def make_graph(small: bool, device):
+    from tinygnn_b200 import synth
+    n, e = SMALL if small else (NODES, EDGES)
+    n, rp, ci, v = synth.chung_lu_csr(n, e, GRAPH_SEED, device=device)
+    return n, rp, ci, v
+
+
+def make_weights(workload: str, device):
+    from tinygnn_b200 import synth
+    g = lambda i, o, s: synth.glorot(i, o, WEIGHT_SEED, s, device)  # noqa: E731
+    z = lambda o: torch.zeros(o, dtype=torch.float32, device=device)  # noqa: E731
+    if workload == "gcn":
+        return {"layer0.weight": g(FEATS, HIDDEN, 1), "layer0.bias": z(HIDDEN),
+                "layer1.weight": g(HIDDEN, CLASSES, 2), "layer1.bias": z(CLASSES)}
+    return {"layer0.weight_neigh": g(FEATS, HIDDEN, 1), "layer0.weight_self": g(FEATS, HIDDEN, 3),
+            "layer0.bias": z(HIDDEN), "layer1.weight_neigh": g(HIDDEN, CLASSES, 2),
+            "layer1.weight_self": g(HIDDEN, CLASSES, 4), "layer1.bias": z(CLASSES)}
+
+
+def layer_stack(workload: str, w):
+    from tinygnn_b200.dist import Layer
+    if workload == "gcn":
+        return [Layer("gcn", w["layer0.weight"], w["layer0.bias"], "relu"),
+                Layer("gcn", w["layer1.weight"], w["layer1.bias"], None)]
+    return [Layer("sage", w["layer0.weight_neigh"], w["layer0.bias"], "relu", w["layer0.weight_self"]),
+            Layer("sage", w["layer1.weight_neigh"], w["layer1.bias"], None, w["layer1.weight_self"])]
+
+
+def ref_spec(workload: str):
+    t = workload
+    return [dict(type=t, **{"in": FEATS, "out": HIDDEN}, act="relu"),
+            dict(type=t, **{"in": HIDDEN, "out": CLASSES}, act=None)]
+
+
+# ── clocks sampled during the timed region ───────────────────────────────────
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            self.gpu = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            self.gpu = str(device_index)
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.out, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except Exception:
+            self.proc.kill()
+        self.out.flush()
+        rows = []
+        with open(self.out.name) as f:
+            for line in f:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) < 7:
+                    continue
+                try:
+                    rows.append((float(p[0]), float(p[1]), float(p[2]), p[3:7]))
+                except ValueError:
+                    continue
+        os.unlink(self.out.name)
+        if not rows:
+            return None
+        load = [r for r in rows if r[2] > 200.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in load for i, x in enumerate(r[3]) if x.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in load), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(load), "power_w_max": max(r[2] for r in rows)}
+
+
+# ── timing helpers ───────────────────────────────────────────────────────────
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_steps(step, K: int, W: int, world: int) -> float:
+    """ms for exactly K steps after W warm-up steps (CUDA events, max over ranks)."""
+    for _ in range(W):
+        step()
+    barrier(world)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(K):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return max_over_ranks(s.elapsed_time(e), world)
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def committed_traffic(kernel_tag: str):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == kernel_tag:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+# ── reference arm / CPU baseline ─────────────────────────────────────────────
+def reference_forward_timer(workload, n, rp, ci, v, X, weights):
+    """A callable running the reference library's Model::forward + log_softmax once."""
+    import oracle
+    R = oracle.ref
+    if R is None:
+        return None, None
+    m = R.model(ref_spec(workload), {k: t.cpu().numpy() for k, t in weights.items()})
+    rp_h = np.ascontiguousarray(rp.cpu().numpy(), dtype=np.int32)
+    ci_h = np.ascontiguousarray(ci.cpu().numpy(), dtype=np.int32)
+    v_h = np.ascontiguousarray(v.cpu().numpy(), dtype=np.float32)
+    X_h = np.ascontiguousarray(X.cpu().numpy(), dtype=np.float32)
+    lib = R.lib
+    # The reference Tensors own copies of the arrays: the forward reads only them.
+    A = lib.ref_tensor_csr(n, ci_h.size, rp_h.ctypes.data, ci_h.ctypes.data, v_h.ctypes.data)
+    Xt = lib.ref_tensor_dense(X_h.shape[0], X_h.shape[1], X_h.ctypes.data)
+    del rp_h, ci_h, v_h, X_h
+
+    def run():
+        rc = lib.ref_model_forward_tensors(m.h, A, Xt, None, 1)
+        if rc:
+            raise RuntimeError(lib.ref_last_error().decode())
+
+    def free():
+        lib.ref_tensor_free(A)
+        lib.ref_tensor_free(Xt)
+
+    return run, free
+
+
+def nnz_normalized(rp, ci, n):
+    """nnz of gcn_norm(A) = nnz(A) + rows without a diagonal entry."""
+    rows = torch.repeat_interleave(torch.arange(n, device=rp.device), (rp[1:] - rp[:-1]).long())
+    has = torch.zeros(n, dtype=torch.bool, device=rp.device)
+    has[rows[ci.long() == rows]] = True
+    return int(ci.numel() + n - int(has.sum()))
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import oracle
+    if oracle.ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libtinygnn_ref.so was not built "
+                          "(the reference sources were absent at build time)"}))
+        return 0
+    dev = "cuda" if torch.cuda.is_available() else "cpu"  # input synthesis only
+    n, rp, ci, v = make_graph(args.small, dev)
+    from tinygnn_b200 import synth
+    X = synth.normal_rows(0, n, FEATS, FEAT_SEED, 0, dev)
+    w = make_weights(args.workload, dev)
+    nnz = nnz_normalized(rp, ci, n) if args.workload == "gcn" else int(ci.numel())
+    run, free = reference_forward_timer(args.workload, n, rp, ci, v, X, w)
+    del rp, ci, v, X
+    if dev == "cuda":
+        torch.cuda.empty_cache()
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = (time.perf_counter() - t0) / args.steps
+    free()
+    value = nnz / dt
+    cores = oracle.ref.max_threads()
+    unit = "edges/s"
+    print(json.dumps({
+        "impl": "reference", "metric": metric_name(args.workload), "value": value, "unit": unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_dict(args, n, nnz),
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "reference",
+                         "sample": f"{args.steps} full Model::forward + log_softmax calls on the whole graph"},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+    return 0
+
+
+def metric_name(workload):
+    return (f"{workload.upper()} forward edges/s (2-layer {FEATS}-{HIDDEN}-{CLASSES}, Reddit-shaped graph "
+            f"{NODES} nodes / {EDGES} edges)")
+
+
+def config_dict(args, n, nnz):
+    return {"workload": f"{args.workload}-reddit-shape" + ("-small" if args.small else ""),
+            "nodes": n, "nnz": nnz, "features": FEATS, "hidden": HIDDEN, "classes": CLASSES,
+            "partition": "1-D equal row blocks, NCCL all-gather of each layer's transformed rows",
+            "parallelism": f"row-partition x{args.gpus}",
+            "l2": "inputs larger than L2 (CSR 918 MB, features 561 MB); no flush between steps",
+            "mode": "exact (bit-identical GEMM + SpMM)" if args.workload == "gcn" else "fast (transform-first)"}
+
+
+# ── our arm ──────────────────────────────────────────────────────────────────
+def run_ours(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    import tinygnn_b200 as tg
+    from tinygnn_b200 import synth
+    from tinygnn_b200.dist import Comm, ShardedModel, gcn_norm_rows, row_block, slice_rows
+
+    comm = Comm(world, rank, group)
+    n, rp, ci, v = make_graph(args.small, dev)
+    R, r0, r1 = row_block(n, world, rank)
+    rows = r1 - r0
+    A_raw = slice_rows(rp, ci, v, r0, r1, n)
+    X = synth.normal_rows(r0, rows, FEATS, FEAT_SEED, 0, dev)
+    w = make_weights(args.workload, dev)
+    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev)
+    A_gcn = gcn_norm_rows(A_raw, r0, R, comm) if args.workload == "gcn" else None
+    nnz_local = A_gcn.nnz if A_gcn is not None else A_raw.nnz
+    nnz_total = nnz_local
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([nnz_local], dtype=torch.int64, device=dev)
+        dist.all_reduce(t)
+        nnz_total = int(t.item())
+    # keep the full graph only where the CPU baseline needs it
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
+    if not want_cpu:
+        del rp, ci, v
+    torch.cuda.synchronize()
+
+    # roofline hook: CUDA events around the layer-1 gather of every step
+    ev = []
+
+    def hook(li, what, edge):
+        if li == 0 and what == "gather":
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            ev.append(e)
+
+    def step():
+        model.forward(A_gcn, A_raw, X)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    launches0 = tg.launches()
+    model.timing = hook
+    ms = time_steps(step, args.steps, args.warmup, world)
+    model.timing = None
+    launches = tg.launches() - launches0
+    pairs = list(zip(ev[0::2], ev[1::2]))[-args.steps:]
+    gather_ms = statistics.mean(a.elapsed_time(b) for a, b in pairs)
+    per_launch = launches / (args.steps + args.warmup)
+
+    # e2e: host inputs -> device -> gcn_norm -> forward -> logits to host
+    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+    h_rp, h_ci, h_v, h_X = pin(A_raw.row_ptr), pin(A_raw.col_ind), pin(A_raw.values), pin(X)
+    h_out = torch.empty((rows, CLASSES), dtype=torch.float32).pin_memory()
+    d_rp, d_ci, d_v = torch.empty_like(A_raw.row_ptr), torch.empty_like(A_raw.col_ind), torch.empty_like(A_raw.values)
+    d_X = torch.empty_like(X)
+    dis_all = torch.zeros(R * world, dtype=torch.float32, device=dev)
+
+    def e2e_step():
+        d_rp.copy_(h_rp, non_blocking=True)
+        d_ci.copy_(h_ci, non_blocking=True)
+        d_v.copy_(h_v, non_blocking=True)
+        d_X.copy_(h_X, non_blocking=True)
+        A = tg.CSR(rows, n, d_rp, d_ci, d_v)
+        An = gcn_norm_rows(A, r0, R, comm, dis_all) if args.workload == "gcn" else None
+        out = model.forward(An, A, d_X)
+        h_out.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    e2e_ms = time_steps(e2e_step, args.steps, min(args.warmup, 3), world)
+    clocks = sampler.stop()
+    h2d = (h_rp.numel() + h_ci.numel()) * 4 + h_v.numel() * 4 + h_X.numel() * 4
+    d2h = h_out.numel() * 4
+
+    # parity spot check of the e2e logits against the device-resident run
+    ref_out = model.forward(A_gcn, A_raw, X)
+    torch.cuda.synchronize()
+    e2e_matches = bool(torch.equal(ref_out.cpu(), h_out))
+
+    # roofline of the layer-1 gather (rank-local)
+    F = HIDDEN
+    alg_bytes = nnz_local * (8 + 4 * F) + rows * (4 + 4 * F) + 4
+    if args.workload == "sage":
+        alg_bytes = nnz_local * (4 + 4 * F) + rows * (4 + 8 * F) + 4  # no values; + self row
+    achieved = alg_bytes / (gather_ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peaks()
+    traffic = committed_traffic(f"gather-{args.workload}-L1-{'small' if args.small else 'full'}-p{world}")
+    roof = {"kernel": "gather_rows (layer-1 SpMM, F=128, fused bias+ReLU)", "bound": "hbm",
+            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_source": f"{peak_kind} HBM copy bandwidth (MEASURED_PEAKS.json)" if peak_kind == "measured"
+            else "fallback 6650 GB/s", "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes,
+            "ms_per_launch": gather_ms}
+
+    cpu = None
+    if want_cpu:
+        Xfull = X
+        run, free = reference_forward_timer(args.workload, n, rp, ci, v, Xfull, w)
+        if run is not None:
+            import oracle
+            run()  # warm-up
+            reps, t0 = 0, time.perf_counter()
+            while reps < 1 or (time.perf_counter() - t0 < args.cpu_seconds and reps < 5):
+                run()
+                reps += 1
+            dt = (time.perf_counter() - t0) / reps
+            free()
+            cpu = {"value": nnz_total / dt, "unit": "edges/s", "cores": oracle.ref.max_threads(),
+                   "kind": "reference", "ms_per_forward": dt * 1e3,
+                   "sample": f"{reps} full Model::forward + log_softmax calls (after 1 warm-up) on the same graph"}
+
+    if rank == 0:
+        value = nnz_total / (ms / args.steps * 1e-3)
+        e2e_val = nnz_total / (e2e_ms / args.steps * 1e-3)
+        line = {
+            "metric": metric_name(args.workload), "value": value, "unit": "edges/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Chung-Lu graph, N(0,1) features, Glorot weights, zero bias)",
+            "config": config_dict(args, n, nnz_total),
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "edges/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms / args.steps, "logits_match_resident_run": e2e_matches,
+                    "note": "rank 0's bytes; every rank moves its own row block"},
+            "clocks": clocks, "gpu_launches": int(per_launch * args.steps),
+        }
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -75,6 +75,12 @@ typedef enum tg_aggregator { TG_AGG_MEAN = 0, TG_AGG_MAX = 1 } tg_aggregator;
  *                 transform-first when F_in > F_out, split long rows). */
 typedef enum tg_mode { TG_MODE_EXACT = 0, TG_MODE_FAST = 1 } tg_mode;
 
+/* OR'ed into a gather entry point's `mode`: every row of the gathered
+ * operand is readable up to its leading dimension (the buffer holds
+ * rows * ld floats), so rows whose width is not a multiple of 4 can still be
+ * read with 16-byte loads.  Results do not change. */
+#define TG_FLAG_B_ROWS_PADDED 0x100
+
 /* ── library ─────────────────────────────────────────────────────────────── */
 TG_API const char* tg_last_error_message(void); /* thread-local */
 TG_API const char* tg_version(void);
@@ -147,6 +153,19 @@ TG_API tg_status tg_sage_aggregate_f32(int64_t M, int64_t K, int64_t nnz,
                                        const float* H, int64_t F, int64_t ldh, float* out,
                                        int64_t ldo, int32_t aggregator, void* stream);
 
+/* The transform-first SAGE-mean combine (TG_MODE_FAST layers and the
+ * row-partitioned driver): with Tn = H . W_neigh (gathered, K x F) and
+ * Ts = H . W_self (this block's rows, M x F),
+ * out[i] = act(mean_{j in row i} Tn[j] + Ts[i] + bias).  Mean is linear, so
+ * this equals SAGELayer's (mean_j H[j]) . W_neigh + H[i] . W_self + b within
+ * fp32 tolerance while gathering F instead of F_in floats per edge. */
+TG_API tg_status tg_sage_mean_combine_f32(int64_t M, int64_t K, int64_t nnz,
+                                          const int32_t* row_ptr, const int32_t* col_ind,
+                                          const float* Tn, int64_t F, int64_t ldn, const float* Ts,
+                                          int64_t lds, const float* bias, int32_t act, float* out,
+                                          int64_t ldo, const int32_t* row_order, int32_t mode,
+                                          void* stream);
+
 /* sage_max_aggregate (src/layers.cpp:359-435), exact. */
 TG_API tg_status tg_sage_max_aggregate_f32(int64_t M, int64_t K, int64_t nnz,
                                            const int32_t* row_ptr, const int32_t* col_ind,
@@ -184,6 +203,29 @@ TG_API tg_status tg_gcn_norm_f32(int64_t N, int64_t nnz, const int32_t* row_ptr,
                                  const int32_t* col_ind, const float* values,
                                  int32_t* row_ptr_out, int32_t* col_ind_out, float* values_out,
                                  int64_t* nnz_out, void* stream);
+
+/* gcn_norm on a block of rows, for row-partitioned graphs.  The three calls
+ *   tg_add_self_loops_rows_f32(rows, row_offset, ...)   -> A_r + I_r
+ *   tg_csr_degree_inv_sqrt_f32(rows, ...)              -> dis_r (this block)
+ *   (all-gather dis_r over the blocks into dis_all)
+ *   tg_csr_scale_sym_f32(rows, ..., dis_r, dis_all)     -> (v * dis_i) * dis_j
+ * give exactly the rows of tg_gcn_norm_f32's result (src/layers.cpp:158-208).
+ * The block holds global rows [row_offset, row_offset + rows) with global
+ * column ids; the diagonal of local row i is column i + row_offset. */
+TG_API tg_status tg_add_self_loops_rows_f32(int64_t rows, int64_t row_offset, int64_t nnz,
+                                            const int32_t* row_ptr, const int32_t* col_ind,
+                                            const float* values, int32_t* row_ptr_out,
+                                            int32_t* col_ind_out, float* values_out,
+                                            int64_t* nnz_out, void* stream);
+/* dis[i] = 1/sqrtf(d_i) for d_i = the row's values summed in stored order,
+ * 0 when d_i is not > 0 (src/layers.cpp:170-187). */
+TG_API tg_status tg_csr_degree_inv_sqrt_f32(int64_t rows, const int32_t* row_ptr,
+                                            const float* values, float* dis_out, void* stream);
+/* values[k] = (values[k] * dis_row[i]) * dis_col[col_ind[k]] in place
+ * (src/layers.cpp:190-198). */
+TG_API tg_status tg_csr_scale_sym_f32(int64_t rows, const int32_t* row_ptr, const int32_t* col_ind,
+                                      float* values, const float* dis_row, const float* dis_col,
+                                      void* stream);
 
 /* Tensor::sparse_csr validation (src/tensor.cpp:46-86) on device arrays:
  * row_ptr[rows] == nnz, row_ptr non-decreasing, 0 <= col_ind < cols.

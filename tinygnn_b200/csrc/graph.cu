@@ -222,14 +222,15 @@ __global__ void row_expand_kernel(int64_t N, const int32_t* hist_scan, int32_t* 
 
 // ── add_self_loops / gcn_norm ───────────────────────────────────────────────
 // Pass 1: new row lengths (len + 1 when the row has no diagonal) into out_rp[i+1].
-__global__ void self_loop_count_kernel(int64_t N, const int32_t* rp, const int32_t* ci, int32_t* out_rp) {
+// The diagonal of local row i is column i + off (a block of rows of a square matrix).
+__global__ void self_loop_count_kernel(int64_t N, int64_t off, const int32_t* rp, const int32_t* ci, int32_t* out_rp) {
     const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     if (row >= N) return;
     const int lane = threadIdx.x & 31;
     const int32_t s = rp[row], e = rp[row + 1];
     bool has = false;
     for (int32_t b = s; b < e && !has; b += 32) {
-        const bool d = (b + lane < e) && ci[b + lane] == static_cast<int32_t>(row);
+        const bool d = (b + lane < e) && ci[b + lane] == static_cast<int32_t>(row + off);
         has = __any_sync(0xffffffffu, d);
     }
     if (lane == 0) out_rp[row + 1] = (e - s) + (has ? 0 : 1);
@@ -239,7 +240,7 @@ __global__ void self_loop_count_kernel(int64_t N, const int32_t* rp, const int32
 // Pass 2: copy with the diagonal inserted before the first column > i (or
 // appended), an existing diagonal becoming v + 1.  NORM also applies
 // gcn_norm's scale (pass 3 of the norm, after the degrees are known).
-__global__ void self_loop_fill_kernel(int64_t N, const int32_t* rp, const int32_t* ci, const float* v,
+__global__ void self_loop_fill_kernel(int64_t N, int64_t off, const int32_t* rp, const int32_t* ci, const float* v,
                                       const int32_t* out_rp, int32_t* out_ci, float* out_v) {
     const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     if (row >= N) return;
@@ -247,7 +248,7 @@ __global__ void self_loop_fill_kernel(int64_t N, const int32_t* rp, const int32_
     const int32_t s = rp[row], e = rp[row + 1];
     const int32_t o = out_rp[row];
     const bool insert = (out_rp[row + 1] - o) != (e - s);
-    const int32_t i32 = static_cast<int32_t>(row);
+    const int32_t i32 = static_cast<int32_t>(row + off);
     int32_t ins = e - s;  // insertion offset within the row (append by default)
     if (insert) {
         for (int32_t b = s; b < e; b += 32) {
@@ -287,12 +288,13 @@ __global__ void gcn_degree_kernel(int64_t N, const int32_t* rp, const float* v, 
     if (lane == 0) dis[row] = d > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(d)) : 0.0f;
 }
 
-__global__ void gcn_scale_kernel(int64_t N, const int32_t* rp, const int32_t* ci, float* v, const float* dis) {
+__global__ void gcn_scale_kernel(int64_t N, const int32_t* rp, const int32_t* ci, float* v, const float* dis_row,
+                                 const float* dis_col) {
     const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     if (row >= N) return;
     const int lane = threadIdx.x & 31;
-    const float di = dis[row];
-    for (int32_t t = rp[row] + lane; t < rp[row + 1]; t += 32) v[t] = __fmul_rn(__fmul_rn(v[t], di), dis[ci[t]]);
+    const float di = dis_row[row];
+    for (int32_t t = rp[row] + lane; t < rp[row + 1]; t += 32) v[t] = __fmul_rn(__fmul_rn(v[t], di), dis_col[ci[t]]);
 }
 
 unsigned stride_grid(int64_t n, int threads) {
@@ -427,29 +429,35 @@ void edge_list_to_csr(int64_t N, int64_t E, const int32_t* src, const int32_t* d
     }
 }
 
-int64_t add_self_loops(int64_t N, int64_t nnz, const int32_t* rp, const int32_t* ci, const float* v, int32_t* orp,
+int64_t add_self_loops(int64_t N, int64_t off, const int32_t* rp, const int32_t* ci, const float* v, int32_t* orp,
                        int32_t* oci, float* ov, cudaStream_t s) {
-    (void)nnz;
     if (N == 0) {
         TG_CUDA(cudaMemsetAsync(orp, 0, sizeof(int32_t), s));
         return 0;
     }
-    launch("self_loop_count", self_loop_count_kernel, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, rp, ci, orp);
+    launch("self_loop_count", self_loop_count_kernel, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, off, rp, ci, orp);
     inclusive_scan_i32(orp + 1, N, s);
-    launch("self_loop_fill", self_loop_fill_kernel, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, rp, ci, v,
+    launch("self_loop_fill", self_loop_fill_kernel, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, off, rp, ci, v,
            static_cast<const int32_t*>(orp), oci, ov);
     return read_back(orp + N, s);
 }
 
-int64_t gcn_norm(int64_t N, int64_t nnz, const int32_t* rp, const int32_t* ci, const float* v, int32_t* orp,
-                 int32_t* oci, float* ov, cudaStream_t s) {
-    const int64_t out = add_self_loops(N, nnz, rp, ci, v, orp, oci, ov, s);
+void degree_inv_sqrt(int64_t N, const int32_t* rp, const float* v, float* dis, cudaStream_t s) {
+    launch("gcn_degree", gcn_degree_kernel, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, rp, v, dis);
+}
+
+void scale_sym(int64_t N, const int32_t* rp, const int32_t* ci, float* v, const float* dis_row, const float* dis_col,
+               cudaStream_t s) {
+    launch("gcn_scale", gcn_scale_kernel, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, rp, ci, v, dis_row, dis_col);
+}
+
+int64_t gcn_norm(int64_t N, const int32_t* rp, const int32_t* ci, const float* v, int32_t* orp, int32_t* oci,
+                 float* ov, cudaStream_t s) {
+    const int64_t out = add_self_loops(N, 0, rp, ci, v, orp, oci, ov, s);
     if (N == 0) return 0;
     Scratch<float> dis(static_cast<size_t>(N), s);
-    launch("gcn_degree", gcn_degree_kernel, dim3(warp_rows_grid(N)), dim3(256), 0, s, N,
-           static_cast<const int32_t*>(orp), static_cast<const float*>(ov), dis.p);
-    launch("gcn_scale", gcn_scale_kernel, dim3(warp_rows_grid(N)), dim3(256), 0, s, N,
-           static_cast<const int32_t*>(orp), static_cast<const int32_t*>(oci), ov, static_cast<const float*>(dis.p));
+    degree_inv_sqrt(N, orp, ov, dis.p, s);
+    scale_sym(N, orp, oci, ov, dis.p, dis.p, s);
     return out;
 }
 
@@ -479,7 +487,7 @@ TG_API tg_status tg_add_self_loops_f32(int64_t N, int64_t nnz, const int32_t* ro
         require_device();
         if (N < 0 || nnz < 0) invalid("add_self_loops: negative size");
         if (nnz + N > INT32_MAX) invalid("add_self_loops: result does not fit int32 row_ptr");
-        const int64_t n = add_self_loops(N, nnz, row_ptr, col_ind, values, row_ptr_out, col_ind_out, values_out,
+        const int64_t n = add_self_loops(N, 0, row_ptr, col_ind, values, row_ptr_out, col_ind_out, values_out,
                                          as_stream(stream));
         if (nnz_out) *nnz_out = n;
     });
@@ -492,9 +500,41 @@ TG_API tg_status tg_gcn_norm_f32(int64_t N, int64_t nnz, const int32_t* row_ptr,
         require_device();
         if (N < 0 || nnz < 0) invalid("gcn_norm: negative size");
         if (nnz + N > INT32_MAX) invalid("gcn_norm: result does not fit int32 row_ptr");
-        const int64_t n = gcn_norm(N, nnz, row_ptr, col_ind, values, row_ptr_out, col_ind_out, values_out,
+        const int64_t n = gcn_norm(N, row_ptr, col_ind, values, row_ptr_out, col_ind_out, values_out,
                                    as_stream(stream));
         if (nnz_out) *nnz_out = n;
+    });
+}
+
+TG_API tg_status tg_add_self_loops_rows_f32(int64_t rows, int64_t row_offset, int64_t nnz, const int32_t* row_ptr,
+                                            const int32_t* col_ind, const float* values, int32_t* row_ptr_out,
+                                            int32_t* col_ind_out, float* values_out, int64_t* nnz_out,
+                                            void* stream) {
+    return guard([&] {
+        require_device();
+        if (rows < 0 || row_offset < 0 || nnz < 0) invalid("add_self_loops: negative size");
+        if (nnz + rows > INT32_MAX) invalid("add_self_loops: result does not fit int32 row_ptr");
+        const int64_t n = add_self_loops(rows, row_offset, row_ptr, col_ind, values, row_ptr_out, col_ind_out,
+                                         values_out, as_stream(stream));
+        if (nnz_out) *nnz_out = n;
+    });
+}
+
+TG_API tg_status tg_csr_degree_inv_sqrt_f32(int64_t rows, const int32_t* row_ptr, const float* values,
+                                            float* dis_out, void* stream) {
+    return guard([&] {
+        require_device();
+        if (rows < 0) invalid("gcn_norm: negative size");
+        if (rows) degree_inv_sqrt(rows, row_ptr, values, dis_out, as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_csr_scale_sym_f32(int64_t rows, const int32_t* row_ptr, const int32_t* col_ind, float* values,
+                                      const float* dis_row, const float* dis_col, void* stream) {
+    return guard([&] {
+        require_device();
+        if (rows < 0) invalid("gcn_norm: negative size");
+        if (rows) scale_sym(rows, row_ptr, col_ind, values, dis_row, dis_col, as_stream(stream));
     });
 }
 

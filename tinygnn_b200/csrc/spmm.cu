@@ -354,11 +354,31 @@ TG_API tg_status tg_spmm_f32(int64_t M, int64_t K, int64_t nnz, const int32_t* r
         check_ptr("spmm", "col_ind/values", col_ind && values ? col_ind : nullptr, nnz > 0);
         check_ptr("spmm", "B", B, nnz > 0 && F > 0);
         check_ptr("spmm", "C", C, M > 0 && F > 0);
-        (void)mode;  // both modes use the order-preserving kernel for now
         GatherArgs a;
         a.M = M; a.rp = row_ptr; a.ci = col_ind; a.val = values; a.order = row_order;
         a.B = B; a.ldb = ldb; a.F = F; a.C = C; a.ldc = ldc;
         a.bias = bias; a.act = act; a.alpha = alpha; a.op = GATHER_SUM;
+        a.b_padded = (mode & TG_FLAG_B_ROWS_PADDED) != 0;
+        gather_rows(a, as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_sage_mean_combine_f32(int64_t M, int64_t K, int64_t nnz, const int32_t* row_ptr,
+                                          const int32_t* col_ind, const float* Tn, int64_t F, int64_t ldn,
+                                          const float* Ts, int64_t lds, const float* bias, int32_t act, float* out,
+                                          int64_t ldo, const int32_t* row_order, int32_t mode, void* stream) {
+    return guard([&] {
+        require_device();
+        (void)K; (void)nnz;
+        if (M < 0 || F < 0) invalid("sage_mean_combine: negative size");
+        check_ld("sage_mean_combine", "Tn", ldn, F);
+        check_ld("sage_mean_combine", "Ts", lds, F);
+        check_ld("sage_mean_combine", "out", ldo, F);
+        GatherArgs a;
+        a.M = M; a.rp = row_ptr; a.ci = col_ind; a.order = row_order;
+        a.B = Tn; a.ldb = ldn; a.F = F; a.self = Ts; a.lds = lds;
+        a.C = out; a.ldc = ldo; a.bias = bias; a.act = act; a.op = GATHER_SUM; a.mean = 1;
+        a.b_padded = (mode & TG_FLAG_B_ROWS_PADDED) != 0;
         gather_rows(a, as_stream(stream));
     });
 }

@@ -169,6 +169,18 @@ def add_bias_(X: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
 
 
 # ── sparse ops ───────────────────────────────────────────────────────────────
+FLAG_B_ROWS_PADDED = 0x100
+
+
+def _padded(t: torch.Tensor) -> bool:
+    """True when every row of the 2-D view t is readable up to its row stride."""
+    if t.dim() != 2 or t.shape[0] == 0:
+        return False
+    storage_elems = t.untyped_storage().nbytes() // t.element_size()
+    last_row_end = t.storage_offset() + (t.shape[0] - 1) * t.stride(0) + t.stride(0)
+    return t.stride(0) % 4 == 0 and last_row_end <= storage_elems
+
+
 def spmm(A: CSR, B: torch.Tensor, bias=None, act=None, alpha: float = 0.0, row_order=None,
          out: Optional[torch.Tensor] = None, mode: str = "exact") -> torch.Tensor:
     """C = act(A . B + bias)  (TinyGNN spmm, src/ops.cpp:198)."""
@@ -182,9 +194,25 @@ def spmm(A: CSR, B: torch.Tensor, bias=None, act=None, alpha: float = 0.0, row_o
     if out is None:
         out = torch.empty((A.n_rows, F), dtype=torch.float32, device=B.device)
     b = _vec(bias)
+    flags = MODE[mode] | (FLAG_B_ROWS_PADDED if _padded(B) else 0)
     check(lib.tg_spmm_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(B), F,
-                          _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha, _p(row_order), MODE[mode],
+                          _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha, _p(row_order), flags,
                           _stream()))
+    return out
+
+
+def sage_mean_combine(A: CSR, Tn: torch.Tensor, Ts: torch.Tensor, bias=None, act=None, row_order=None,
+                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[i] = act(mean_j Tn[j] + Ts[i] + bias): transform-first SAGE mean."""
+    Tn, Ts = _dense(Tn, "Tn"), _dense(Ts, "Ts")
+    F = Tn.shape[1]
+    if out is None:
+        out = torch.empty((A.n_rows, F), dtype=torch.float32, device=Tn.device)
+    b = _vec(bias)
+    flags = FLAG_B_ROWS_PADDED if _padded(Tn) else 0
+    check(lib.tg_sage_mean_combine_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(Tn), F,
+                                       _ld(Tn), _p(Ts), _ld(Ts), _p(b), ACT[act], _p(out), _ld(out),
+                                       _p(row_order), flags, _stream()))
     return out
 
 
@@ -262,6 +290,35 @@ def add_self_loops(A: CSR) -> CSR:
 def gcn_norm(A: CSR) -> CSR:
     """gcn_norm (src/layers.cpp:158): D^-1/2 (A + I) D^-1/2."""
     return _csr_expand(lib.tg_gcn_norm_f32, A)
+
+
+def add_self_loops_rows(A: CSR, row_offset: int) -> CSR:
+    """add_self_loops of a row block (global rows row_offset.., global columns)."""
+    N = A.n_rows
+    cap = A.nnz + N
+    dev = A.row_ptr.device
+    rp = torch.empty(N + 1, dtype=torch.int32, device=dev)
+    ci = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+    v = torch.empty(max(cap, 1), dtype=torch.float32, device=dev)
+    nnz = C.c_int64(0)
+    check(lib.tg_add_self_loops_rows_f32(N, row_offset, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(rp),
+                                         _p(ci), _p(v), C.byref(nnz), _stream()))
+    return CSR(N, A.n_cols, rp, ci[:nnz.value], v[:nnz.value])
+
+
+def degree_inv_sqrt(A: CSR, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """dis[i] = 1/sqrtf(sum of row i's values) (0 for non-positive sums)."""
+    if out is None:
+        out = torch.empty(A.n_rows, dtype=torch.float32, device=A.row_ptr.device)
+    check(lib.tg_csr_degree_inv_sqrt_f32(A.n_rows, _p(A.row_ptr), _p(A.values), _p(out), _stream()))
+    return out
+
+
+def scale_sym_(A: CSR, dis_row: torch.Tensor, dis_col: torch.Tensor) -> CSR:
+    """values = (values * dis_row[i]) * dis_col[j], in place."""
+    check(lib.tg_csr_scale_sym_f32(A.n_rows, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(dis_row),
+                                   _p(dis_col), _stream()))
+    return A
 
 
 def csr_validate(A: CSR) -> None:

@@ -65,6 +65,19 @@ def normal(shape, seed: int, stream: int = 0, device="cpu") -> torch.Tensor:
     return z.to(torch.float32).reshape(shape)
 
 
+def normal_rows(row0: int, rows: int, cols: int, seed: int, stream: int = 0, device="cpu") -> torch.Tensor:
+    """Rows [row0, row0 + rows) of a seeded N(0, 1) matrix with ``cols`` columns.
+
+    Element (i, j) depends only on (seed, i*cols + j), so any row block of
+    the global matrix is the same whichever process generates it.
+    """
+    idx = torch.arange(row0 * cols, (row0 + rows) * cols, device=device)
+    u1 = (_lsr(hash64(idx, seed, 2 * stream + 1), 11).to(torch.float64) + 1.0) * (1.0 / (1 << 53))
+    u2 = _lsr(hash64(idx, seed, 2 * stream + 2), 11).to(torch.float64) * (1.0 / (1 << 53))
+    z = torch.sqrt(-2.0 * torch.log(u1)) * torch.cos(2 * math.pi * u2)
+    return z.to(torch.float32).reshape(rows, cols)
+
+
 def glorot(fan_in: int, fan_out: int, seed: int, stream: int = 0, device="cpu") -> torch.Tensor:
     """Glorot-uniform fan_in x fan_out weight."""
     r = math.sqrt(6.0 / (fan_in + fan_out))
