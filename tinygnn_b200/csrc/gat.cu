@@ -27,6 +27,7 @@ namespace tg {
 
 void gemm_exact(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
                 float* C, int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s);
+void csr_degree_order(int64_t M, const int32_t* rp, int32_t* out, cudaStream_t s);
 
 namespace {
 
@@ -230,6 +231,12 @@ void gat_layer(int64_t N, const int32_t* rp, const int32_t* ci, const float* Hf,
     Scratch<float> cat(concat ? 1 : static_cast<size_t>(N * HD), s);
     if (!concat) { cat_out = cat.p; cat_ld = HD; }
 
+    // Longest rows first unless the caller scheduled them (see gather_rows).
+    Scratch<int32_t> auto_order(order || N < 16384 ? 1 : static_cast<size_t>(N), s);
+    if (!order && N >= 16384) {
+        csr_degree_order(N, rp, auto_order.p, s);
+        order = auto_order.p;
+    }
     GatArgs g{N, rp, ci, order, Wh.p, ldw, sd.p, H, d, slope, bias, act, concat ? post : TG_ACT_NONE, cat_out, cat_ld};
     int vec = (d % 4 == 0) ? 4 : (d % 2 == 0 ? 2 : 1);
     while (vec > 1 && HD / vec < 8) vec /= 2;

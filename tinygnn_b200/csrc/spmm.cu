@@ -1,245 +1,104 @@
 // ============================================================================
-//  spmm.cu -- CSR row-gather kernels: spmm, SAGE aggregation, degree order.
+//  spmm.cu -- CSR row-gather entry points: spmm, SAGE aggregation, the
+//  transform-first SAGE combine, and the degree-ordered row schedule.
 //
 //  Reference: TinyGNN spmm (src/ops.cpp:198-297), SAGE mean/max aggregation
 //  (src/layers.cpp:588-637, 674-700), sage_max_aggregate (359-435).
 //
 //  Layout in HBM: CSR row_ptr/col_ind int32, values fp32; dense operands
-//  row-major fp32 with a leading dimension.  A row is owned by a sub-warp of
-//  LPR lanes; lane l holds SPL vectors of VEC floats of the output row
-//  (features (s*LPR + l)*VEC .. +VEC-1).  The row's col/val are read LPR at a
-//  time (coalesced) and broadcast with shuffles; U gathered rows are loaded
-//  before their fused multiply-adds are applied in stored order, which keeps
-//  U*SPL 4..16-byte loads per lane in flight.  The kernel is HBM-bound: its
-//  algorithmic traffic is nnz*(8 + 4F) + M*(4 + 4F) bytes.
+//  row-major fp32 with a leading dimension.  The kernel (gather_kernel.cuh)
+//  is HBM/L2-bound: algorithmic traffic nnz*(8 + 4F) + M*(4 + 4F) bytes for
+//  spmm (nnz*(4 + 4F) + ... without values).
 // ============================================================================
 #include <algorithm>
+#include <memory>
 
 #include "gather.cuh"
+#include "gather_kernel.cuh"
 #include "launch.cuh"
 
 namespace tg {
 
 namespace {
 
-template <int V>
-struct VecT;
-template <>
-struct VecT<1> { using T = float; };
-template <>
-struct VecT<2> { using T = float2; };
-template <>
-struct VecT<4> { using T = float4; };
-
-template <int V>
-__device__ __forceinline__ void ldv(const float* p, float (&x)[V]) {
-    if constexpr (V == 4) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(p));
-        x[0] = t.x; x[1] = t.y; x[2] = t.z; x[3] = t.w;
-    } else if constexpr (V == 2) {
-        const float2 t = __ldg(reinterpret_cast<const float2*>(p));
-        x[0] = t.x; x[1] = t.y;
-    } else {
-        x[0] = __ldg(p);
-    }
-}
-
-template <int V>
-__device__ __forceinline__ void stv(float* p, const float (&x)[V]) {
-    if constexpr (V == 4) {
-        *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
-    } else if constexpr (V == 2) {
-        *reinterpret_cast<float2*>(p) = make_float2(x[0], x[1]);
-    } else {
-        p[0] = x[0];
-    }
-}
-
-template <int OP>
-__device__ __forceinline__ float reduce_step(float acc, float w, float h, bool avx_col) {
-    if constexpr (OP == GATHER_SUM) {
-        return fmaf(w, h, acc);  // acc += w * h, one rounding (reference FMA chain)
-    } else {
-        // _mm256_max_ps(r, h) on full 8-groups vs std::max(r, h) elsewhere.
-        return avx_col ? ((acc > h) ? acc : h) : ((acc < h) ? h : acc);
-    }
-}
-
-// Kernel: one sub-warp of LPR lanes per output row; gridDim.y feature passes.
-template <int VEC, int LPR, int SPL, int OP>
-__global__ void __launch_bounds__(256) gather_rows_kernel(const GatherArgs a) {
-    constexpr int RPW = 32 / LPR;                 // rows per warp
-    constexpr int U = (SPL >= 4) ? 2 : (SPL == 2 ? 4 : 8);  // gathered rows in flight
-    const int lane = threadIdx.x & 31;
-    const int sub = lane / LPR;
-    const int l = lane % LPR;
-    const unsigned mask = (LPR == 32) ? 0xffffffffu : (((1u << LPR) - 1u) << (sub * LPR));
-
-    const int64_t slot = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW + sub;
-    if (slot >= a.M) return;  // whole sub-warps leave together
-    const int64_t row = a.order ? static_cast<int64_t>(__ldg(a.order + slot)) : slot;
-
-    const int64_t f0 = static_cast<int64_t>(blockIdx.y) * (LPR * SPL * VEC);  // feature pass
-    bool live[SPL], full[SPL];
-    int64_t fo[SPL];
-#pragma unroll
-    for (int s = 0; s < SPL; ++s) {
-        fo[s] = f0 + static_cast<int64_t>(s * LPR + l) * VEC;
-        live[s] = fo[s] < a.F;          // vector starts inside the row
-        full[s] = fo[s] + VEC <= a.F;   // ... and ends inside it (else B is padded)
-    }
-
-    float acc[SPL][VEC];
-    const float init = (OP == GATHER_SUM) ? 0.0f : -INFINITY;
-#pragma unroll
-    for (int s = 0; s < SPL; ++s)
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) acc[s][k] = init;
-
-    bool avx[SPL][VEC];
-#pragma unroll
-    for (int s = 0; s < SPL; ++s)
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) avx[s][k] = (fo[s] + k) < a.max_avx_cols;
-
-    const int32_t start = __ldg(a.rp + row);
-    const int32_t end = __ldg(a.rp + row + 1);
-
-    for (int32_t base = start; base < end; base += LPR) {
-        const int n = min(LPR, end - base);
-        int my_c = 0;
-        float my_w = 1.0f;
-        if (l < n) {
-            my_c = __ldg(a.ci + base + l);
-            if (a.val) my_w = __ldg(a.val + base + l);
-        }
-        int e = 0;
-        for (; e + U <= n; e += U) {
-            int c[U];
-            float w[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                c[u] = __shfl_sync(mask, my_c, e + u, LPR);
-                w[u] = __shfl_sync(mask, my_w, e + u, LPR);
-            }
-            float h[U][SPL][VEC];
-#pragma unroll
-            for (int u = 0; u < U; ++u)
-#pragma unroll
-                for (int s = 0; s < SPL; ++s)
-                    if (live[s]) ldv<VEC>(a.B + static_cast<int64_t>(c[u]) * a.ldb + fo[s], h[u][s]);
-#pragma unroll
-            for (int u = 0; u < U; ++u)
-#pragma unroll
-                for (int s = 0; s < SPL; ++s)
-                    if (live[s])
-#pragma unroll
-                        for (int k = 0; k < VEC; ++k)
-                            acc[s][k] = reduce_step<OP>(acc[s][k], w[u], h[u][s][k], avx[s][k]);
-        }
-        for (; e < n; ++e) {
-            const int c = __shfl_sync(mask, my_c, e, LPR);
-            const float w = __shfl_sync(mask, my_w, e, LPR);
-#pragma unroll
-            for (int s = 0; s < SPL; ++s)
-                if (live[s]) {
-                    float h[VEC];
-                    ldv<VEC>(a.B + static_cast<int64_t>(c) * a.ldb + fo[s], h);
-#pragma unroll
-                    for (int k = 0; k < VEC; ++k) acc[s][k] = reduce_step<OP>(acc[s][k], w, h[k], avx[s][k]);
-                }
-        }
-    }
-
-    // Epilogue: (mean) -> (+ self) -> (+ bias) -> activation, each one rounding.
-    const int32_t deg = end - start;
-    const float inv_deg = (OP == GATHER_SUM && a.mean && deg > 0) ? __fdiv_rn(1.0f, static_cast<float>(deg)) : 1.0f;
-#pragma unroll
-    for (int s = 0; s < SPL; ++s) {
-        if (!live[s]) continue;
-        float x[VEC];
-        float sv[VEC], bv[VEC];
-        if (full[s]) {
-            if (a.self) ldv<VEC>(a.self + row * a.lds + fo[s], sv);
-            if (a.bias) ldv<VEC>(a.bias + fo[s], bv);
-        } else {
-#pragma unroll
-            for (int k = 0; k < VEC; ++k) {
-                const bool in = fo[s] + k < a.F;
-                sv[k] = (a.self && in) ? a.self[row * a.lds + fo[s] + k] : 0.0f;
-                bv[k] = (a.bias && in) ? a.bias[fo[s] + k] : 0.0f;
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) {
-            float v = acc[s][k];
-            if (OP == GATHER_MAX && deg == 0) v = 0.0f;
-            if (OP == GATHER_SUM && a.mean && deg > 0) v = __fmul_rn(v, inv_deg);
-            if (a.self) v = __fadd_rn(v, sv[k]);
-            if (a.bias) v = __fadd_rn(v, bv[k]);
-            x[k] = apply_act(a.act, v, a.alpha);
-        }
-        if (full[s]) {
-            stv<VEC>(a.C + row * a.ldc + fo[s], x);
-        } else {
-#pragma unroll
-            for (int k = 0; k < VEC; ++k)
-                if (fo[s] + k < a.F) a.C[row * a.ldc + fo[s] + k] = x[k];
-        }
-    }
-}
-
-template <int VEC, int LPR, int SPL>
-void launch_gather(const GatherArgs& a, cudaStream_t s) {
-    constexpr int RPB = (256 / 32) * (32 / LPR);  // rows per block
-    const int64_t per_pass = static_cast<int64_t>(LPR) * SPL * VEC;
-    const int64_t passes = ceil_div(a.F, per_pass);
-    dim3 grid(static_cast<unsigned>(ceil_div(a.M, RPB)), static_cast<unsigned>(passes));
-    if (a.op == GATHER_SUM)
-        launch("gather_rows<sum>", gather_rows_kernel<VEC, LPR, SPL, GATHER_SUM>, grid, dim3(256), 0, s, a);
-    else
-        launch("gather_rows<max>", gather_rows_kernel<VEC, LPR, SPL, GATHER_MAX>, grid, dim3(256), 0, s, a);
-}
-
-template <int VEC>
-void dispatch_lpr(const GatherArgs& a, cudaStream_t s) {
-    const int64_t S = ceil_div(a.F, VEC);  // vector slots per row
-    if (S <= 8) launch_gather<VEC, 8, 1>(a, s);
-    else if (S <= 16) launch_gather<VEC, 16, 1>(a, s);
-    else if (S <= 32) launch_gather<VEC, 32, 1>(a, s);
-    else if (S <= 64) launch_gather<VEC, 32, 2>(a, s);
-    else launch_gather<VEC, 32, 4>(a, s);  // feature passes of 128 vectors beyond
-}
+// Row count from which a gather without a schedule computes a degree order.
+constexpr int64_t kAutoOrderRows = 16384;
 
 inline bool aligned(const void* p, int bytes) {
     return (reinterpret_cast<uintptr_t>(p) % static_cast<uintptr_t>(bytes)) == 0;
 }
 
+template <int VEC, int LPR, int SPL, bool CVEC>
+void launch_gather(const GatherArgs& a, cudaStream_t s) {
+    constexpr int RPB = (256 / 32) * (32 / LPR);  // rows per block
+    // Gathered rows in flight per batch (sweep on the Reddit-shaped graph,
+    // degree-ordered: 4 for 32-lane rows, 8 for narrower ones).
+    constexpr int U = (SPL >= 4) ? 2 : (SPL == 2 ? 4 : (LPR == 32 ? 4 : 8));
+    const int64_t per_pass = static_cast<int64_t>(LPR) * SPL * VEC;
+    const int64_t passes = ceil_div(a.F, per_pass);
+    dim3 grid(static_cast<unsigned>(ceil_div(a.M, RPB)), static_cast<unsigned>(passes));
+    if (a.op == GATHER_SUM)
+        launch("gather_rows<sum>", gk::gather_rows_kernel<VEC, LPR, SPL, GATHER_SUM, U, CVEC>, grid, dim3(256), 0,
+               s, a);
+    else
+        launch("gather_rows<max>", gk::gather_rows_kernel<VEC, LPR, SPL, GATHER_MAX, U, CVEC>, grid, dim3(256), 0,
+               s, a);
+}
+
+template <int VEC, bool CVEC>
+void dispatch_lpr(const GatherArgs& a, cudaStream_t s) {
+    const int64_t S = ceil_div(a.F, VEC);  // vector slots per row
+    if (S <= 8) launch_gather<VEC, 8, 1, CVEC>(a, s);
+    else if (S <= 16) launch_gather<VEC, 16, 1, CVEC>(a, s);
+    else if (S <= 32) launch_gather<VEC, 32, 1, CVEC>(a, s);
+    else if (S <= 64) launch_gather<VEC, 32, 2, CVEC>(a, s);
+    else launch_gather<VEC, 32, 4, CVEC>(a, s);  // feature passes of 128 vectors beyond
+}
+
+template <int VEC>
+void dispatch_cvec(const GatherArgs& a, cudaStream_t s) {
+    bool cvec = a.ldc % VEC == 0 && aligned(a.C, 4 * VEC);
+    if (a.self) cvec = cvec && a.lds % VEC == 0 && aligned(a.self, 4 * VEC);
+    if (a.bias) cvec = cvec && aligned(a.bias, 4 * VEC);
+    if (cvec) dispatch_lpr<VEC, true>(a, s);
+    else dispatch_lpr<VEC, false>(a, s);
+}
+
 }  // namespace
 
-void gather_rows(const GatherArgs& a, cudaStream_t s) {
-    if (a.M == 0 || a.F == 0) return;
-    // Widest vector that divides F and every leading dimension and keeps
-    // every base aligned; narrower when it would leave fewer than 8 vectors.
-    int vec = 4;
+void csr_degree_order(int64_t M, const int32_t* rp, int32_t* out, cudaStream_t s);
+
+void gather_rows(const GatherArgs& args, cudaStream_t s) {
+    if (args.M == 0 || args.F == 0) return;
+    GatherArgs a = args;
+    // Without a caller-given schedule, large launches start their longest
+    // rows first: a hub row left to the end of the grid is a serial tail
+    // (measured 5.8 -> 3.7 ms on the Reddit-shaped layer-1 gather).
+    std::unique_ptr<Scratch<int32_t>> order;
+    if (!a.order && a.M >= kAutoOrderRows) {
+        order.reset(new Scratch<int32_t>(static_cast<size_t>(a.M), s));
+        csr_degree_order(a.M, a.rp, order->p, s);
+        a.order = order->p;
+    }
+    // Load width: the widest vector dividing B's leading dimension with B
+    // aligned, and dividing F unless B's rows are padded; narrower when it
+    // would leave fewer than 8 vectors per row.
     auto ok = [&](int v) {
-        if ((a.F % v && !a.b_padded) || a.ldb % v || a.ldc % v) return false;
-        if (!aligned(a.B, 4 * v) || !aligned(a.C, 4 * v)) return false;
-        if (a.self && (a.lds % v || !aligned(a.self, 4 * v))) return false;
-        if (a.bias && !aligned(a.bias, 4 * v)) return false;
-        return true;
+        if (a.F % v && !a.b_padded) return false;
+        return a.ldb % v == 0 && aligned(a.B, 4 * v);
     };
+    int vec = 4;
     while (vec > 1 && (!ok(vec) || ceil_div(a.F, vec) < 8)) vec /= 2;
-    if (vec == 4) dispatch_lpr<4>(a, s);
-    else if (vec == 2) dispatch_lpr<2>(a, s);
-    else dispatch_lpr<1>(a, s);
+    if (vec == 4) dispatch_cvec<4>(a, s);
+    else if (vec == 2) dispatch_cvec<2>(a, s);
+    else dispatch_cvec<1>(a, s);
 }
 
 // ── Degree order: a stable bucket sort of rows by decreasing length ─────────
-// Bucket b(i) = 31 - floor(log2(len_i + 1)) (longest rows in bucket 0..).
-// Three passes: per-block bucket counts, one exclusive scan over
-// (bucket, block), then a stable scatter (ranks from warp match/popc and
-// per-warp prefix counts in shared memory).
+// Bucket b(i) = clz(len_i + 1) (longest rows in the lowest bucket).  Three
+// passes: per-block bucket counts, one exclusive scan over (bucket, block),
+// then a stable scatter (ranks from warp match/popc and per-warp prefix
+// counts in shared memory).
 namespace {
 constexpr int ORDER_BLOCK = 1024;
 constexpr int NBUCKET = 32;

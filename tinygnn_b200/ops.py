@@ -46,6 +46,10 @@ def _ld(t: torch.Tensor) -> int:
     return max(t.stride(0), t.shape[1]) if t.dim() == 2 else 1
 
 
+def _ord(A, row_order):
+    return row_order if row_order is not None else getattr(A, "order", None)
+
+
 def _vec(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
     if t is None:
         return None
@@ -61,10 +65,18 @@ class CSR:
     row_ptr: torch.Tensor
     col_ind: torch.Tensor
     values: torch.Tensor
+    # Optional row schedule (int32 permutation, longest rows first) reused by
+    # every gather over this matrix; without it large gathers compute one.
+    order: Optional[torch.Tensor] = None
 
     @property
     def nnz(self) -> int:
         return int(self.col_ind.numel())
+
+    def with_degree_order(self) -> "CSR":
+        """Compute and keep the longest-rows-first schedule."""
+        self.order = degree_order(self)
+        return self
 
     @classmethod
     def from_numpy(cls, row_ptr, col_ind, values=None, n_cols=None, device="cuda") -> "CSR":
@@ -196,7 +208,7 @@ def spmm(A: CSR, B: torch.Tensor, bias=None, act=None, alpha: float = 0.0, row_o
     b = _vec(bias)
     flags = MODE[mode] | (FLAG_B_ROWS_PADDED if _padded(B) else 0)
     check(lib.tg_spmm_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(B), F,
-                          _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha, _p(row_order), flags,
+                          _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha, _p(_ord(A, row_order)), flags,
                           _stream()))
     return out
 
@@ -212,7 +224,7 @@ def sage_mean_combine(A: CSR, Tn: torch.Tensor, Ts: torch.Tensor, bias=None, act
     flags = FLAG_B_ROWS_PADDED if _padded(Tn) else 0
     check(lib.tg_sage_mean_combine_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(Tn), F,
                                        _ld(Tn), _p(Ts), _ld(Ts), _p(b), ACT[act], _p(out), _ld(out),
-                                       _p(row_order), flags, _stream()))
+                                       _p(_ord(A, row_order)), flags, _stream()))
     return out
 
 
@@ -337,7 +349,7 @@ def gcn_layer(A_norm: CSR, H: torch.Tensor, W: torch.Tensor, bias=None, act="rel
     b = _vec(bias)
     check(lib.tg_gcn_layer_f32(N, A_norm.nnz, _p(A_norm.row_ptr), _p(A_norm.col_ind), _p(A_norm.values), _p(H),
                                _ld(H), W.shape[0], F_out, _p(W), _p(b), ACT[act], _p(out), _ld(out),
-                               _p(row_order), MODE[mode], _stream()))
+                               _p(_ord(A_norm, row_order)), MODE[mode], _stream()))
     return out
 
 
@@ -352,7 +364,7 @@ def sage_layer(A: CSR, H: torch.Tensor, W_neigh: torch.Tensor, W_self: torch.Ten
     b = _vec(bias)
     check(lib.tg_sage_layer_f32(N, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(H), _ld(H), Wn.shape[0], F_out,
                                 _p(Wn), _p(Ws), _p(b), _lib.AGG_MAX if aggregator == "max" else _lib.AGG_MEAN,
-                                ACT[act], _p(out), _ld(out), _p(row_order), MODE[mode], _stream()))
+                                ACT[act], _p(out), _ld(out), _p(_ord(A, row_order)), MODE[mode], _stream()))
     return out
 
 
@@ -372,5 +384,5 @@ def gat_layer(A_sl: CSR, H: torch.Tensor, W: torch.Tensor, a_left: torch.Tensor,
         out = torch.empty((N, heads * F_out if concat else F_out), dtype=torch.float32, device=H.device)
     check(lib.tg_gat_layer_f32(N, A_sl.nnz, _p(A_sl.row_ptr), _p(A_sl.col_ind), _p(H), _ld(H), W.shape[0], heads,
                                F_out, _p(W), _p(al), _p(ar), _p(b), negative_slope, int(concat), ACT[act],
-                               _p(out), _ld(out), _p(row_order), _stream()))
+                               _p(out), _ld(out), _p(_ord(A_sl, row_order)), _stream()))
     return out
