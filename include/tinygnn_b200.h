@@ -95,8 +95,11 @@ TG_API uint64_t tg_kernel_launch_count(void);
 
 /* C[M,N] = A[M,K] . B[K,N]  (TinyGNN matmul, src/ops.cpp:70-162).
  * EXACT: every C[i][j] is one fused multiply-add chain over k = 0..K-1,
- * the reference's order -> bit-identical.  Optional epilogue: + bias[N]
- * (add_bias, src/ops.cpp:622) then activation `act` with parameter alpha. */
+ * the reference's order -> bit-identical.  FAST: tcgen05 tensor cores with
+ * a 3xTF32 split (within the fp32 tolerance) when lda % 4 == 0, A is
+ * 16-byte aligned and N <= 256; otherwise the EXACT kernel.  Optional
+ * epilogue: + bias[N] (add_bias, src/ops.cpp:622) then activation `act`
+ * with parameter alpha. */
 TG_API tg_status tg_gemm_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                              const float* B, int64_t ldb, float* C, int64_t ldc,
                              const float* bias, int32_t act, float alpha, int32_t mode,
@@ -269,7 +272,12 @@ TG_API tg_status tg_gat_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
                                   const float* a_left, const float* a_right, const float* bias,
                                   float negative_slope, int32_t concat, int32_t act,
                                   float* out, int64_t ldo, const int32_t* row_order,
-                                  void* stream);
+                                  int32_t mode, void* stream);
+
+/* Reads and clears the device error word of the tensor-core GEMM (FAST mode):
+ * TG_ERR_TIMEOUT when one of its bounded pipeline waits ran out since the
+ * last call (that GEMM's output is then invalid).  Synchronises `stream`. */
+TG_API tg_status tg_take_device_error(void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -165,6 +165,23 @@ def test_spmm_exact_vs_oracle(tg, F):
     assert_bits_equal(host(tg.spmm(A, dev(B), row_order=order)), ref, f"spmm F={F} degree order")
 
 
+@pytest.mark.parametrize("F", [16, 41, 128])
+def test_spmm_large_auto_schedule_vs_oracle(tg, F):
+    """Above 16,384 rows the library schedules longest rows first by itself."""
+    rng = np.random.default_rng(100 + F)
+    n = 40000
+    rp, ci, v = powerlaw_csr(rng, n, 24)
+    B = rng.standard_normal((n, F)).astype(np.float32)
+    A = csr(tg, rp, ci, v)
+    assert A.order is None
+    assert_bits_equal(host(tg.spmm(A, dev(B))), P.spmm(rp, ci, v, B), f"spmm auto-ordered F={F}")
+    H = rng.standard_normal((n, 12)).astype(np.float32)
+    W = (rng.standard_normal((12, F)) * 0.3).astype(np.float32)
+    An = P.gcn_norm(rp, ci, v)
+    assert_bits_equal(host(tg.gcn_layer(csr(tg, *An), dev(H), dev(W), None, "relu")),
+                      P.gcn_layer(*An, H, W, None, True), f"gcn auto-ordered F={F}")
+
+
 def test_spmm_epilogue_and_strides(tg):
     rng = np.random.default_rng(5)
     n, F = 1000, 41

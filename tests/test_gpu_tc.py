@@ -1,0 +1,100 @@
+"""The tcgen05 tensor-core GEMM (FAST mode, 3xTF32) against the exact oracle.
+
+Tolerance |d| <= 1e-5 + 1e-4 |ref| scaled by the row's magnitude: the
+3xTF32 product is within a few 1e-6 relative of fp32 per term, so the check
+is on |d| <= 1e-5 + 1e-4 * sum_k |a_ik||b_kj| (the magnitude the rounding
+acts on).  After every call the device error word must be clear.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+P = oracle.port
+
+
+@pytest.fixture(scope="module")
+def tg():
+    assert torch.cuda.is_available()
+    import tinygnn_b200
+    return tinygnn_b200
+
+
+def padded(a, mult=4):
+    """Device copy of a with the row stride rounded up (TMA needs 16-byte rows)."""
+    M, K = a.shape
+    ld = (K + mult - 1) // mult * mult
+    t = torch.zeros((M, ld), dtype=torch.float32, device="cuda")
+    t[:, :K] = torch.as_tensor(a).cuda()
+    return t[:, :K]
+
+
+def check(got, A, B, what, bias=None):
+    ref = P.matmul(A, B)
+    if bias is not None:
+        ref = P.add_bias(ref, bias)
+    mag = np.abs(A).astype(np.float64) @ np.abs(B).astype(np.float64)
+    err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+    bad = err > 1e-5 + 1e-4 * mag
+    assert not bad.any(), f"{what}: {bad.sum()} outside; max err {err.max():.3g}"
+    # and the plain elementwise tolerance on these well-conditioned inputs
+    rel = err / (1e-5 + 1e-4 * np.abs(ref))
+    return float(rel.max())
+
+
+@pytest.mark.parametrize("shape", [(128, 32, 16), (1, 8, 7), (130, 70, 41), (300, 602, 128), (257, 256, 64),
+                                   (1000, 128, 41), (4099, 602, 256), (64, 1433, 16), (513, 33, 48), (200, 4, 1)])
+def test_tc_gemm_vs_oracle(tg, shape):
+    M, K, N = shape
+    rng = np.random.default_rng(M * 7 + K + N)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = (rng.standard_normal((K, N)) / np.sqrt(K)).astype(np.float32)
+    out = tg.matmul(padded(A), torch.as_tensor(B).cuda(), mode="fast")
+    torch.cuda.synchronize()
+    tg.ops.take_device_error()
+    check(out.cpu().numpy(), A, B, f"tc {shape}")
+
+
+def test_tc_gemm_epilogue_and_strided_out(tg):
+    rng = np.random.default_rng(3)
+    A = rng.standard_normal((700, 602)).astype(np.float32)
+    B = (rng.standard_normal((602, 41)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(41).astype(np.float32)
+    Cw = torch.full((700, 48), 5.0, device="cuda")
+    tg.matmul(padded(A), torch.as_tensor(B).cuda(), bias=torch.as_tensor(b).cuda(), out=Cw[:, 2:43], mode="fast")
+    torch.cuda.synchronize()
+    tg.ops.take_device_error()
+    h = Cw.cpu().numpy()
+    check(h[:, 2:43], A, B, "tc bias", bias=b)
+    assert np.all(h[:, :2] == 5.0) and np.all(h[:, 43:] == 5.0)
+
+
+def test_fast_mode_falls_back_when_rows_are_not_16B(tg):
+    """lda % 4 != 0 cannot feed TMA: FAST mode then runs the exact kernel."""
+    rng = np.random.default_rng(4)
+    A = rng.standard_normal((100, 602)).astype(np.float32)   # contiguous: lda = 602
+    B = rng.standard_normal((602, 16)).astype(np.float32)
+    out = tg.matmul(torch.as_tensor(A).cuda(), torch.as_tensor(B).cuda(), mode="fast").cpu().numpy()
+    assert np.array_equal(out.view(np.uint32), P.matmul(A, B).view(np.uint32))
+
+
+def test_fast_layers_within_tolerance(tg):
+    from tests.helpers import assert_close, powerlaw_csr
+    rng = np.random.default_rng(5)
+    n = 5000
+    rp, ci, v = powerlaw_csr(rng, n, 12, weighted=False, diag=False)
+    H = rng.standard_normal((n, 96)).astype(np.float32)
+    W = (rng.standard_normal((96, 64)) * 0.1).astype(np.float32)
+    W2 = (rng.standard_normal((96, 64)) * 0.1).astype(np.float32)
+    b = rng.standard_normal(64).astype(np.float32) * 0.1
+    An = P.gcn_norm(rp, ci, v)
+    Hd = padded(H)
+    got = tg.gcn_layer(tg.CSR.from_numpy(*An), Hd, torch.as_tensor(W).cuda(), torch.as_tensor(b).cuda(), "relu",
+                       mode="fast")
+    assert_close(got.cpu().numpy(), P.gcn_layer(*An, H, W, b, True), "gcn fast")
+    got = tg.sage_layer(tg.CSR.from_numpy(rp, ci, v), Hd, torch.as_tensor(W).cuda(), torch.as_tensor(W2).cuda(),
+                        torch.as_tensor(b).cuda(), "mean", "relu", mode="fast")
+    assert_close(got.cpu().numpy(), P.sage_layer(rp, ci, v, H, W, W2, b, "mean", True), "sage fast")
+    tg.ops.take_device_error()

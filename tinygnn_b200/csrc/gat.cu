@@ -25,8 +25,8 @@
 
 namespace tg {
 
-void gemm_exact(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
-                float* C, int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s);
+void gemm(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
+          int64_t ldc, const float* bias, int act, float alpha, int mode, cudaStream_t s);
 void csr_degree_order(int64_t M, const int32_t* rp, int32_t* out, cudaStream_t s);
 
 namespace {
@@ -216,12 +216,13 @@ __global__ void head_average_kernel(int64_t N, int H, int d, const float* cat, i
 // Full multi-head layer.  W_all is F_in x (H*d); a_l, a_r, bias are H*d.
 void gat_layer(int64_t N, const int32_t* rp, const int32_t* ci, const float* Hf, int64_t ldh, int64_t F_in, int H,
                int d, const float* W_all, const float* al, const float* ar, const float* bias, float slope,
-               bool concat, int act, int post, float* out, int64_t ldo, const int32_t* order, cudaStream_t s) {
+               bool concat, int act, int post, float* out, int64_t ldo, const int32_t* order, int mode,
+               cudaStream_t s) {
     if (N == 0) return;
     const int64_t HD = static_cast<int64_t>(H) * d;
     const int64_t ldw = (HD + 3) / 4 * 4;
     Scratch<float> Wh(static_cast<size_t>(N * ldw), s);
-    gemm_exact(N, HD, F_in, Hf, ldh, W_all, HD, Wh.p, ldw, nullptr, TG_ACT_NONE, 0.0f, s);
+    gemm(N, HD, F_in, Hf, ldh, W_all, HD, Wh.p, ldw, nullptr, TG_ACT_NONE, 0.0f, mode, s);
     Scratch<float> sd(static_cast<size_t>(N * 2 * H), s);
     launch("gat_scores", gat_scores_kernel, dim3(static_cast<unsigned>(ceil_div(N * H, 256))), dim3(256), 0, s, N, H,
            d, static_cast<const float*>(Wh.p), ldw, al, ar, sd.p);

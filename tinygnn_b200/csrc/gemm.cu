@@ -182,6 +182,21 @@ void gemm_exact(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
     dispatch_gemm<false>(g, s);
 }
 
+bool gemm_tc_supported(int64_t N, int64_t K, const float* A, int64_t lda);
+int gemm_tc_take_error(cudaStream_t s);
+void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
+             int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s);
+
+// FAST: tensor cores (3xTF32) when the operands allow TMA; otherwise, and in
+// EXACT mode, the k-sequential FMA kernel.
+void gemm(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
+          int64_t ldc, const float* bias, int act, float alpha, int mode, cudaStream_t s) {
+    if ((mode & 0xff) == TG_MODE_FAST && gemm_tc_supported(N, K, A, lda))
+        gemm_tc(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, s);
+    else
+        gemm_exact(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, s);
+}
+
 void gemm_dual_exact(int64_t M, int64_t N, int64_t K, const float* A1, int64_t lda1,
                      const float* A2, int64_t lda2, const float* B1, const float* B2, int64_t ldb,
                      float* C, int64_t ldc, const float* bias, int act, float alpha,
@@ -210,8 +225,17 @@ TG_API tg_status tg_gemm_f32(int64_t M, int64_t N, int64_t K, const float* A, in
         check_ptr("matmul", "A", A, M > 0 && K > 0);
         check_ptr("matmul", "B", B, K > 0 && N > 0);
         check_ptr("matmul", "C", C, M > 0 && N > 0);
-        (void)mode;
-        gemm_exact(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, as_stream(stream));
+        gemm(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, mode, as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_take_device_error(void* stream) {
+    return guard([&] {
+        require_device();
+        const int code = gemm_tc_take_error(as_stream(stream));
+        if (code)
+            fail(TG_ERR_TIMEOUT, "a tensor-core GEMM pipeline wait ran out (stage code " + std::to_string(code) +
+                                     "); its output is invalid");
     });
 }
 

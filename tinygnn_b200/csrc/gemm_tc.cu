@@ -1,0 +1,377 @@
+// ============================================================================
+//  gemm_tc.cu -- C = A . B on the 5th-generation tensor cores (FAST mode).
+//
+//  fp32 inputs through tcgen05.mma kind::tf32 with the 3xTF32 split:
+//      A = Ah + Al,  Ah = round-to-nearest tf32(A),  Al = A - Ah (exact)
+//      A.B ~= Ah.Bh + Ah.Bl + Al.Bh      (fp32 accumulation in TMEM)
+//  which keeps the product within ~3e-6 relative of fp32 -- inside the
+//  1e-5 + 1e-4|ref| tolerance -- at tensor-core rate.  (Plain TF32 would
+//  miss it: a 10-bit mantissa over K = 602.)
+//
+//  One CTA owns a 128-row tile of C and all of its N (<= 256) columns:
+//    warp 0      TMA producer: A tile (128 x 32 fp32, 128B swizzle) and the
+//                pre-split B^T hi/lo tiles per k-block, into a 3-stage ring;
+//    warp 1      allocates TMEM and issues the MMAs (one thread);
+//    warps 2-5   split each A tile into Ah (in place) / Al in shared memory,
+//                then run the epilogue: TMEM -> registers, + bias,
+//                activation, store.
+//  Every mbarrier wait is bounded; a wait that runs out records a code in
+//  a device error word, the CTA drains its copies, frees TMEM and returns.
+//  A is read once from HBM (the tile's B^T comes from L2): the kernel is
+//  bound by max(A bytes / HBM BW, 3 * 2MNK / tf32 peak).
+//
+//  Requirements (else the caller uses the exact SIMT kernel): lda % 4 == 0
+//  and A 16-byte aligned (TMA row stride), N <= 256.
+// ============================================================================
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "launch.cuh"
+
+namespace tg {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;       // fp32 per 128-byte swizzled row
+constexpr long kWaitLimit = 1L << 24;  // ~1 s of polling with back-off
+
+// Pipeline depth from the per-stage footprint (A, Al, Bh, Bl) within ~200 KB.
+constexpr int stages_for(int BN) {
+    return (200 * 1024) / ((2 * BM * BK + 2 * BN * BK) * 4) > 4 ? 4 : (200 * 1024) / ((2 * BM * BK + 2 * BN * BK) * 4);
+}
+
+__device__ int g_tc_error = 0;  // first timeout code seen (0 = none)
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait; false (and the error word set) when it runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+    for (long i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if (i > 32) __nanosleep(64);
+    }
+    atomicCAS(&g_tc_error, 0, code);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 B,
+// 8-row groups 1024 B apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(const void* p) {
+    const uint32_t a = smem_u32(p);
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((a >> 4) & 0x3FFF);
+    d |= static_cast<uint64_t>(1) << 16;              // LBO (unused for swizzled K-major)
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;      // SBO
+    d |= static_cast<uint64_t>(1) << 46;              // version
+    d |= static_cast<uint64_t>(2) << 61;              // SWIZZLE_128B
+    return d;
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ float tf32_rn(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+template <int BN>
+struct TcSmem {
+    static constexpr int STAGES = stages_for(BN);
+    float A[STAGES][BM * BK];     // raw tile, split in place into Ah
+    float Al[STAGES][BM * BK];
+    float Bh[STAGES][BN * BK];
+    float Bl[STAGES][BN * BK];
+    uint64_t full[STAGES], split[STAGES], empty[STAGES], acc, drain;
+    uint32_t tmem;
+};
+
+struct TcArgs {
+    float* C;
+    int64_t ldc, M, N, K;
+    const float* bias;
+    int act;
+    float alpha;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                         const __grid_constant__ CUtensorMap tmBh,
+                                                         const __grid_constant__ CUtensorMap tmBl,
+                                                         const TcArgs g) {
+    extern __shared__ uint8_t raw[];
+    TcSmem<BN>& s = *reinterpret_cast<TcSmem<BN>*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    constexpr int STAGES = TcSmem<BN>::STAGES;
+    constexpr uint32_t TMEM_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+    constexpr uint32_t STAGE_BYTES = (BM * BK + 2 * BN * BK) * 4;
+    // tf32 x tf32 -> f32, K-major A and B, M = 128, N = BN.
+    constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.x) * BM;
+    const int KB = static_cast<int>((g.K + BK - 1) / BK);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.split[i], 128);
+            mbar_init(&s.empty[i], 1);
+        }
+        mbar_init(&s.acc, 1);
+        mbar_init(&s.drain, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = s.tmem;
+
+    if (warp == 0) {
+        // ── TMA producer ──
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int st = kb % STAGES;
+                const uint32_t ph = (kb / STAGES) & 1;
+                if (kb >= STAGES && !mbar_wait(&s.empty[st], ph ^ 1, 1)) break;
+                mbar_expect_tx(&s.full[st], STAGE_BYTES);
+                tma_load_2d(s.A[st], &tmA, kb * BK, static_cast<int>(m0), &s.full[st]);
+                tma_load_2d(s.Bh[st], &tmBh, kb * BK, 0, &s.full[st]);
+                tma_load_2d(s.Bl[st], &tmBl, kb * BK, 0, &s.full[st]);
+                ++issued;
+            }
+            // Every copy issued must have landed before the CTA may exit.
+            for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; ++kb)
+                mbar_wait(&s.full[kb % STAGES], (kb / STAGES) & 1, 2);
+        }
+    } else if (warp == 1) {
+        // ── MMA issuer ──
+        if (lane == 0) {
+            bool ok = true;
+            for (int kb = 0; kb < KB && ok; ++kb) {
+                const int st = kb % STAGES;
+                const uint32_t ph = (kb / STAGES) & 1;
+                if (!(ok = mbar_wait(&s.split[st], ph, 3))) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+                for (int k = 0; k < BK / 8; ++k) {  // K = 8 tf32 (32 bytes) per MMA
+                    const uint64_t ah = sw128_desc(s.A[st] + k * 8), al = sw128_desc(s.Al[st] + k * 8);
+                    const uint64_t bh = sw128_desc(s.Bh[st] + k * 8), bl = sw128_desc(s.Bl[st] + k * 8);
+                    mma_tf32(tmem, al, bh, IDESC, (kb | k) != 0);
+                    mma_tf32(tmem, ah, bl, IDESC, 1);
+                    mma_tf32(tmem, ah, bh, IDESC, 1);
+                }
+                mma_commit(&s.empty[st]);  // frees the stage once these MMAs have read it
+            }
+            mma_commit(&s.acc);            // accumulator complete (or: everything issued has retired)
+        }
+    } else {
+        // ── split (Ah in place, Al) then epilogue: 128 threads ──
+        const int t = threadIdx.x - 64;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+            const int st = kb % STAGES;
+            const uint32_t ph = (kb / STAGES) & 1;
+            if (!(ok = mbar_wait(&s.full[st], ph, 4))) break;
+            float4* a = reinterpret_cast<float4*>(s.A[st]);
+            float4* l = reinterpret_cast<float4*>(s.Al[st]);
+#pragma unroll 4
+            for (int i = t; i < BM * BK / 4; i += 128) {
+                const float4 x = a[i];
+                const float4 h = make_float4(tf32_rn(x.x), tf32_rn(x.y), tf32_rn(x.z), tf32_rn(x.w));
+                a[i] = h;
+                l[i] = make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z), __fsub_rn(x.w, h.w));
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+            mbar_arrive(&s.split[st]);
+        }
+        if (ok && mbar_wait(&s.acc, 0, 5)) {
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const int q = warp & 3;  // this warp's TMEM lane quarter
+            const int64_t row = m0 + q * 32 + lane;
+            const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                uint32_t r[16];
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+                    "%13, %14, %15}, [%16];"
+                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                      "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                      "=r"(r[15])
+                    : "r"(taddr + c0));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (row < g.M) {
+                    float* crow = g.C + row * g.ldc;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int64_t col = c0 + j;
+                        if (col < g.N) {
+                            float v = __uint_as_float(r[j]);
+                            if (g.bias) v = __fadd_rn(v, __ldg(g.bias + col));
+                            crow[col] = apply_act(g.act, v, g.alpha);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    // Teardown: all MMAs retired (the acc commit covers every earlier MMA),
+    // all copies landed (producer drain), then TMEM is returned.
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        if (lane == 0) {
+            mma_commit(&s.drain);
+            mbar_wait(&s.drain, 0, 6);
+        }
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
+// B (K x N, ld ldb) -> Bt_hi, Bt_lo (N x Kp, K-major), tf32 round-to-nearest split.
+__global__ void split_bt_kernel(const float* B, int64_t ldb, int64_t K, int64_t N, int64_t Kp, float* hi, float* lo) {
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= N * Kp) return;
+    const int64_t n = t / Kp, k = t % Kp;
+    const float x = k < K ? B[k * ldb + n] : 0.0f;
+    const float h = tf32_rn(x);
+    hi[t] = h;
+    lo[t] = __fsub_rn(x, h);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    });
+    if (!fn) fail(TG_ERR_CUDA, "gemm (tensor cores): cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
+CUtensorMap make_map(const float* base, int64_t inner, int64_t outer, int64_t row_stride_elems, uint32_t box_outer) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_elems) * 4};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides,
+                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(TG_ERR_CUDA, "gemm (tensor cores): tensor map encoding failed (" + std::to_string(r) + ")");
+    return m;
+}
+
+template <int BN>
+void launch_tc(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g, cudaStream_t s) {
+    const size_t smem = sizeof(TcSmem<BN>) + 1024;
+    TG_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    launch("gemm_tc", gemm_tc_kernel<BN>, dim3(static_cast<unsigned>(ceil_div(g.M, BM))), dim3(192), smem, s, a, bh, bl, g);
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int64_t N, int64_t K, const float* A, int64_t lda) {
+    return N >= 1 && N <= 256 && K >= 1 && lda % 4 == 0 && (reinterpret_cast<uintptr_t>(A) % 16) == 0;
+}
+
+void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
+             int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s) {
+    if (M == 0 || N == 0) return;
+    const int BN = N <= 16 ? 16 : N <= 32 ? 32 : N <= 48 ? 48 : N <= 64 ? 64 : N <= 128 ? 128 : 256;
+    const int64_t Kp = (K + 3) / 4 * 4;
+    Scratch<float> bt(static_cast<size_t>(2 * N * Kp), s);
+    launch("split_bt", split_bt_kernel, dim3(static_cast<unsigned>(ceil_div(N * Kp, 256))), dim3(256), 0, s, B, ldb, K,
+           N, Kp, bt.p, bt.p + N * Kp);
+    const CUtensorMap ma = make_map(A, K, M, lda, BM);
+    const CUtensorMap mh = make_map(bt.p, K, N, Kp, static_cast<uint32_t>(BN));
+    const CUtensorMap ml = make_map(bt.p + N * Kp, K, N, Kp, static_cast<uint32_t>(BN));
+    const TcArgs g{C, ldc, M, N, K, bias, act, alpha};
+    switch (BN) {
+        case 16: launch_tc<16>(ma, mh, ml, g, s); break;
+        case 32: launch_tc<32>(ma, mh, ml, g, s); break;
+        case 48: launch_tc<48>(ma, mh, ml, g, s); break;
+        case 64: launch_tc<64>(ma, mh, ml, g, s); break;
+        case 128: launch_tc<128>(ma, mh, ml, g, s); break;
+        default: launch_tc<256>(ma, mh, ml, g, s); break;
+    }
+}
+
+// Reads and clears the tensor-core kernels' error word (synchronises `s`).
+int gemm_tc_take_error(cudaStream_t s) {
+    int h = 0;
+    TG_CUDA(cudaStreamSynchronize(s));
+    TG_CUDA(cudaMemcpyFromSymbol(&h, g_tc_error, sizeof(int)));
+    if (h) {
+        const int zero = 0;
+        TG_CUDA(cudaMemcpyToSymbol(g_tc_error, &zero, sizeof(int)));
+    }
+    return h;
+}
+
+}  // namespace tg

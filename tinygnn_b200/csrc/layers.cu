@@ -1,12 +1,13 @@
 // ============================================================================
 //  layers.cu -- GCN / SAGE / GAT layer forwards composed from the kernels.
 //
-//  GCN  (src/layers.cpp:286-339): HW = H . W (exact GEMM into a row-padded
-//       scratch), then one gather pass out = act(A_norm . HW + b) with bias
-//       and activation in the epilogue.
+//  GCN  (src/layers.cpp:286-339): HW = H . W into a row-padded scratch
+//       (EXACT: k-sequential FMA GEMM, bit-identical; FAST: 3xTF32 tensor
+//       cores), then one gather pass out = act(A_norm . HW + b) with bias and
+//       activation in its epilogue.
 //  SAGE (src/layers.cpp:538-752): aggregate-first (mean/max gather into a
 //       scratch, then the interleaved dual product with bias + activation),
-//       bit-identical for mean; or, in FAST mode with F_in > F_out (mean),
+//       bit-identical; or, in FAST mode with F_in > F_out (mean),
 //       transform-first: T = H . [Wn | Ws], then one gather of the Wn half
 //       with the self half, bias and activation fused -- fewer bytes per edge.
 //  GAT  (src/layers.cpp:945-1129 + src/model.cpp:403-422): gat.cu.
@@ -16,24 +17,25 @@
 
 namespace tg {
 
-void gemm_exact(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
-                float* C, int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s);
+void gemm(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
+          int64_t ldc, const float* bias, int act, float alpha, int mode, cudaStream_t s);
 void gemm_dual_exact(int64_t M, int64_t N, int64_t K, const float* A1, int64_t lda1, const float* A2, int64_t lda2,
                      const float* B1, const float* B2, int64_t ldb, float* C, int64_t ldc, const float* bias, int act,
                      float alpha, cudaStream_t s);
 void gat_layer(int64_t N, const int32_t* rp, const int32_t* ci, const float* Hf, int64_t ldh, int64_t F_in, int H,
                int d, const float* W_all, const float* al, const float* ar, const float* bias, float slope,
-               bool concat, int act, int post, float* out, int64_t ldo, const int32_t* order, cudaStream_t s);
+               bool concat, int act, int post, float* out, int64_t ldo, const int32_t* order, int mode,
+               cudaStream_t s);
 
 inline int64_t pad4(int64_t n) { return (n + 3) / 4 * 4; }
 
 void gcn_layer(int64_t N, const int32_t* rp, const int32_t* ci, const float* v, const float* H, int64_t ldh,
                int64_t F_in, int64_t F_out, const float* W, const float* bias, int act, float* out, int64_t ldo,
-               const int32_t* order, cudaStream_t s) {
+               const int32_t* order, int mode, cudaStream_t s) {
     if (N == 0 || F_out == 0) return;
     const int64_t ldw = pad4(F_out);
     Scratch<float> HW(static_cast<size_t>(N * ldw), s);
-    gemm_exact(N, F_out, F_in, H, ldh, W, F_out, HW.p, ldw, nullptr, TG_ACT_NONE, 0.0f, s);
+    gemm(N, F_out, F_in, H, ldh, W, F_out, HW.p, ldw, nullptr, TG_ACT_NONE, 0.0f, mode, s);
     GatherArgs a;
     a.M = N; a.rp = rp; a.ci = ci; a.val = v; a.order = order;
     a.B = HW.p; a.ldb = ldw; a.b_padded = true; a.F = F_out;
@@ -45,7 +47,8 @@ void sage_layer(int64_t N, const int32_t* rp, const int32_t* ci, const float* H,
                 int64_t F_out, const float* Wn, const float* Ws, const float* bias, int agg, int act, float* out,
                 int64_t ldo, const int32_t* order, int mode, cudaStream_t s) {
     if (N == 0 || F_out == 0) return;
-    const bool transform_first = (mode == TG_MODE_FAST) && (agg == TG_AGG_MEAN) && (F_in > F_out);
+    const bool fast = (mode & 0xff) == TG_MODE_FAST;
+    const bool transform_first = fast && (agg == TG_AGG_MEAN) && (F_in > F_out);
     if (!transform_first) {
         const int64_t lda = pad4(F_in);
         Scratch<float> A(static_cast<size_t>(N * lda), s);
@@ -58,26 +61,17 @@ void sage_layer(int64_t N, const int32_t* rp, const int32_t* ci, const float* H,
         gemm_dual_exact(N, F_out, F_in, A.p, lda, H, ldh, Wn, Ws, F_out, out, ldo, bias, act, 0.0f, s);
         return;
     }
-    // Transform first: T = H . [Wn | Ws]  (N x 2F_out), then
-    // out_i = act(mean_j T[j, :F_out] + T[i, F_out:] + b).
-    const int64_t F2 = 2 * F_out;
-    Scratch<float> Wcat(static_cast<size_t>(F_in * F2), s);
-    TG_CUDA(cudaMemcpy2DAsync(Wcat.p, F2 * sizeof(float), Wn, F_out * sizeof(float), F_out * sizeof(float), F_in,
-                              cudaMemcpyDeviceToDevice, s));
-    TG_CUDA(cudaMemcpy2DAsync(Wcat.p + F_out, F2 * sizeof(float), Ws, F_out * sizeof(float), F_out * sizeof(float),
-                              F_in, cudaMemcpyDeviceToDevice, s));
-    const int64_t ldt = pad4(F_out) * 2;  // neighbour half at 0, self half at pad4(F_out)
+    // Transform first: Tn = H . Wn and Ts = H . Ws (side by side in one
+    // padded buffer), then out_i = act(mean_j Tn[j] + Ts[i] + b).
+    const int64_t half = pad4(F_out);
+    const int64_t ldt = 2 * half;
     Scratch<float> T(static_cast<size_t>(N * ldt), s);
-    if (pad4(F_out) == F_out) {
-        gemm_exact(N, F2, F_in, H, ldh, Wcat.p, F2, T.p, ldt, nullptr, TG_ACT_NONE, 0.0f, s);
-    } else {
-        gemm_exact(N, F_out, F_in, H, ldh, Wn, F_out, T.p, ldt, nullptr, TG_ACT_NONE, 0.0f, s);
-        gemm_exact(N, F_out, F_in, H, ldh, Ws, F_out, T.p + pad4(F_out), ldt, nullptr, TG_ACT_NONE, 0.0f, s);
-    }
+    gemm(N, F_out, F_in, H, ldh, Wn, F_out, T.p, ldt, nullptr, TG_ACT_NONE, 0.0f, mode, s);
+    gemm(N, F_out, F_in, H, ldh, Ws, F_out, T.p + half, ldt, nullptr, TG_ACT_NONE, 0.0f, mode, s);
     GatherArgs a;
     a.M = N; a.rp = rp; a.ci = ci; a.order = order;
     a.B = T.p; a.ldb = ldt; a.b_padded = true; a.F = F_out;
-    a.self = T.p + pad4(F_out); a.lds = ldt;
+    a.self = T.p + half; a.lds = ldt;
     a.C = out; a.ldc = ldo; a.bias = bias; a.act = act; a.op = GATHER_SUM; a.mean = 1;
     gather_rows(a, s);
 }
@@ -94,12 +88,12 @@ TG_API tg_status tg_gcn_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
                                   const int32_t* row_order, int32_t mode, void* stream) {
     return guard([&] {
         require_device();
-        (void)nnz; (void)mode;
+        (void)nnz;
         if (F_in <= 0) invalid("GCNLayer: in_features must be > 0.");
         if (F_out <= 0) invalid("GCNLayer: out_features must be > 0.");
         check_ld("GCNLayer::forward", "H", ldh, F_in);
         check_ld("GCNLayer::forward", "out", ldo, F_out);
-        gcn_layer(N, row_ptr, col_ind, values, H, ldh, F_in, F_out, W, bias, act, out, ldo, row_order,
+        gcn_layer(N, row_ptr, col_ind, values, H, ldh, F_in, F_out, W, bias, act, out, ldo, row_order, mode,
                   as_stream(stream));
     });
 }
@@ -124,7 +118,7 @@ TG_API tg_status tg_gat_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
                                   const float* H, int64_t ldh, int64_t F_in, int64_t heads, int64_t F_out,
                                   const float* W, const float* a_left, const float* a_right, const float* bias,
                                   float negative_slope, int32_t concat, int32_t act, float* out, int64_t ldo,
-                                  const int32_t* row_order, void* stream) {
+                                  const int32_t* row_order, int32_t mode, void* stream) {
     return guard([&] {
         require_device();
         (void)nnz;
@@ -134,7 +128,7 @@ TG_API tg_status tg_gat_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
         check_ld("GATLayer::forward", "H", ldh, F_in);
         check_ld("GATLayer::forward", "out", ldo, concat ? heads * F_out : F_out);
         gat_layer(N, row_ptr, col_ind, H, ldh, F_in, static_cast<int>(heads), static_cast<int>(F_out), W, a_left,
-                  a_right, bias, negative_slope, concat != 0, act, TG_ACT_NONE, out, ldo, row_order,
+                  a_right, bias, negative_slope, concat != 0, act, TG_ACT_NONE, out, ldo, row_order, mode,
                   as_stream(stream));
     });
 }

@@ -370,7 +370,7 @@ def sage_layer(A: CSR, H: torch.Tensor, W_neigh: torch.Tensor, W_self: torch.Ten
 
 def gat_layer(A_sl: CSR, H: torch.Tensor, W: torch.Tensor, a_left: torch.Tensor, a_right: torch.Tensor,
               heads: int = 1, bias=None, negative_slope: float = 0.2, concat: bool = True, act=None,
-              row_order=None, out=None) -> torch.Tensor:
+              row_order=None, out=None, mode: str = "exact") -> torch.Tensor:
     """Multi-head GATLayer::forward + head concat/average (src/layers.cpp:945, src/model.cpp:403).
 
     W is F_in x (heads*F_out) with head h in columns [h*F_out, (h+1)*F_out);
@@ -384,5 +384,10 @@ def gat_layer(A_sl: CSR, H: torch.Tensor, W: torch.Tensor, a_left: torch.Tensor,
         out = torch.empty((N, heads * F_out if concat else F_out), dtype=torch.float32, device=H.device)
     check(lib.tg_gat_layer_f32(N, A_sl.nnz, _p(A_sl.row_ptr), _p(A_sl.col_ind), _p(H), _ld(H), W.shape[0], heads,
                                F_out, _p(W), _p(al), _p(ar), _p(b), negative_slope, int(concat), ACT[act],
-                               _p(out), _ld(out), _p(_ord(A_sl, row_order)), _stream()))
+                               _p(out), _ld(out), _p(_ord(A_sl, row_order)), MODE[mode], _stream()))
     return out
+
+
+def take_device_error() -> None:
+    """Raise if a tensor-core GEMM pipeline wait timed out since the last call."""
+    check(lib.tg_take_device_error(_stream()))
