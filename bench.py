@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["gcn", "sage"], default="gcn")
+    ap.add_argument("--mode", choices=["fast", "exact"], default="fast",
+                    help="fast: 3xTF32 tensor-core GEMMs (within fp32 tolerance); exact: bit-identical GEMMs")
     ap.add_argument("--small", action="store_true", help="a 20k-node graph (quick functional run)")
     ap.add_argument("--edges", type=int, default=0, help="override the edge count (profiling on a smaller graph)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -301,7 +303,9 @@ def config_dict(args, n, nnz):
             "partition": "1-D equal row blocks, NCCL all-gather of each layer's transformed rows",
             "parallelism": f"row-partition x{args.gpus}",
             "l2": "inputs larger than L2 (CSR 918 MB, features 561 MB); no flush between steps",
-            "mode": "exact (bit-identical GEMM + SpMM)" if args.workload == "gcn" else "fast (transform-first)"}
+            "mode": ("fast: 3xTF32 tcgen05 GEMMs, order-preserving fp32 gathers" if args.mode == "fast"
+                     else "exact: bit-identical FMA-chain GEMMs and gathers") +
+                    ("" if args.workload == "gcn" else "; SAGE transform-first")}
 
 
 # ── our arm ──────────────────────────────────────────────────────────────────
@@ -326,9 +330,13 @@ def run_ours(args):
     R, r0, r1 = row_block(n, world, rank)
     rows = r1 - r0
     A_raw = slice_rows(rp, ci, v, r0, r1, n)
-    X = synth.normal_rows(r0, rows, FEATS, FEAT_SEED, 0, dev)
+    # Feature rows live at a 16-byte row stride (602 -> 604 floats) so the
+    # tensor-core GEMM can read them with TMA; the view is 602 wide.
+    Xp = torch.zeros((rows, (FEATS + 3) // 4 * 4), dtype=torch.float32, device=dev)
+    Xp[:, :FEATS] = synth.normal_rows(r0, rows, FEATS, FEAT_SEED, 0, dev)
+    X = Xp[:, :FEATS]
     w = make_weights(args.workload, dev)
-    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev)
+    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode)
     A_gcn = gcn_norm_rows(A_raw, r0, R, comm) if args.workload == "gcn" else None
     # The cached normalised graph keeps its longest-rows-first schedule (the
     # e2e path computes one per call inside the library).
@@ -347,13 +355,12 @@ def run_ours(args):
     torch.cuda.synchronize()
 
     # roofline hook: CUDA events around the layer-1 gather of every step
-    ev = []
+    ev = {}  # (layer, phase) -> [start, end, start, end, ...] events
 
     def hook(li, what, edge):
-        if li == 0 and what == "gather":
-            e = torch.cuda.Event(enable_timing=True)
-            e.record()
-            ev.append(e)
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        ev.setdefault((li, what), []).append(e)
 
     def step():
         model.forward(A_gcn, A_raw, X)
@@ -365,8 +372,13 @@ def run_ours(args):
     ms = time_steps(step, args.steps, args.warmup, world)
     model.timing = None
     launches = tg.launches() - launches0
-    pairs = list(zip(ev[0::2], ev[1::2]))[-args.steps:]
-    gather_ms = statistics.mean(a.elapsed_time(b) for a, b in pairs)
+    def phase_ms(key):
+        evs = ev.get(key, [])
+        pairs = list(zip(evs[0::2], evs[1::2]))[-args.steps:]
+        return statistics.mean(a.elapsed_time(b) for a, b in pairs) if pairs else None
+
+    gather_ms = phase_ms((0, "gather"))
+    phases = {f"layer{li}_{what}": phase_ms((li, what)) for li in range(2) for what in ("gemm", "gather")}
     per_launch = launches / (args.steps + args.warmup)
 
     # e2e: host inputs -> device -> gcn_norm -> forward -> logits to host
@@ -374,7 +386,7 @@ def run_ours(args):
     h_rp, h_ci, h_v, h_X = pin(A_raw.row_ptr), pin(A_raw.col_ind), pin(A_raw.values), pin(X)
     h_out = torch.empty((rows, CLASSES), dtype=torch.float32).pin_memory()
     d_rp, d_ci, d_v = torch.empty_like(A_raw.row_ptr), torch.empty_like(A_raw.col_ind), torch.empty_like(A_raw.values)
-    d_X = torch.empty_like(X)
+    d_X = torch.zeros_like(Xp)[:, :FEATS]
     dis_all = torch.zeros(R * world, dtype=torch.float32, device=dev)
 
     def e2e_step():
@@ -444,6 +456,7 @@ def run_ours(args):
                     "logits_match_resident_run": e2e_matches,
                     "note": "rank 0's bytes; every rank moves its own row block"},
             "clocks": clocks, "gpu_launches": int(per_launch * args.steps),
+            "phase_ms": phases,
         }
         print(json.dumps(line))
     if world > 1:

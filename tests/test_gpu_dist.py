@@ -1,0 +1,132 @@
+"""The row-partitioned GCN / SAGE path on one GPU, P ranks emulated in lockstep.
+
+Each emulated rank is a tinygnn_b200.dist.ShardedModel over its own row
+block; the all-gather between the transform and aggregate phases is
+emulated by copying every shard's block into every shard's gather buffer
+(the layout NCCL's all_gather_into_tensor produces).  Results must equal the
+unpartitioned forward bit for bit (exact mode), and the row-block gcn_norm
+must equal the rows of the global gcn_norm.  The real NCCL path runs under
+torchrun in tests/test_gpu_dist_nccl.py when several GPUs are visible.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.helpers import assert_bits_equal, assert_close, powerlaw_csr
+
+pytestmark = pytest.mark.gpu
+P = oracle.port
+
+
+@pytest.fixture(scope="module")
+def tg():
+    assert torch.cuda.is_available()
+    import tinygnn_b200
+    return tinygnn_b200
+
+
+class LocalComm:
+    """Comm stand-in for one shard when the exchange is done by the test."""
+
+    def __init__(self, world, rank):
+        self.world, self.rank, self.group = world, rank, None
+
+    def all_gather_rows(self, full, R):
+        pass
+
+
+def _graph(n=30000, seed=1):
+    rng = np.random.default_rng(seed)
+    rp, ci, v = powerlaw_csr(rng, n, 14, weighted=False, diag=False)
+    X = rng.standard_normal((n, 40)).astype(np.float32)
+    return rng, rp, ci, v, X
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_row_block_gcn_norm_matches_global(tg, world):
+    from tinygnn_b200.dist import row_block, slice_rows
+    rng, rp, ci, v, X = _graph()
+    n = rp.size - 1
+    A = tg.CSR.from_numpy(rp, ci, v)
+    G = P.gcn_norm(rp, ci, v)
+    R = (n + world - 1) // world
+    dis_all = torch.zeros(R * world, device="cuda")
+    blocks = []
+    for r in range(world):  # phase 1: local self-loops + degrees
+        _, r0, r1 = row_block(n, world, r)
+        Ar = slice_rows(A.row_ptr, A.col_ind, A.values, r0, r1, n)
+        asl = tg.ops.add_self_loops_rows(Ar, r0)
+        tg.ops.degree_inv_sqrt(asl, out=dis_all[r * R:r * R + (r1 - r0)])
+        blocks.append((r0, r1, asl))
+    for r, (r0, r1, asl) in enumerate(blocks):  # phase 2: scale with every rank's 1/sqrt(deg)
+        tg.ops.scale_sym_(asl, dis_all[r * R:r * R + (r1 - r0)], dis_all)
+        a, b = G[0][r0], G[0][r1]
+        assert_bits_equal(asl.row_ptr.cpu().numpy(), (G[0][r0:r1 + 1] - a).astype(np.int32), "row_ptr")
+        assert_bits_equal(asl.col_ind.cpu().numpy(), G[1][a:b], "col_ind")
+        assert_bits_equal(asl.values.cpu().numpy(), G[2][a:b], "values")
+
+
+@pytest.mark.parametrize("workload,world", [("gcn", 2), ("gcn", 4), ("sage", 3), ("gcn", 8)])
+def test_sharded_forward_equals_unpartitioned(tg, workload, world):
+    from tinygnn_b200.dist import Layer, ShardedModel, gcn_norm_rows, row_block, slice_rows
+    rng, rp, ci, v, X = _graph(seed=world)
+    n = rp.size - 1
+    W0 = torch.as_tensor((rng.standard_normal((40, 32)) * 0.2).astype(np.float32)).cuda()
+    W1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
+    S0 = torch.as_tensor((rng.standard_normal((40, 32)) * 0.2).astype(np.float32)).cuda()
+    S1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
+    b0 = torch.as_tensor((rng.standard_normal(32) * 0.1).astype(np.float32)).cuda()
+    b1 = torch.as_tensor((rng.standard_normal(11) * 0.1).astype(np.float32)).cuda()
+    kind = workload
+    layers = [Layer(kind, W0, b0, "relu", S0 if kind == "sage" else None),
+              Layer(kind, W1, b1, None, S1 if kind == "sage" else None)]
+    A = tg.CSR.from_numpy(rp, ci, v)
+    Xd = torch.as_tensor(X).cuda()
+
+    # reference: one shard holding everything
+    one = ShardedModel(layers, n, LocalComm(1, 0), "cuda")
+    from tinygnn_b200.dist import Comm
+    An_full = gcn_norm_rows(A, 0, n, Comm(1, 0)) if kind == "gcn" else None
+    ref = one.forward(An_full, A, Xd).clone()
+
+    shards, graphs, H = [], [], []
+    R = (n + world - 1) // world
+    dis_all = torch.zeros(R * world, device="cuda")
+    for r in range(world):
+        _, r0, r1 = row_block(n, world, r)
+        Ar = slice_rows(A.row_ptr, A.col_ind, A.values, r0, r1, n)
+        shards.append(ShardedModel(layers, n, LocalComm(world, r), "cuda"))
+        graphs.append([r0, r1, Ar, None])
+        H.append(Xd[r0:r1])
+    if kind == "gcn":
+        asls = []
+        for r, (r0, r1, Ar, _) in enumerate(graphs):
+            asl = tg.ops.add_self_loops_rows(Ar, r0)
+            tg.ops.degree_inv_sqrt(asl, out=dis_all[r * R:r * R + (r1 - r0)])
+            asls.append(asl)
+        for r, asl in enumerate(asls):
+            r0, r1 = graphs[r][0], graphs[r][1]
+            graphs[r][3] = tg.ops.scale_sym_(asl, dis_all[r * R:r * R + (r1 - r0)], dis_all)
+    for li in range(2):
+        for r, sh in enumerate(shards):
+            sh.transform(li, H[r])
+        for r, sh in enumerate(shards):  # emulated all-gather
+            for q, src in enumerate(shards):
+                if q != r:
+                    sh.full[li][q * R:(q + 1) * R] = src.full[li][q * R:(q + 1) * R]
+        H = [sh.aggregate(li, graphs[r][3], graphs[r][2]) for r, sh in enumerate(shards)]
+    got = torch.cat([tg.log_softmax_(h) for h in H], 0)
+    torch.cuda.synchronize()
+    if kind == "gcn":
+        assert_bits_equal(got.cpu().numpy(), ref.cpu().numpy(), f"{kind} x{world}")
+    else:
+        assert_close(got.cpu().numpy(), ref.cpu().numpy(), f"{kind} x{world}")
+    # and the unpartitioned forward itself against the oracle
+    spec = [dict(type=kind, **{"in": 40, "out": 32}, act="relu"), dict(type=kind, **{"in": 32, "out": 11})]
+    w = ({"layer0.weight": W0, "layer0.bias": b0, "layer1.weight": W1, "layer1.bias": b1} if kind == "gcn" else
+         {"layer0.weight_neigh": W0, "layer0.weight_self": S0, "layer0.bias": b0,
+          "layer1.weight_neigh": W1, "layer1.weight_self": S1, "layer1.bias": b1})
+    w = {k: t.cpu().numpy() for k, t in w.items()}
+    oref = P.activation("log_softmax", oracle.model_forward(P, spec, w, rp, ci, v, X))
+    assert_close(ref.cpu().numpy(), oref, f"{kind} vs oracle")

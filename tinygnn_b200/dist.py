@@ -93,8 +93,8 @@ class ShardedModel:
     rows and feature rows, already in HBM; buffers are allocated once.
     """
 
-    def __init__(self, layers: List[Layer], n: int, comm: Comm, device):
-        self.layers, self.n, self.comm, self.device = layers, n, comm, device
+    def __init__(self, layers: List[Layer], n: int, comm: Comm, device, mode: str = "exact"):
+        self.layers, self.n, self.comm, self.device, self.mode = layers, n, comm, device, mode
         self.R, self.row0, self.row1 = row_block(n, comm.world, comm.rank)
         self.rows = self.row1 - self.row0
         P = comm.world
@@ -121,9 +121,9 @@ class ShardedModel:
         fo = L.W.shape[1]
         r = self.comm.rank
         self._mark(li, "gemm", "start")
-        ops.matmul(H, L.W, out=self.full[li][r * self.R:r * self.R + self.rows, :fo])
+        ops.matmul(H, L.W, out=self.full[li][r * self.R:r * self.R + self.rows, :fo], mode=self.mode)
         if L.kind == "sage":
-            ops.matmul(H, L.W_self, out=self.selfs[li][:, :fo])
+            ops.matmul(H, L.W_self, out=self.selfs[li][:, :fo], mode=self.mode)
         self._mark(li, "gemm", "end")
 
     def exchange(self, li: int) -> None:
