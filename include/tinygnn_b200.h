@@ -247,6 +247,26 @@ TG_API tg_status tg_gcn_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
                                   const float* bias, int32_t act, float* out, int64_t ldo,
                                   const int32_t* row_order, int32_t mode, void* stream);
 
+/* No counterpart in the reference: tg_gcn_layer_f32 for callers that cannot
+ * let the library allocate device memory (serving loops that must not call
+ * cudaMalloc after start-up, runtimes that own all device memory).  Same
+ * arguments and bit-identical results as tg_gcn_layer_f32 in TG_MODE_EXACT,
+ * but the N x F_out intermediate H.W lives in a fixed array inside the
+ * library (TG_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits),
+ * so it allocates nothing: N * round_up(F_out, 4) * 4 bytes must fit, larger
+ * layers return TG_ERR_INVALID_ARGUMENT.  Rows run in the caller's
+ * row_order, or in natural order when it is NULL (no schedule is computed).
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the one array: calls whose work overlaps on the GPU (other
+ * streams, other threads) race on it and must be serialised by the caller. */
+#define TG_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+TG_API tg_status tg_gcn_layer_noalloc_f32(int64_t N, int64_t nnz, const int32_t* row_ptr,
+                                          const int32_t* col_ind, const float* values,
+                                          const float* H, int64_t ldh, int64_t F_in, int64_t F_out,
+                                          const float* W, const float* bias, int32_t act, float* out,
+                                          int64_t ldo, const int32_t* row_order, void* stream);
+
 /* SAGELayer::forward (src/layers.cpp:538-752) on the raw adjacency (no
  * self-loops): out = act(AGG_j H[j] . Wn + H[i] . Ws + b).  EXACT computes
  * the aggregate first and the interleaved dual product (bit-identical for

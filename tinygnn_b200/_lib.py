@@ -61,6 +61,7 @@ SIGNATURES = {
     "tg_gat_layer_f32": (i32, [i64, i64, vp, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp, f32, i32, i32, vp, i64,
                                vp, i32, vp]),
     "tg_take_device_error": (i32, [vp]),
+    "tg_gcn_layer_noalloc_f32": (i32, [i64, i64, vp, vp, vp, vp, i64, i64, i64, vp, vp, i32, vp, i64, vp, vp]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():

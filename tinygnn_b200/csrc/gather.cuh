@@ -39,6 +39,9 @@ struct GatherArgs {
     // B's rows are readable up to ldb (an internal buffer of K*ldb floats):
     // lets the kernel use vectors wider than F's divisibility allows.
     bool b_padded = false;
+    // Without `order`, large launches compute a longest-rows-first schedule
+    // in pool memory; false keeps the natural row order and allocates nothing.
+    bool allow_auto_order = true;
 };
 
 // Queues the gather on `s`.

@@ -1,0 +1,98 @@
+// ============================================================================
+//  noalloc.cu -- a GCN layer forward that allocates no device memory.
+//
+//  Some callers cannot let a library allocate: real-time serving loops that
+//  must not call cudaMalloc/cudaMallocAsync after start-up (an allocation can
+//  block on the driver and break the latency budget), and host runtimes that
+//  own all device memory through their own allocator and forbid
+//  library-side allocations.  tg_gcn_layer_f32 needs an N x F_out scratch
+//  for H.W (taken from the stream-ordered pool); this variant keeps that
+//  intermediate in a fixed array in the library's own device memory instead.
+//
+//  The array is a file-scope __device__ variable of TG_NOALLOC_SCRATCH_BYTES
+//  (16 MiB).  Every GPU that loads the library holds it until the process
+//  exits.  Host code cannot use the variable's name as a device address (in
+//  host code it names a host-side stand-in), so each device's address is
+//  looked up once with cudaGetSymbolAddress, with that device current, on
+//  the first call made on that device.
+// ============================================================================
+#include <mutex>
+#include <vector>
+
+#include "gather.cuh"
+#include "launch.cuh"
+
+namespace tg {
+
+void gemm_exact(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
+                float* C, int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s);
+
+namespace {
+
+static __device__ __align__(256) float g_noalloc_scratch[TG_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+std::mutex g_mu;
+std::vector<float*> g_addr;  // per device; nullptr = not looked up yet
+
+// The scratch array's device address on the current device.
+float* scratch_address() {
+    int dev = 0;
+    TG_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (static_cast<int>(g_addr.size()) <= dev) g_addr.resize(dev + 1, nullptr);
+    if (!g_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            fail(TG_ERR_CUDA, std::string("gcn_layer (no-alloc): cudaGetSymbolAddress failed: ") +
+                                  cudaGetErrorString(e));
+        }
+        g_addr[dev] = static_cast<float*>(p);
+    }
+    return g_addr[dev];
+}
+
+}  // namespace
+
+}  // namespace tg
+
+using namespace tg;
+
+extern "C" {
+
+TG_API tg_status tg_gcn_layer_noalloc_f32(int64_t N, int64_t nnz, const int32_t* row_ptr, const int32_t* col_ind,
+                                          const float* values, const float* H, int64_t ldh, int64_t F_in,
+                                          int64_t F_out, const float* W, const float* bias, int32_t act, float* out,
+                                          int64_t ldo, const int32_t* row_order, void* stream) {
+    return guard([&] {
+        require_device();
+        (void)nnz;
+        if (F_in <= 0) invalid("GCNLayer: in_features must be > 0.");
+        if (F_out <= 0) invalid("GCNLayer: out_features must be > 0.");
+        if (N < 0) invalid("GCNLayer::forward: negative node count");
+        check_ld("GCNLayer::forward", "H", ldh, F_in);
+        check_ld("GCNLayer::forward", "out", ldo, F_out);
+        const int64_t ldw = (F_out + 3) / 4 * 4;
+        const int64_t need = N * ldw * static_cast<int64_t>(sizeof(float));
+        if (need > static_cast<int64_t>(TG_NOALLOC_SCRATCH_BYTES))
+            invalid("gcn_layer (no-alloc): N x F_out = " + std::to_string(N) + " x " + std::to_string(F_out) +
+                    " needs " + std::to_string(need) + " bytes of scratch; the fixed scratch holds " +
+                    std::to_string(static_cast<long long>(TG_NOALLOC_SCRATCH_BYTES)) +
+                    " (use tg_gcn_layer_f32, which allocates)");
+        if (N == 0) return;
+        const cudaStream_t s = as_stream(stream);
+        float* HW = scratch_address();
+        // Every element the gather reads is written by this GEMM first, so
+        // nothing carried over from an earlier call needs clearing.
+        gemm_exact(N, F_out, F_in, H, ldh, W, F_out, HW, ldw, nullptr, TG_ACT_NONE, 0.0f, s);
+        GatherArgs a;
+        a.M = N; a.rp = row_ptr; a.ci = col_ind; a.val = values; a.order = row_order;
+        a.B = HW; a.ldb = ldw; a.b_padded = true; a.F = F_out;
+        a.C = out; a.ldc = ldo; a.bias = bias; a.act = act; a.op = GATHER_SUM;
+        a.allow_auto_order = false;  // a schedule would need pool memory
+        gather_rows(a, s);
+    });
+}
+
+}  // extern "C"

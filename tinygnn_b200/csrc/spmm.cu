@@ -75,7 +75,7 @@ void gather_rows(const GatherArgs& args, cudaStream_t s) {
     // rows first: a hub row left to the end of the grid is a serial tail
     // (measured 5.8 -> 3.7 ms on the Reddit-shaped layer-1 gather).
     std::unique_ptr<Scratch<int32_t>> order;
-    if (!a.order && a.M >= kAutoOrderRows) {
+    if (!a.order && a.allow_auto_order && a.M >= kAutoOrderRows) {
         order.reset(new Scratch<int32_t>(static_cast<size_t>(a.M), s));
         csr_degree_order(a.M, a.rp, order->p, s);
         a.order = order->p;
