@@ -1,0 +1,61 @@
+"""Worker for tests/test_gpu_dist_nccl.py, run under torchrun (one process per GPU).
+
+Builds the same seeded graph on every rank, runs the row-partitioned GCN
+forward over NCCL (tinygnn_b200.dist), gathers the logits on rank 0 and
+compares them with the single-GPU forward of the whole graph (bit-identical
+in exact mode).  Exit code 0 = pass.
+"""
+import datetime
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def main() -> int:
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    import tinygnn_b200 as tg
+    from tinygnn_b200 import synth
+    from tinygnn_b200.dist import Comm, Layer, ShardedModel, gcn_norm_rows, row_block, slice_rows
+
+    n, rp, ci, v = synth.chung_lu_csr(50000, 3_000_000, 5, device=dev)
+    X = synth.normal_rows(0, n, 64, 6, 0, dev)
+    W0, W1 = synth.glorot(64, 32, 7, 1, dev), synth.glorot(32, 9, 7, 2, dev)
+    b0 = torch.zeros(32, device=dev)
+    b1 = torch.full((9,), 0.1, device=dev)
+    layers = [Layer("gcn", W0, b0, "relu"), Layer("gcn", W1, b1, None)]
+    comm = Comm(world, rank)
+    R, r0, r1 = row_block(n, world, rank)
+    A = slice_rows(rp, ci, v, r0, r1, n)
+    An = gcn_norm_rows(A, r0, R, comm)
+    model = ShardedModel(layers, n, comm, dev, mode="exact")
+    out = model.forward(An, A, X[r0:r1].contiguous())
+    parts = [torch.zeros((R, 9), device=dev) for _ in range(world)]
+    mine = torch.zeros((R, 9), device=dev)
+    mine[:r1 - r0] = out
+    dist.all_gather(parts, mine)
+    ok = True
+    if rank == 0:
+        got = torch.cat(parts, 0)[:n]
+        full = tg.CSR(n, n, rp, ci, v)
+        one = ShardedModel(layers, n, Comm(1, 0), dev, mode="exact")
+        ref = one.forward(gcn_norm_rows(full, 0, n, Comm(1, 0)), full, X)
+        ok = bool(torch.equal(got, ref))
+        print(f"world={world} bit-identical={ok}", flush=True)
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.broadcast(flag, 0)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0 if int(flag.item()) == 1 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
