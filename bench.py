@@ -59,6 +59,8 @@ def parse():
                     help="fast: 3xTF32 tensor-core GEMMs (within fp32 tolerance); exact: bit-identical GEMMs")
     ap.add_argument("--small", action="store_true", help="a 20k-node graph (quick functional run)")
     ap.add_argument("--edges", type=int, default=0, help="override the edge count (profiling on a smaller graph)")
+    ap.add_argument("--blocks-per-rank", type=int, default=1,
+                    help="column blocks per rank for the gathers (passes with smaller working sets)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
@@ -319,6 +321,8 @@ def run_ours(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
+        # rank 0's stdout carries exactly one JSON line: NCCL's own messages go to stderr
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
 
     import tinygnn_b200 as tg
@@ -327,7 +331,7 @@ def run_ours(args):
 
     comm = Comm(world, rank, group)
     n, rp, ci, v = make_graph(args.small, dev, args.edges)
-    R, r0, r1 = row_block(n, world, rank)
+    R, r0, r1 = row_block(n, world, rank, args.blocks_per_rank)
     rows = r1 - r0
     A_raw = slice_rows(rp, ci, v, r0, r1, n)
     # Feature rows live at a 16-byte row stride (602 -> 604 floats) so the
@@ -336,7 +340,8 @@ def run_ours(args):
     Xp[:, :FEATS] = synth.normal_rows(r0, rows, FEATS, FEAT_SEED, 0, dev)
     X = Xp[:, :FEATS]
     w = make_weights(args.workload, dev)
-    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode)
+    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode,
+                         blocks_per_rank=args.blocks_per_rank)
     A_gcn = gcn_norm_rows(A_raw, r0, R, comm) if args.workload == "gcn" else None
     # The cached normalised graph keeps its longest-rows-first schedule (the
     # e2e path computes one per call inside the library).
@@ -378,7 +383,8 @@ def run_ours(args):
         return statistics.mean(a.elapsed_time(b) for a, b in pairs) if pairs else None
 
     gather_ms = phase_ms((0, "gather"))
-    phases = {f"layer{li}_{what}": phase_ms((li, what)) for li in range(2) for what in ("gemm", "gather")}
+    phases = {f"layer{li}_{what}": phase_ms((li, what)) for li in range(2)
+              for what in ("gemm", "exchange", "gather")}
     per_launch = launches / (args.steps + args.warmup)
 
     # e2e: host inputs -> device -> gcn_norm -> forward -> logits to host

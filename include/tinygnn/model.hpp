@@ -1,0 +1,79 @@
+// ============================================================================
+//  tinygnn/model.hpp -- Model (execution graph) and the binary file loaders.
+//
+//  Same interface as the reference's include/tinygnn/model.hpp:42-164:
+//  load_cora_binary, the TGNN weight file format (magic "TGNN", version 1,
+//  test accuracy, named row-major fp32 tensors), Model::add_*_layer,
+//  load_weights (names layer{i}.weight|bias|weight_neigh|weight_self|
+//  head{j}.{weight,attn_left,attn_right,bias}) and forward.  forward runs on
+//  the device: gcn_norm / add_self_loops once per call, every layer's fused
+//  kernels, and a multi-head GAT layer as one pass over the graph for all
+//  heads (heads concatenated or averaged as in model.cpp:403-422).
+// ============================================================================
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "tinygnn/layers.hpp"
+#include "tinygnn/tensor.hpp"
+
+namespace tinygnn {
+
+struct CoraData {
+    std::size_t num_nodes = 0, num_features = 0, num_classes = 0, num_edges = 0;
+    Tensor adjacency;   // SparseCSR N x N, values 1.0
+    Tensor features;    // Dense N x F
+    std::vector<int32_t> labels;
+    std::vector<uint8_t> train_mask, val_mask, test_mask;
+};
+
+CoraData load_cora_binary(const std::string& path);
+
+struct WeightFile {
+    float test_accuracy = 0.0f;
+    std::unordered_map<std::string, Tensor> tensors;
+};
+
+WeightFile load_weight_file(const std::string& path);
+
+class Model {
+public:
+    enum class InterActivation : uint8_t { None = 0, ReLU = 1, ELU = 2 };
+
+    std::size_t add_gcn_layer(std::size_t in_f, std::size_t out_f, bool bias = true,
+                              Activation act = Activation::ReLU,
+                              InterActivation post = InterActivation::None);
+    std::size_t add_sage_layer(std::size_t in_f, std::size_t out_f,
+                               SAGELayer::Aggregator agg = SAGELayer::Aggregator::Mean, bool bias = true,
+                               Activation act = Activation::ReLU,
+                               InterActivation post = InterActivation::None);
+    std::size_t add_gat_layer(std::size_t in_f, std::size_t out_f, std::size_t num_heads = 1,
+                              bool concat = true, float neg_slope = 0.2f, bool bias = true,
+                              Activation act = Activation::None,
+                              InterActivation post = InterActivation::None);
+    std::size_t num_layers() const noexcept { return layers_.size(); }
+
+    void load_weights(const std::string& path);
+    void load_weights(const WeightFile& wf);
+
+    Tensor forward(const Tensor& adjacency, const Tensor& features) const;
+
+private:
+    struct LayerEntry {
+        enum class Type : uint8_t { GCN, SAGE, GAT };
+        Type type;
+        std::size_t start_idx, count;
+        bool gat_concat;
+        InterActivation post_act;
+    };
+    std::vector<LayerEntry> layers_;
+    std::vector<GCNLayer> gcn_layers_;
+    std::vector<SAGELayer> sage_layers_;
+    std::vector<GATLayer> gat_layers_;
+};
+
+}  // namespace tinygnn

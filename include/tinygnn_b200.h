@@ -143,6 +143,37 @@ TG_API tg_status tg_spmm_f32(int64_t M, int64_t K, int64_t nnz, const int32_t* r
                              int32_t act, float alpha, const int32_t* row_order, int32_t mode,
                              void* stream);
 
+/* Column-block passes.  For a CSR whose rows are sorted by column (as
+ * TinyGNN's builders produce), tg_csr_column_splits writes the split points
+ * of `nblocks` column blocks of `width` columns: splits[q*M + i] is the
+ * first entry of row i with column >= q*width (q = 0..nblocks, the last
+ * being row_ptr[i+1]).  tg_spmm_segment_f32 then runs one pass over entries
+ * [seg_begin[i], seg_end[i]) of every row: with carry = 0 the accumulator
+ * starts at zero, with carry = 1 it continues from C; bias and activation
+ * are applied only with last = 1.  Passes over q = 0..nblocks-1 in order
+ * reproduce tg_spmm_f32 bit for bit, while each pass gathers from only one
+ * block of B's rows (an L2-sized working set, or the block another GPU has
+ * just delivered).  The same for the SAGE-mean combine (the 1/deg uses the
+ * whole row). */
+TG_API tg_status tg_csr_column_splits(int64_t M, const int32_t* row_ptr, const int32_t* col_ind,
+                                      int32_t nblocks, int64_t width, int32_t* splits_out,
+                                      void* stream);
+TG_API tg_status tg_spmm_segment_f32(int64_t M, int64_t K, const int32_t* row_ptr,
+                                     const int32_t* col_ind, const float* values,
+                                     const int32_t* seg_begin, const int32_t* seg_end,
+                                     const float* B, int64_t F, int64_t ldb, float* C, int64_t ldc,
+                                     const float* bias, int32_t act, float alpha,
+                                     const int32_t* row_order, int32_t carry, int32_t last,
+                                     int32_t mode, void* stream);
+TG_API tg_status tg_sage_mean_combine_segment_f32(int64_t M, int64_t K, const int32_t* row_ptr,
+                                                  const int32_t* col_ind, const int32_t* seg_begin,
+                                                  const int32_t* seg_end, const float* Tn, int64_t F,
+                                                  int64_t ldn, const float* Ts, int64_t lds,
+                                                  const float* bias, int32_t act, float* out,
+                                                  int64_t ldo, const int32_t* row_order,
+                                                  int32_t carry, int32_t last, int32_t mode,
+                                                  void* stream);
+
 /* Rows sorted by decreasing stored length (ties by row id) into
  * order_out[M]: a schedule that starts the longest rows first. */
 TG_API tg_status tg_csr_degree_order(int64_t M, const int32_t* row_ptr, int32_t* order_out,

@@ -67,6 +67,27 @@ def test_row_block_gcn_norm_matches_global(tg, world):
         assert_bits_equal(asl.values.cpu().numpy(), G[2][a:b], "values")
 
 
+@pytest.mark.parametrize("workload,bpr", [("gcn", 2), ("gcn", 3), ("sage", 4)])
+def test_single_gpu_column_blocks_are_bit_identical(tg, workload, bpr):
+    from tinygnn_b200.dist import Comm, Layer, ShardedModel, gcn_norm_rows
+    rng, rp, ci, v, X = _graph(seed=bpr)
+    n = rp.size - 1
+    W0 = torch.as_tensor((rng.standard_normal((40, 32)) * 0.2).astype(np.float32)).cuda()
+    W1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
+    S0 = torch.as_tensor((rng.standard_normal((40, 32)) * 0.2).astype(np.float32)).cuda()
+    S1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
+    sage = workload == "sage"
+    layers = [Layer(workload, W0, None, "relu", S0 if sage else None),
+              Layer(workload, W1, None, None, S1 if sage else None)]
+    A = tg.CSR.from_numpy(rp, ci, v)
+    An = gcn_norm_rows(A, 0, n, Comm(1, 0)) if not sage else None
+    Xd = torch.as_tensor(X).cuda()
+    one = ShardedModel(layers, n, Comm(1, 0), "cuda").forward(An, A, Xd).clone()
+    blk = ShardedModel(layers, n, Comm(1, 0), "cuda", blocks_per_rank=bpr).forward(An, A, Xd)
+    torch.cuda.synchronize()
+    assert_bits_equal(blk.cpu().numpy(), one.cpu().numpy(), f"{workload} {bpr} blocks")
+
+
 @pytest.mark.parametrize("workload,world", [("gcn", 2), ("gcn", 4), ("sage", 3), ("gcn", 8)])
 def test_sharded_forward_equals_unpartitioned(tg, workload, world):
     from tinygnn_b200.dist import Layer, ShardedModel, gcn_norm_rows, row_block, slice_rows

@@ -182,6 +182,33 @@ def test_spmm_large_auto_schedule_vs_oracle(tg, F):
                       P.gcn_layer(*An, H, W, None, True), f"gcn auto-ordered F={F}")
 
 
+@pytest.mark.parametrize("nblocks", [1, 2, 3, 8])
+def test_column_block_passes_equal_one_pass(tg, nblocks):
+    """Passes over column blocks in order reproduce spmm / the SAGE combine bit for bit."""
+    rng = np.random.default_rng(nblocks)
+    n, F = 20000, 41
+    rp, ci, v = powerlaw_csr(rng, n, 16)
+    A = csr(tg, rp, ci, v)
+    B = torch.zeros((n, 44), device="cuda")
+    B[:, :F] = dev(rng.standard_normal((n, F)).astype(np.float32))
+    b = dev(rng.standard_normal(F).astype(np.float32))
+    width = (n + nblocks - 1) // nblocks
+    sp = tg.ops.column_splits(A, nblocks, width)
+    h_sp = host(sp)
+    assert np.array_equal(h_sp[0], rp[:-1]) and np.array_equal(h_sp[-1], rp[1:])
+    ref = host(tg.spmm(A, B[:, :F], bias=b, act="relu"))
+    out = torch.empty((n, F), device="cuda")
+    for q in range(nblocks):
+        tg.ops.spmm_segment(A, B[:, :F], sp[q], sp[q + 1], out, q > 0, q == nblocks - 1, bias=b, act="relu")
+    assert_bits_equal(host(out), ref, f"spmm in {nblocks} passes")
+    Ts = dev(rng.standard_normal((n, F)).astype(np.float32))
+    ref = host(tg.ops.sage_mean_combine(A, B[:, :F], Ts, bias=b, act="relu"))
+    for q in range(nblocks):
+        tg.ops.sage_mean_combine_segment(A, B[:, :F], Ts, sp[q], sp[q + 1], out, q > 0, q == nblocks - 1, bias=b,
+                                         act="relu")
+    assert_bits_equal(host(out), ref, f"sage combine in {nblocks} passes")
+
+
 def test_spmm_epilogue_and_strides(tg):
     rng = np.random.default_rng(5)
     n, F = 1000, 41

@@ -44,6 +44,11 @@ SIGNATURES = {
     "tg_add_bias_f32": (i32, [vp, i64, i64, i64, vp, vp]),
     "tg_spmm_f32": (i32, [i64, i64, i64, vp, vp, vp, vp, i64, i64, vp, i64, vp, i32, f32, vp, i32, vp]),
     "tg_csr_degree_order": (i32, [i64, vp, vp, vp]),
+    "tg_csr_column_splits": (i32, [i64, vp, vp, i32, i64, vp, vp]),
+    "tg_spmm_segment_f32": (i32, [i64, i64, vp, vp, vp, vp, vp, vp, i64, i64, vp, i64, vp, i32, f32, vp, i32, i32,
+                                  i32, vp]),
+    "tg_sage_mean_combine_segment_f32": (i32, [i64, i64, vp, vp, vp, vp, vp, i64, i64, vp, i64, vp, i32, vp, i64,
+                                               vp, i32, i32, i32, vp]),
     "tg_sage_aggregate_f32": (i32, [i64, i64, i64, vp, vp, vp, i64, i64, vp, i64, i32, vp]),
     "tg_sage_max_aggregate_f32": (i32, [i64, i64, i64, vp, vp, vp, i64, i64, vp, i64, vp]),
     "tg_sage_mean_combine_f32": (i32, [i64, i64, i64, vp, vp, vp, i64, i64, vp, i64, vp, i32, vp, i64, vp, i32,

@@ -42,6 +42,14 @@ struct GatherArgs {
     // Without `order`, large launches compute a longest-rows-first schedule
     // in pool memory; false keeps the natural row order and allocates nothing.
     bool allow_auto_order = true;
+    // Column-block pass: only entries [seg_lo[i], seg_hi[i]) of row i; the
+    // accumulator starts from C (carry) and the epilogue (1/deg with the full
+    // row length, self, bias, activation) runs only on the last pass, so the
+    // passes in increasing column order reproduce the one-pass arithmetic.
+    const int32_t* seg_lo = nullptr;
+    const int32_t* seg_hi = nullptr;
+    bool carry = false;
+    bool last = true;
 };
 
 // Queues the gather on `s`.

@@ -124,9 +124,19 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherArgs a) {
     float acc[SPL][VEC];
     const float init = (OP == GATHER_SUM) ? 0.0f : -INFINITY;
 #pragma unroll
-    for (int s = 0; s < SPL; ++s)
+    for (int s = 0; s < SPL; ++s) {
+        if (a.carry && live[s]) {  // continue the chain stored by the previous pass
+            if (CVEC && full[s]) {
+                ldv_plain<VEC>(a.C + row * a.ldc + fo[s], acc[s]);
+            } else {
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) acc[s][k] = init;
+                for (int k = 0; k < VEC; ++k) acc[s][k] = (fo[s] + k < a.F) ? a.C[row * a.ldc + fo[s] + k] : init;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) acc[s][k] = init;
+        }
+    }
 
     bool avx[SPL][VEC];
 #pragma unroll
@@ -134,8 +144,10 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherArgs a) {
 #pragma unroll
         for (int k = 0; k < VEC; ++k) avx[s][k] = (fo[s] + k) < a.max_avx_cols;
 
-    const int32_t start = ld_i32(a.rp + row, stream);
-    const int32_t end = ld_i32(a.rp + row + 1, stream);
+    const int32_t row_begin = ld_i32(a.rp + row, stream);
+    const int32_t row_end = ld_i32(a.rp + row + 1, stream);
+    const int32_t start = a.seg_lo ? ld_i32(a.seg_lo + row, stream) : row_begin;
+    const int32_t end = a.seg_hi ? ld_i32(a.seg_hi + row, stream) : row_end;
 
     // Window of LPR entries: one (col, val) per lane; the next one is loaded
     // before the current one is consumed.
@@ -191,7 +203,21 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherArgs a) {
         }
     }
 
-    const int32_t deg = end - start;
+    if (!a.last) {  // intermediate pass: store the raw accumulator
+#pragma unroll
+        for (int s = 0; s < SPL; ++s) {
+            if (!live[s]) continue;
+            if (CVEC && full[s]) {
+                stv<VEC>(a.C + row * a.ldc + fo[s], acc[s]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < VEC; ++k)
+                    if (fo[s] + k < a.F) a.C[row * a.ldc + fo[s] + k] = acc[s][k];
+            }
+        }
+        return;
+    }
+    const int32_t deg = row_end - row_begin;  // the whole row, whichever segment this pass covered
     const float inv_deg = (OP == GATHER_SUM && a.mean && deg > 0) ? __fdiv_rn(1.0f, static_cast<float>(deg)) : 1.0f;
 #pragma unroll
     for (int s = 0; s < SPL; ++s) {

@@ -182,6 +182,26 @@ __global__ void order_scatter_kernel(int64_t M, const int32_t* rp, const int32_t
 }
 }  // namespace
 
+// splits[q*M + i] = first entry of row i with column >= q*width (rows sorted
+// by column); splits[0*M + i] = row_ptr[i], splits[nb*M + i] = row_ptr[i+1].
+__global__ void column_splits_kernel(int64_t M, const int32_t* rp, const int32_t* ci, int nb, int64_t width,
+                                     int32_t* out) {
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= M * (nb + 1)) return;
+    const int q = static_cast<int>(t / M);
+    const int64_t i = t % M;
+    int32_t lo = rp[i], hi = rp[i + 1];
+    if (q == 0) { out[t] = lo; return; }
+    if (q == nb) { out[t] = hi; return; }
+    const int64_t key = static_cast<int64_t>(q) * width;
+    while (lo < hi) {  // lower_bound
+        const int32_t mid = lo + (hi - lo) / 2;
+        if (static_cast<int64_t>(ci[mid]) < key) lo = mid + 1;
+        else hi = mid;
+    }
+    out[t] = lo;
+}
+
 void csr_degree_order(int64_t M, const int32_t* rp, int32_t* out, cudaStream_t s) {
     if (M == 0) return;
     const int64_t nb = ceil_div(M, ORDER_BLOCK);
@@ -238,6 +258,63 @@ TG_API tg_status tg_sage_mean_combine_f32(int64_t M, int64_t K, int64_t nnz, con
         a.B = Tn; a.ldb = ldn; a.F = F; a.self = Ts; a.lds = lds;
         a.C = out; a.ldc = ldo; a.bias = bias; a.act = act; a.op = GATHER_SUM; a.mean = 1;
         a.b_padded = (mode & TG_FLAG_B_ROWS_PADDED) != 0;
+        gather_rows(a, as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_csr_column_splits(int64_t M, const int32_t* row_ptr, const int32_t* col_ind, int32_t nblocks,
+                                      int64_t width, int32_t* splits_out, void* stream) {
+    return guard([&] {
+        require_device();
+        if (M < 0 || nblocks < 1 || width < 1) invalid("csr_column_splits: need M >= 0, nblocks >= 1, width >= 1");
+        const int64_t total = M * (nblocks + 1);
+        if (total == 0) return;
+        launch("column_splits", column_splits_kernel, dim3(static_cast<unsigned>(ceil_div(total, 256))), dim3(256), 0,
+               as_stream(stream), M, row_ptr, col_ind, static_cast<int>(nblocks), width, splits_out);
+    });
+}
+
+TG_API tg_status tg_spmm_segment_f32(int64_t M, int64_t K, const int32_t* row_ptr, const int32_t* col_ind,
+                                     const float* values, const int32_t* seg_begin, const int32_t* seg_end,
+                                     const float* B, int64_t F, int64_t ldb, float* C, int64_t ldc, const float* bias,
+                                     int32_t act, float alpha, const int32_t* row_order, int32_t carry, int32_t last,
+                                     int32_t mode, void* stream) {
+    return guard([&] {
+        require_device();
+        (void)K;
+        if (M < 0 || F < 0) invalid("spmm_segment: negative size");
+        check_ld("spmm_segment", "B", ldb, F);
+        check_ld("spmm_segment", "C", ldc, F);
+        check_ptr("spmm_segment", "seg_begin/seg_end", seg_begin && seg_end ? seg_begin : nullptr, M > 0);
+        GatherArgs a;
+        a.M = M; a.rp = row_ptr; a.ci = col_ind; a.val = values; a.order = row_order;
+        a.B = B; a.ldb = ldb; a.F = F; a.C = C; a.ldc = ldc;
+        a.bias = bias; a.act = act; a.alpha = alpha; a.op = GATHER_SUM;
+        a.b_padded = (mode & TG_FLAG_B_ROWS_PADDED) != 0;
+        a.seg_lo = seg_begin; a.seg_hi = seg_end; a.carry = carry != 0; a.last = last != 0;
+        gather_rows(a, as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_sage_mean_combine_segment_f32(int64_t M, int64_t K, const int32_t* row_ptr,
+                                                  const int32_t* col_ind, const int32_t* seg_begin,
+                                                  const int32_t* seg_end, const float* Tn, int64_t F, int64_t ldn,
+                                                  const float* Ts, int64_t lds, const float* bias, int32_t act,
+                                                  float* out, int64_t ldo, const int32_t* row_order, int32_t carry,
+                                                  int32_t last, int32_t mode, void* stream) {
+    return guard([&] {
+        require_device();
+        (void)K;
+        if (M < 0 || F < 0) invalid("sage_mean_combine_segment: negative size");
+        check_ld("sage_mean_combine_segment", "Tn", ldn, F);
+        check_ld("sage_mean_combine_segment", "Ts", lds, F);
+        check_ld("sage_mean_combine_segment", "out", ldo, F);
+        GatherArgs a;
+        a.M = M; a.rp = row_ptr; a.ci = col_ind; a.order = row_order;
+        a.B = Tn; a.ldb = ldn; a.F = F; a.self = Ts; a.lds = lds;
+        a.C = out; a.ldc = ldo; a.bias = bias; a.act = act; a.op = GATHER_SUM; a.mean = 1;
+        a.b_padded = (mode & TG_FLAG_B_ROWS_PADDED) != 0;
+        a.seg_lo = seg_begin; a.seg_hi = seg_end; a.carry = carry != 0; a.last = last != 0;
         gather_rows(a, as_stream(stream));
     });
 }

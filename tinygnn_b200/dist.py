@@ -1,22 +1,31 @@
 """Row-partitioned GCN / SAGE forward over several GPUs (one process per GPU).
 
 Partitioning (1-D, by rows): with P ranks and N nodes, rank r owns global
-rows [r*R, min(N, (r+1)*R)) where R = ceil(N/P) -- its rows of the
-adjacency (global column ids) and of the features.  Every per-layer exchange
-is one NCCL all-gather of the transformed rows into a (P*R) x F buffer whose
-row j is global node j, so gathers index it with the global column ids
-directly (no remapping).  Hubs are never split across ranks.
+rows [r*R, min(N, (r+1)*R)) where R = ceil(N/P) (rounded up to a multiple of
+the column blocks per rank) -- its rows of the adjacency (global column ids)
+and of the features.  Each layer's transformed rows are exchanged into a
+(P*R) x F buffer whose row j is global node j, so gathers index it with the
+global column ids directly (no remapping).  Hubs are never split across
+ranks.
 
 Per GCN layer on rank r (src/layers.cpp:286-339 per block of rows):
-  1. HW[rR : rR + rows] = H_r . W          (exact GEMM, this rank's rows)
-  2. all-gather HW over the ranks           (torch.distributed, NCCL)
-  3. H'_r = act(A_norm[r-rows] . HW + b)    (gather kernel, fused epilogue)
+  1. HW[rR : rR + rows] = H_r . W          (this rank's rows)
+  2. exchange HW over the ranks             (NCCL via torch.distributed)
+  3. H'_r = act(A_norm[r-rows] . HW + b)    (gather, fused epilogue)
+Step 2-3 run as column-block passes: every rank's block is broadcast
+asynchronously, and the gather runs one pass per block in increasing column
+order (tg_spmm_segment_f32), starting as soon as that block has arrived.
+The passes carry each output element's FMA chain through the output, so the
+result is bit-identical to the one-pass gather -- and to one GPU -- while
+the transfer of block q+1 overlaps the pass over block q, and each pass
+reads only one block of the gathered operand (an L2-sized working set).
+
 gcn_norm of a row block (src/layers.cpp:158-208): self-loops and degrees are
 row-local; the column scale needs every node's 1/sqrt(deg), which one
 all-gather of the degree vector provides -- bit-identical to the
 single-GPU gcn_norm.
 
-SAGE (transform-first, mean): Tn_r = H_r . W_neigh is all-gathered,
+SAGE (transform-first, mean): Tn_r = H_r . W_neigh is exchanged,
 Ts_r = H_r . W_self stays local, H'_r = act(mean_j Tn[j] + Ts_r[i] + b).
 """
 from __future__ import annotations
@@ -31,9 +40,10 @@ from . import ops
 from .ops import CSR
 
 
-def row_block(n: int, world: int, rank: int) -> Tuple[int, int, int]:
-    """(R, row0, row1): the equal-size row block of ``rank``."""
+def row_block(n: int, world: int, rank: int, multiple: int = 1) -> Tuple[int, int, int]:
+    """(R, row0, row1): the equal-size row block of ``rank`` (R a multiple of ``multiple``)."""
     R = (n + world - 1) // world
+    R = (R + multiple - 1) // multiple * multiple
     r0 = min(n, rank * R)
     return R, r0, min(n, r0 + R)
 
@@ -52,7 +62,7 @@ def _pad4(n: int) -> int:
 
 
 class Comm:
-    """The exchange step: all-gather of equal row blocks (NCCL), or nothing at P=1."""
+    """The exchange steps (NCCL through torch.distributed); nothing at P = 1."""
 
     def __init__(self, world: int, rank: int, group=None):
         self.world, self.rank, self.group = world, rank, group
@@ -63,6 +73,12 @@ class Comm:
             return
         mine = full[self.rank * R:(self.rank + 1) * R]
         dist.all_gather_into_tensor(full, mine, group=self.group)
+
+    def broadcast_rows(self, full: torch.Tensor, R: int, src: int):
+        """Start sending rank ``src``'s rows of ``full`` to every rank; returns a waitable."""
+        if self.world == 1:
+            return None
+        return dist.broadcast(full[src * R:(src + 1) * R], src=src, group=self.group, async_op=True)
 
 
 def gcn_norm_rows(A: CSR, row0: int, R: int, comm: Comm, dis_all: Optional[torch.Tensor] = None) -> CSR:
@@ -91,12 +107,18 @@ class ShardedModel:
 
     ``forward`` takes this rank's normalised (GCN) or raw (SAGE) adjacency
     rows and feature rows, already in HBM; buffers are allocated once.
+    ``blocks_per_rank`` > 1 splits every rank's columns into that many
+    column blocks (extra passes that each gather from a smaller working set).
     """
 
-    def __init__(self, layers: List[Layer], n: int, comm: Comm, device, mode: str = "exact"):
+    def __init__(self, layers: List[Layer], n: int, comm: Comm, device, mode: str = "exact",
+                 blocks_per_rank: int = 1):
         self.layers, self.n, self.comm, self.device, self.mode = layers, n, comm, device, mode
-        self.R, self.row0, self.row1 = row_block(n, comm.world, comm.rank)
+        self.bpr = max(1, int(blocks_per_rank))
+        self.R, self.row0, self.row1 = row_block(n, comm.world, comm.rank, self.bpr)
         self.rows = self.row1 - self.row0
+        self.nblocks = comm.world * self.bpr
+        self.width = self.R // self.bpr
         P = comm.world
         self.full = []   # gathered operand per layer: (P*R) x pad4(F_out)
         self.outs = []
@@ -107,13 +129,23 @@ class ShardedModel:
             self.outs.append(torch.empty((self.rows, fo), dtype=torch.float32, device=device))
             self.selfs.append(torch.empty((self.rows, _pad4(fo)), dtype=torch.float32, device=device)
                               if L.kind == "sage" else None)
-        self.timing = None  # optional hook: (layer index, "gather"|"gemm", start|end) -> None
+        self.timing = None  # optional hook: (layer index, phase, "start"|"end") -> None
 
     def _mark(self, li: int, what: str, edge: str) -> None:
         if self.timing is not None:
             self.timing(li, what, edge)
 
-    # The three phases of a layer; forward() runs them in order.  Tests that
+    def splits(self, A: CSR) -> Optional[torch.Tensor]:
+        """Column-block split points of A's rows (cached on A)."""
+        if self.nblocks == 1:
+            return None
+        key = (self.nblocks, self.width)
+        cache = getattr(A, "_splits", None)
+        if cache is None or cache[0] != key:
+            A._splits = (key, ops.column_splits(A, self.nblocks, self.width))
+        return A._splits[1]
+
+    # The phases of a layer; forward() runs them in order.  Tests that
     # emulate several ranks in one process interleave them across shards.
     def transform(self, li: int, H: torch.Tensor) -> None:
         """This rank's rows of H . W (and H . W_self for SAGE) into the gather buffer."""
@@ -127,17 +159,51 @@ class ShardedModel:
         self._mark(li, "gemm", "end")
 
     def exchange(self, li: int) -> None:
+        """Blocking all-gather (used by single-pass aggregation)."""
+        self._mark(li, "exchange", "start")
         self.comm.all_gather_rows(self.full[li], self.R)
+        self._mark(li, "exchange", "end")
 
-    def aggregate(self, li: int, A_gcn: Optional[CSR], A_raw: Optional[CSR]) -> torch.Tensor:
+    def _pass(self, li: int, A: CSR, lo, hi, carry: bool, last: bool) -> torch.Tensor:
         L = self.layers[li]
         fo = L.W.shape[1]
         B = self.full[li][:self.n, :fo]
-        self._mark(li, "gather", "start")
         if L.kind == "gcn":
-            H = ops.spmm(A_gcn, B, bias=L.b, act=L.act, out=self.outs[li])
-        else:
-            H = ops.sage_mean_combine(A_raw, B, self.selfs[li][:, :fo], bias=L.b, act=L.act, out=self.outs[li])
+            if lo is None:
+                return ops.spmm(A, B, bias=L.b, act=L.act, out=self.outs[li])
+            return ops.spmm_segment(A, B, lo, hi, self.outs[li], carry, last, bias=L.b, act=L.act)
+        if lo is None:
+            return ops.sage_mean_combine(A, B, self.selfs[li][:, :fo], bias=L.b, act=L.act, out=self.outs[li])
+        return ops.sage_mean_combine_segment(A, B, self.selfs[li][:, :fo], lo, hi, self.outs[li], carry, last,
+                                             bias=L.b, act=L.act)
+
+    def aggregate(self, li: int, A_gcn: Optional[CSR], A_raw: Optional[CSR]) -> torch.Tensor:
+        """Single pass over the whole (already exchanged) operand."""
+        A = A_gcn if self.layers[li].kind == "gcn" else A_raw
+        self._mark(li, "gather", "start")
+        H = self._pass(li, A, None, None, False, True)
+        self._mark(li, "gather", "end")
+        return H
+
+    def exchange_and_aggregate(self, li: int, A_gcn: Optional[CSR], A_raw: Optional[CSR]) -> torch.Tensor:
+        """Per-block passes, each started as soon as its block has arrived."""
+        A = A_gcn if self.layers[li].kind == "gcn" else A_raw
+        sp = self.splits(A)
+        if sp is None:
+            self.exchange(li)
+            return self.aggregate(li, A_gcn, A_raw)
+        self._mark(li, "gather", "start")
+        works = [self.comm.broadcast_rows(self.full[li], self.R, src) for src in range(self.comm.world)]
+        H = None
+        for q in range(self.nblocks):
+            src = q // self.bpr
+            if works[src] is not None and src != self.comm.rank:
+                works[src].wait()
+                works[src] = None
+            H = self._pass(li, A, sp[q], sp[q + 1], q > 0, q == self.nblocks - 1)
+        for w in works:
+            if w is not None:
+                w.wait()
         self._mark(li, "gather", "end")
         return H
 
@@ -146,8 +212,7 @@ class ShardedModel:
         H = X
         for li in range(len(self.layers)):
             self.transform(li, H)
-            self.exchange(li)
-            H = self.aggregate(li, A_gcn, A_raw)
+            H = self.exchange_and_aggregate(li, A_gcn, A_raw)
         if log_softmax:
             ops.log_softmax_(H)
         return H

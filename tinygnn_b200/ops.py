@@ -213,6 +213,38 @@ def spmm(A: CSR, B: torch.Tensor, bias=None, act=None, alpha: float = 0.0, row_o
     return out
 
 
+def column_splits(A: CSR, nblocks: int, width: int) -> torch.Tensor:
+    """(nblocks+1) x n_rows split points of sorted rows at column multiples of `width`."""
+    out = torch.empty((nblocks + 1, A.n_rows), dtype=torch.int32, device=A.row_ptr.device)
+    check(lib.tg_csr_column_splits(A.n_rows, _p(A.row_ptr), _p(A.col_ind), nblocks, width, _p(out), _stream()))
+    return out
+
+
+def spmm_segment(A: CSR, B: torch.Tensor, seg_begin: torch.Tensor, seg_end: torch.Tensor, out: torch.Tensor,
+                 carry: bool, last: bool, bias=None, act=None, alpha: float = 0.0, row_order=None) -> torch.Tensor:
+    """One column-block pass of spmm (see tg_spmm_segment_f32)."""
+    B = _dense(B, "B")
+    b = _vec(bias)
+    flags = FLAG_B_ROWS_PADDED if _padded(B) else 0
+    check(lib.tg_spmm_segment_f32(A.n_rows, A.n_cols, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(seg_begin),
+                                  _p(seg_end), _p(B), B.shape[1], _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha,
+                                  _p(_ord(A, row_order)), int(carry), int(last), flags, _stream()))
+    return out
+
+
+def sage_mean_combine_segment(A: CSR, Tn: torch.Tensor, Ts: torch.Tensor, seg_begin, seg_end, out, carry: bool,
+                              last: bool, bias=None, act=None, row_order=None) -> torch.Tensor:
+    """One column-block pass of the transform-first SAGE-mean combine."""
+    Tn, Ts = _dense(Tn, "Tn"), _dense(Ts, "Ts")
+    b = _vec(bias)
+    flags = FLAG_B_ROWS_PADDED if _padded(Tn) else 0
+    check(lib.tg_sage_mean_combine_segment_f32(A.n_rows, A.n_cols, _p(A.row_ptr), _p(A.col_ind), _p(seg_begin),
+                                               _p(seg_end), _p(Tn), Tn.shape[1], _ld(Tn), _p(Ts), _ld(Ts), _p(b),
+                                               ACT[act], _p(out), _ld(out), _p(_ord(A, row_order)), int(carry),
+                                               int(last), flags, _stream()))
+    return out
+
+
 def sage_mean_combine(A: CSR, Tn: torch.Tensor, Ts: torch.Tensor, bias=None, act=None, row_order=None,
                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out[i] = act(mean_j Tn[j] + Ts[i] + bias): transform-first SAGE mean."""
