@@ -59,8 +59,8 @@ def parse():
                     help="fast: 3xTF32 tensor-core GEMMs (within fp32 tolerance); exact: bit-identical GEMMs")
     ap.add_argument("--small", action="store_true", help="a 20k-node graph (quick functional run)")
     ap.add_argument("--edges", type=int, default=0, help="override the edge count (profiling on a smaller graph)")
-    ap.add_argument("--blocks-per-rank", type=int, default=1,
-                    help="column blocks per rank for the gathers (passes with smaller working sets)")
+    ap.add_argument("--blocks-per-rank", default="auto",
+                    help="column blocks per rank for the gathers: 'auto' or a count")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
@@ -302,7 +302,8 @@ def metric_name(workload):
 def config_dict(args, n, nnz):
     return {"workload": f"{args.workload}-reddit-shape" + ("-small" if args.small else ""),
             "nodes": n, "nnz": nnz, "features": FEATS, "hidden": HIDDEN, "classes": CLASSES,
-            "partition": "1-D equal row blocks, NCCL all-gather of each layer's transformed rows",
+            "partition": "1-D equal row blocks; each layer's transformed rows broadcast per rank block "
+                         "(NCCL, async) with one exact gather pass per arriving column block",
             "parallelism": f"row-partition x{args.gpus}",
             "l2": "inputs larger than L2 (CSR 918 MB, features 561 MB); no flush between steps",
             "mode": ("fast: 3xTF32 tcgen05 GEMMs, order-preserving fp32 gathers" if args.mode == "fast"
@@ -331,7 +332,10 @@ def run_ours(args):
 
     comm = Comm(world, rank, group)
     n, rp, ci, v = make_graph(args.small, dev, args.edges)
-    R, r0, r1 = row_block(n, world, rank, args.blocks_per_rank)
+    w = make_weights(args.workload, dev)
+    bpr = args.blocks_per_rank if args.blocks_per_rank == "auto" else int(args.blocks_per_rank)
+    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode, blocks_per_rank=bpr)
+    R, r0, r1 = model.R, model.row0, model.row1
     rows = r1 - r0
     A_raw = slice_rows(rp, ci, v, r0, r1, n)
     # Feature rows live at a 16-byte row stride (602 -> 604 floats) so the
@@ -339,9 +343,6 @@ def run_ours(args):
     Xp = torch.zeros((rows, (FEATS + 3) // 4 * 4), dtype=torch.float32, device=dev)
     Xp[:, :FEATS] = synth.normal_rows(r0, rows, FEATS, FEAT_SEED, 0, dev)
     X = Xp[:, :FEATS]
-    w = make_weights(args.workload, dev)
-    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode,
-                         blocks_per_rank=args.blocks_per_rank)
     A_gcn = gcn_norm_rows(A_raw, r0, R, comm) if args.workload == "gcn" else None
     # The cached normalised graph keeps its longest-rows-first schedule (the
     # e2e path computes one per call inside the library).

@@ -1,0 +1,50 @@
+// ============================================================================
+//  api/internal.hpp -- shared helpers of the C++ API (not installed).
+// ============================================================================
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "tinygnn/tensor.hpp"
+#include "tinygnn_b200.h"
+
+namespace tinygnn {
+namespace detail {
+
+// Every C++ API call runs on the calling thread's default stream.
+inline void* stream() { return reinterpret_cast<void*>(cudaStreamPerThread); }
+inline cudaStream_t cstream() { return cudaStreamPerThread; }
+
+// tg_status -> the exception TinyGNN throws for that condition.
+inline void check(tg_status s) {
+    if (s == TG_OK) return;
+    const std::string msg = tg_last_error_message();
+    if (s == TG_ERR_INVALID_ARGUMENT) throw std::invalid_argument(msg);
+    if (s == TG_ERR_OUT_OF_RANGE) throw std::out_of_range(msg);
+    throw std::runtime_error(msg);
+}
+
+inline void cuda(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+inline int mode() { return fast_math() ? TG_MODE_FAST : TG_MODE_EXACT; }
+
+inline std::size_t pad4(std::size_t n) { return (n + 3) / 4 * 4; }
+
+inline std::string shape_str(std::size_t r, std::size_t c) {
+    return "(" + std::to_string(r) + "\xC3\x97" + std::to_string(c) + ")";
+}
+
+}  // namespace detail
+
+// Constructs tensors over device buffers the API has just produced.
+struct TensorAccess {
+    static Tensor csr_from_device(std::size_t rows, std::size_t cols, int32_t* d_rp, int32_t* d_ci, float* d_v,
+                                  std::size_t nnz);
+};
+
+}  // namespace tinygnn

@@ -1,0 +1,241 @@
+// ============================================================================
+//  api/model.cpp -- Model (execution graph) and the binary loaders (reference
+//  src/model.cpp:30-439).
+//
+//  The file formats are TinyGNN's (cora_graph.bin: N, F, C, E as uint32
+//  LE, features, labels, three masks, src[E], dst[E]; TGNN weight files:
+//  magic, version 1, accuracy, named tensors), read on the host; the
+//  adjacency CSR is built on the device (edge_list_to_csr, bit-identical).
+//  Model::forward normalises on the device once per call, like the
+//  reference, runs every layer's fused kernels, and runs a multi-head GAT
+//  layer as one pass over the graph for all heads.
+// ============================================================================
+#include "tinygnn/model.hpp"
+
+#include <cstring>
+#include <fstream>
+
+#include "internal.hpp"
+#include "tinygnn/graph_loader.hpp"
+#include "tinygnn/ops.hpp"
+
+namespace tinygnn {
+
+using detail::check;
+using detail::stream;
+
+namespace {
+
+void read_exact(std::ifstream& f, void* buf, std::size_t n, const char* ctx) {
+    f.read(reinterpret_cast<char*>(buf), static_cast<std::streamsize>(n));
+    if (!f) throw std::runtime_error(std::string(ctx) + ": unexpected end of file or read error.");
+}
+
+template <class T>
+T read_le(std::ifstream& f, const char* ctx) {
+    T v{};
+    read_exact(f, &v, sizeof(T), ctx);  // little-endian host
+    return v;
+}
+
+float* dalloc(std::size_t n) {
+    void* p = nullptr;
+    detail::cuda(cudaMallocAsync(&p, (n ? n : 1) * sizeof(float), detail::cstream()), "tinygnn allocation");
+    return static_cast<float*>(p);
+}
+
+struct DevBuf {
+    float* p = nullptr;
+    explicit DevBuf(std::size_t n) : p(dalloc(n)) {}
+    ~DevBuf() {
+        if (p && cudaFreeAsync(p, detail::cstream()) != cudaSuccess) cudaGetLastError();
+    }
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+};
+
+// Packs rows x cols of `src` (device, row stride ld) into dst at column offset.
+void pack(float* dst, std::size_t dst_ld, std::size_t col0, const Tensor& src) {
+    if (src.rows() * src.cols() == 0) return;
+    detail::cuda(cudaMemcpy2DAsync(dst + col0, dst_ld * sizeof(float), src.device_data(),
+                                   src.device_ld() * sizeof(float), src.cols() * sizeof(float), src.rows(),
+                                   cudaMemcpyDeviceToDevice, detail::cstream()),
+                 "Model::forward");
+}
+
+}  // namespace
+
+CoraData load_cora_binary(const std::string& path) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f.is_open()) throw std::runtime_error("load_cora_binary: cannot open " + path);
+    const char* ctx = "load_cora_binary";
+    CoraData cd;
+    cd.num_nodes = read_le<uint32_t>(f, ctx);
+    cd.num_features = read_le<uint32_t>(f, ctx);
+    cd.num_classes = read_le<uint32_t>(f, ctx);
+    cd.num_edges = read_le<uint32_t>(f, ctx);
+    const std::size_t N = cd.num_nodes, F = cd.num_features, E = cd.num_edges;
+    std::vector<float> feat(N * F);
+    read_exact(f, feat.data(), N * F * sizeof(float), ctx);
+    cd.features = Tensor::dense(N, F, std::move(feat));
+    cd.labels.resize(N);
+    read_exact(f, cd.labels.data(), N * sizeof(int32_t), ctx);
+    cd.train_mask.resize(N);
+    cd.val_mask.resize(N);
+    cd.test_mask.resize(N);
+    read_exact(f, cd.train_mask.data(), N, ctx);
+    read_exact(f, cd.val_mask.data(), N, ctx);
+    read_exact(f, cd.test_mask.data(), N, ctx);
+    std::vector<int32_t> src(E), dst(E);
+    read_exact(f, src.data(), E * sizeof(int32_t), ctx);
+    read_exact(f, dst.data(), E * sizeof(int32_t), ctx);
+    std::vector<std::pair<int32_t, int32_t>> edges(E);
+    for (std::size_t e = 0; e < E; ++e) edges[e] = {src[e], dst[e]};
+    cd.adjacency = GraphLoader::edge_list_to_csr(edges, N);  // same CSR algorithm (model.cpp:89-122)
+    return cd;
+}
+
+WeightFile load_weight_file(const std::string& path) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f.is_open()) throw std::runtime_error("load_weight_file: cannot open " + path);
+    const char* ctx = "load_weight_file";
+    char magic[4]{};
+    read_exact(f, magic, 4, ctx);
+    if (std::memcmp(magic, "TGNN", 4) != 0) throw std::runtime_error("load_weight_file: invalid magic in " + path);
+    const uint32_t version = read_le<uint32_t>(f, ctx);
+    if (version != 1)
+        throw std::runtime_error("load_weight_file: unsupported version " + std::to_string(version) + " in " + path);
+    WeightFile wf;
+    wf.test_accuracy = read_le<float>(f, ctx);
+    const uint32_t count = read_le<uint32_t>(f, ctx);
+    for (uint32_t t = 0; t < count; ++t) {
+        const uint32_t len = read_le<uint32_t>(f, ctx);
+        std::string name(len, '\0');
+        read_exact(f, name.data(), len, ctx);
+        const uint32_t rows = read_le<uint32_t>(f, ctx), cols = read_le<uint32_t>(f, ctx);
+        std::vector<float> data(static_cast<std::size_t>(rows) * cols);
+        read_exact(f, data.data(), data.size() * sizeof(float), ctx);
+        wf.tensors[name] = Tensor::dense(rows, cols, std::move(data));
+    }
+    return wf;
+}
+
+std::size_t Model::add_gcn_layer(std::size_t in_f, std::size_t out_f, bool bias, Activation act,
+                                 InterActivation post) {
+    gcn_layers_.emplace_back(in_f, out_f, bias, act);
+    layers_.push_back({LayerEntry::Type::GCN, gcn_layers_.size() - 1, 1, false, post});
+    return layers_.size() - 1;
+}
+
+std::size_t Model::add_sage_layer(std::size_t in_f, std::size_t out_f, SAGELayer::Aggregator agg, bool bias,
+                                  Activation act, InterActivation post) {
+    sage_layers_.emplace_back(in_f, out_f, agg, bias, act);
+    layers_.push_back({LayerEntry::Type::SAGE, sage_layers_.size() - 1, 1, false, post});
+    return layers_.size() - 1;
+}
+
+std::size_t Model::add_gat_layer(std::size_t in_f, std::size_t out_f, std::size_t num_heads, bool concat,
+                                 float neg_slope, bool bias, Activation act, InterActivation post) {
+    const std::size_t idx = gat_layers_.size();
+    for (std::size_t h = 0; h < num_heads; ++h) gat_layers_.emplace_back(in_f, out_f, neg_slope, bias, act);
+    layers_.push_back({LayerEntry::Type::GAT, idx, num_heads, concat, post});
+    return layers_.size() - 1;
+}
+
+void Model::load_weights(const std::string& path) { load_weights(load_weight_file(path)); }
+
+void Model::load_weights(const WeightFile& wf) {
+    auto get = [&](const std::string& name) -> const Tensor& {
+        auto it = wf.tensors.find(name);
+        if (it == wf.tensors.end()) throw std::runtime_error("Model::load_weights: missing tensor '" + name + "'");
+        return it->second;
+    };
+    for (std::size_t li = 0; li < layers_.size(); ++li) {
+        const auto& e = layers_[li];
+        const std::string p = "layer" + std::to_string(li);
+        switch (e.type) {
+            case LayerEntry::Type::GCN: {
+                auto& l = gcn_layers_[e.start_idx];
+                l.set_weight(get(p + ".weight"));
+                if (l.has_bias()) l.set_bias(get(p + ".bias"));
+                break;
+            }
+            case LayerEntry::Type::SAGE: {
+                auto& l = sage_layers_[e.start_idx];
+                l.set_weight_neigh(get(p + ".weight_neigh"));
+                l.set_weight_self(get(p + ".weight_self"));
+                if (l.has_bias()) l.set_bias(get(p + ".bias"));
+                break;
+            }
+            case LayerEntry::Type::GAT:
+                for (std::size_t h = 0; h < e.count; ++h) {
+                    auto& l = gat_layers_[e.start_idx + h];
+                    const std::string hp = p + ".head" + std::to_string(h);
+                    l.set_weight(get(hp + ".weight"));
+                    l.set_attn_left(get(hp + ".attn_left"));
+                    l.set_attn_right(get(hp + ".attn_right"));
+                    if (l.has_bias()) l.set_bias(get(hp + ".bias"));
+                }
+                break;
+        }
+    }
+}
+
+Tensor Model::forward(const Tensor& adjacency, const Tensor& features) const {
+    if (layers_.empty()) throw std::runtime_error("Model::forward: no layers configured.");
+    bool need_norm = false, need_sl = false;
+    for (const auto& e : layers_) {
+        need_norm |= e.type == LayerEntry::Type::GCN;
+        need_sl |= e.type == LayerEntry::Type::GAT;
+    }
+    Tensor A_gcn, A_sl;
+    if (need_norm) A_gcn = gcn_norm(adjacency);
+    if (need_sl) A_sl = add_self_loops(adjacency);
+
+    Tensor H;
+    const Tensor* in = &features;
+    for (const auto& e : layers_) {
+        Tensor out;
+        switch (e.type) {
+            case LayerEntry::Type::GCN: out = gcn_layers_[e.start_idx].forward(A_gcn, *in); break;
+            case LayerEntry::Type::SAGE: out = sage_layers_[e.start_idx].forward(adjacency, *in); break;
+            case LayerEntry::Type::GAT: {
+                if (e.count == 1) {
+                    out = gat_layers_[e.start_idx].forward(A_sl, *in);
+                    break;
+                }
+                // All heads in one pass: W = [W_0 | W_1 | ...], a_l / a_r / b stacked.
+                const GATLayer& h0 = gat_layers_[e.start_idx];
+                const std::size_t heads = e.count, d = h0.out_features(), fi = h0.in_features();
+                if (in->format() != StorageFormat::Dense || in->cols() != fi || in->rows() != A_sl.rows())
+                    h0.forward(A_sl, *in);  // raises the reference's validation error
+                DevBuf W(fi * heads * d), al(heads * d), ar(heads * d), b(heads * d);
+                for (std::size_t h = 0; h < heads; ++h) {
+                    const GATLayer& L = gat_layers_[e.start_idx + h];
+                    pack(W.p, heads * d, h * d, L.weight());
+                    pack(al.p, heads * d, h * d, L.attn_left());
+                    pack(ar.p, heads * d, h * d, L.attn_right());
+                    pack(b.p, heads * d, h * d, L.bias());
+                }
+                const std::size_t ocols = e.gat_concat ? heads * d : d;
+                out = Tensor::dense_device(in->rows(), ocols);
+                check(tg_gat_layer_f32(static_cast<int64_t>(in->rows()), static_cast<int64_t>(A_sl.nnz()),
+                                       A_sl.device_row_ptr(), A_sl.device_col_ind(), in->device_data(),
+                                       static_cast<int64_t>(in->device_ld()), static_cast<int64_t>(fi),
+                                       static_cast<int64_t>(heads), static_cast<int64_t>(d), W.p, al.p, ar.p,
+                                       h0.has_bias() ? b.p : nullptr, h0.negative_slope(), e.gat_concat ? 1 : 0,
+                                       h0.activation() == Activation::ReLU ? TG_ACT_RELU : TG_ACT_NONE,
+                                       out.mutable_device_data(), static_cast<int64_t>(out.device_ld()), nullptr,
+                                       detail::mode(), stream()));
+                break;
+            }
+        }
+        if (e.post_act == InterActivation::ReLU) relu_inplace(out);
+        else if (e.post_act == InterActivation::ELU) elu_inplace(out);
+        H = std::move(out);
+        in = &H;
+    }
+    return H;
+}
+
+}  // namespace tinygnn

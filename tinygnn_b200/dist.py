@@ -30,6 +30,7 @@ Ts_r = H_r . W_self stays local, H'_r = act(mean_j Tn[j] + Ts_r[i] + b).
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 from typing import List, Optional, Tuple
 
@@ -111,14 +112,24 @@ class ShardedModel:
     column blocks (extra passes that each gather from a smaller working set).
     """
 
+    # A rank's block of a gathered operand above this size is split into
+    # column blocks (measured on B200: 2 blocks for the 119 MB F=128 operand
+    # -6% time, more blocks or smaller operands slower).
+    BLOCK_BYTES = 64 << 20
+
     def __init__(self, layers: List[Layer], n: int, comm: Comm, device, mode: str = "exact",
-                 blocks_per_rank: int = 1):
+                 blocks_per_rank="auto"):
         self.layers, self.n, self.comm, self.device, self.mode = layers, n, comm, device, mode
-        self.bpr = max(1, int(blocks_per_rank))
-        self.R, self.row0, self.row1 = row_block(n, comm.world, comm.rank, self.bpr)
+        R0 = (n + comm.world - 1) // comm.world
+        if blocks_per_rank == "auto":
+            self.bprs = [max(1, -(-(R0 * _pad4(L.W.shape[1]) * 4) // self.BLOCK_BYTES)) for L in layers]
+        else:
+            self.bprs = [max(1, int(blocks_per_rank))] * len(layers)
+        multiple = 1
+        for b in self.bprs:
+            multiple = multiple * b // math.gcd(multiple, b)
+        self.R, self.row0, self.row1 = row_block(n, comm.world, comm.rank, multiple)
         self.rows = self.row1 - self.row0
-        self.nblocks = comm.world * self.bpr
-        self.width = self.R // self.bpr
         P = comm.world
         self.full = []   # gathered operand per layer: (P*R) x pad4(F_out)
         self.outs = []
@@ -135,15 +146,18 @@ class ShardedModel:
         if self.timing is not None:
             self.timing(li, what, edge)
 
-    def splits(self, A: CSR) -> Optional[torch.Tensor]:
-        """Column-block split points of A's rows (cached on A)."""
-        if self.nblocks == 1:
+    def splits(self, A: CSR, bpr: int) -> Optional[torch.Tensor]:
+        """Column-block split points of A's rows for `bpr` blocks per rank (cached on A)."""
+        nblocks = self.comm.world * bpr
+        if nblocks == 1:
             return None
-        key = (self.nblocks, self.width)
+        key = (nblocks, self.R // bpr)
         cache = getattr(A, "_splits", None)
-        if cache is None or cache[0] != key:
-            A._splits = (key, ops.column_splits(A, self.nblocks, self.width))
-        return A._splits[1]
+        if cache is None:
+            cache = A._splits = {}
+        if key not in cache:
+            cache[key] = ops.column_splits(A, nblocks, self.R // bpr)
+        return cache[key]
 
     # The phases of a layer; forward() runs them in order.  Tests that
     # emulate several ranks in one process interleave them across shards.
@@ -188,19 +202,21 @@ class ShardedModel:
     def exchange_and_aggregate(self, li: int, A_gcn: Optional[CSR], A_raw: Optional[CSR]) -> torch.Tensor:
         """Per-block passes, each started as soon as its block has arrived."""
         A = A_gcn if self.layers[li].kind == "gcn" else A_raw
-        sp = self.splits(A)
+        bpr = self.bprs[li]
+        sp = self.splits(A, bpr)
         if sp is None:
             self.exchange(li)
             return self.aggregate(li, A_gcn, A_raw)
+        nblocks = self.comm.world * bpr
         self._mark(li, "gather", "start")
         works = [self.comm.broadcast_rows(self.full[li], self.R, src) for src in range(self.comm.world)]
         H = None
-        for q in range(self.nblocks):
-            src = q // self.bpr
+        for q in range(nblocks):
+            src = q // bpr
             if works[src] is not None and src != self.comm.rank:
                 works[src].wait()
                 works[src] = None
-            H = self._pass(li, A, sp[q], sp[q + 1], q > 0, q == self.nblocks - 1)
+            H = self._pass(li, A, sp[q], sp[q + 1], q > 0, q == nblocks - 1)
         for w in works:
             if w is not None:
                 w.wait()
