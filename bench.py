@@ -59,6 +59,8 @@ def parse():
                     help="fast: 3xTF32 tensor-core GEMMs (within fp32 tolerance); exact: bit-identical GEMMs")
     ap.add_argument("--small", action="store_true", help="a 20k-node graph (quick functional run)")
     ap.add_argument("--edges", type=int, default=0, help="override the edge count (profiling on a smaller graph)")
+    ap.add_argument("--pipeline", action="store_true",
+                    help="N > 1: per-rank async broadcasts with a gather pass per arriving block")
     ap.add_argument("--blocks-per-rank", default="auto",
                     help="column blocks per rank for the gathers: 'auto' or a count")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -302,8 +304,10 @@ def metric_name(workload):
 def config_dict(args, n, nnz):
     return {"workload": f"{args.workload}-reddit-shape" + ("-small" if args.small else ""),
             "nodes": n, "nnz": nnz, "features": FEATS, "hidden": HIDDEN, "classes": CLASSES,
-            "partition": "1-D equal row blocks; each layer's transformed rows broadcast per rank block "
-                         "(NCCL, async) with one exact gather pass per arriving column block",
+            "partition": ("1-D equal row blocks; each layer's transformed rows broadcast per rank block "
+                          "(NCCL, async) with one exact gather pass per arriving column block" if args.pipeline else
+                          "1-D equal row blocks; each layer's transformed rows exchanged by one in-place NCCL "
+                          "all-gather, then exact gather passes over column blocks"),
             "parallelism": f"row-partition x{args.gpus}",
             "l2": "inputs larger than L2 (CSR 918 MB, features 561 MB); no flush between steps",
             "mode": ("fast: 3xTF32 tcgen05 GEMMs, order-preserving fp32 gathers" if args.mode == "fast"
@@ -334,7 +338,8 @@ def run_ours(args):
     n, rp, ci, v = make_graph(args.small, dev, args.edges)
     w = make_weights(args.workload, dev)
     bpr = args.blocks_per_rank if args.blocks_per_rank == "auto" else int(args.blocks_per_rank)
-    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode, blocks_per_rank=bpr)
+    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode, blocks_per_rank=bpr,
+                         pipeline=args.pipeline)
     R, r0, r1 = model.R, model.row0, model.row1
     rows = r1 - r0
     A_raw = slice_rows(rp, ci, v, r0, r1, n)
@@ -386,26 +391,23 @@ def run_ours(args):
     gather_ms = phase_ms((0, "gather"))
     phases = {f"layer{li}_{what}": phase_ms((li, what)) for li in range(2)
               for what in ("gemm", "exchange", "gather")}
+    phases = {k: v for k, v in phases.items() if v is not None}
+    rank_phases = [phases]
+    if world > 1:  # every rank's phase times (the exchange absorbs imbalance)
+        import torch.distributed as dist
+        rank_phases = [None] * world
+        dist.all_gather_object(rank_phases, phases)
     per_launch = launches / (args.steps + args.warmup)
 
     # e2e: host inputs -> device -> gcn_norm -> forward -> logits to host
     pin = lambda t: t.cpu().pin_memory()  # noqa: E731
     h_rp, h_ci, h_v, h_X = pin(A_raw.row_ptr), pin(A_raw.col_ind), pin(A_raw.values), pin(X)
     h_out = torch.empty((rows, CLASSES), dtype=torch.float32).pin_memory()
-    d_rp, d_ci, d_v = torch.empty_like(A_raw.row_ptr), torch.empty_like(A_raw.col_ind), torch.empty_like(A_raw.values)
-    d_X = torch.zeros_like(Xp)[:, :FEATS]
-    dis_all = torch.zeros(R * world, dtype=torch.float32, device=dev)
+    e2e_bufs = {}
 
     def e2e_step():
-        d_rp.copy_(h_rp, non_blocking=True)
-        d_ci.copy_(h_ci, non_blocking=True)
-        d_v.copy_(h_v, non_blocking=True)
-        d_X.copy_(h_X, non_blocking=True)
-        A = tg.CSR(rows, n, d_rp, d_ci, d_v)
-        An = gcn_norm_rows(A, r0, R, comm, dis_all) if args.workload == "gcn" else None
-        out = model.forward(An, A, d_X)
-        h_out.copy_(out, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        # the public call: host CSR rows + feature rows in, host logits out
+        model.forward_from_host(h_rp, h_ci, h_v, h_X, h_out, e2e_bufs)
 
     e2e_ms = None if args.no_e2e else time_steps(e2e_step, args.steps, min(args.warmup, 3), world)
     clocks = sampler.stop()
@@ -464,6 +466,7 @@ def run_ours(args):
                     "note": "rank 0's bytes; every rank moves its own row block"},
             "clocks": clocks, "gpu_launches": int(per_launch * args.steps),
             "phase_ms": phases,
+            "phase_ms_per_rank": rank_phases if world > 1 else None,
         }
         print(json.dumps(line))
     if world > 1:

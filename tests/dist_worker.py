@@ -36,19 +36,24 @@ def main() -> int:
     R, r0, r1 = row_block(n, world, rank)
     A = slice_rows(rp, ci, v, r0, r1, n)
     An = gcn_norm_rows(A, r0, R, comm)
-    model = ShardedModel(layers, n, comm, dev, mode="exact")
-    out = model.forward(An, A, X[r0:r1].contiguous())
-    parts = [torch.zeros((R, 9), device=dev) for _ in range(world)]
-    mine = torch.zeros((R, 9), device=dev)
-    mine[:r1 - r0] = out
-    dist.all_gather(parts, mine)
     ok = True
+    ref = None
     if rank == 0:
-        got = torch.cat(parts, 0)[:n]
         full = tg.CSR(n, n, rp, ci, v)
         one = ShardedModel(layers, n, Comm(1, 0), dev, mode="exact")
-        ref = one.forward(gcn_norm_rows(full, 0, n, Comm(1, 0)), full, X)
-        ok = bool(torch.equal(got, ref))
+        ref = one.forward(gcn_norm_rows(full, 0, n, Comm(1, 0)), full, X).clone()
+    for pipeline in (False, True):  # one all-gather / per-block broadcasts
+        model = ShardedModel(layers, n, comm, dev, mode="exact", pipeline=pipeline)
+        out = model.forward(An, A, X[r0:r1].contiguous())
+        parts = [torch.zeros((R, 9), device=dev) for _ in range(world)]
+        mine = torch.zeros((R, 9), device=dev)
+        mine[:r1 - r0] = out
+        dist.all_gather(parts, mine)
+        if rank == 0:
+            same = bool(torch.equal(torch.cat(parts, 0)[:n], ref))
+            print(f"pipeline={pipeline} same={same}", flush=True)
+            ok = ok and same
+    if rank == 0:
         print(f"world={world} bit-identical={ok}", flush=True)
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.broadcast(flag, 0)

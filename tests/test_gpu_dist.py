@@ -88,6 +88,36 @@ def test_single_gpu_column_blocks_are_bit_identical(tg, workload, bpr):
     assert_bits_equal(blk.cpu().numpy(), one.cpu().numpy(), f"{workload} {bpr} blocks")
 
 
+@pytest.mark.parametrize("workload,mode,blocks", [("gcn", "exact", 8), ("gcn", "fast", 5), ("sage", "fast", 1)])
+def test_forward_from_host_equals_resident_forward(tg, workload, mode, blocks):
+    """The pipelined host-input call (uploads overlapped with gcn_norm and the
+    per-block layer-1 passes) returns exactly the resident forward's logits."""
+    from tinygnn_b200.dist import Comm, Layer, ShardedModel, gcn_norm_rows
+    rng, rp, ci, v, X = _graph(seed=11)
+    n = rp.size - 1
+    W0 = torch.as_tensor((rng.standard_normal((40, 32)) * 0.2).astype(np.float32)).cuda()
+    W1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
+    S0 = torch.as_tensor((rng.standard_normal((40, 32)) * 0.2).astype(np.float32)).cuda()
+    S1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
+    b0 = torch.as_tensor((rng.standard_normal(32) * 0.1).astype(np.float32)).cuda()
+    sage = workload == "sage"
+    layers = [Layer(workload, W0, b0, "relu", S0 if sage else None),
+              Layer(workload, W1, None, None, S1 if sage else None)]
+    model = ShardedModel(layers, n, Comm(1, 0), "cuda", mode=mode)
+    A = tg.CSR.from_numpy(rp, ci, v)
+    Xd = torch.zeros((n, 40), device="cuda")
+    Xd[:] = torch.as_tensor(X).cuda()
+    An = gcn_norm_rows(A, 0, n, Comm(1, 0)) if not sage else None
+    ref = model.forward(An, A, Xd).cpu().numpy().copy()
+    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+    h_out = torch.empty((n, 11)).pin_memory()
+    bufs = {}
+    for _ in range(2):  # buffers reused on the second call
+        model.forward_from_host(pin(A.row_ptr), pin(A.col_ind), pin(A.values), pin(Xd), h_out, bufs,
+                                feature_blocks=blocks)
+        assert_bits_equal(h_out.numpy(), ref, f"{workload} {mode} from host")
+
+
 @pytest.mark.parametrize("workload,world", [("gcn", 2), ("gcn", 4), ("sage", 3), ("gcn", 8)])
 def test_sharded_forward_equals_unpartitioned(tg, workload, world):
     from tinygnn_b200.dist import Layer, ShardedModel, gcn_norm_rows, row_block, slice_rows

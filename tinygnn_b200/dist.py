@@ -118,8 +118,12 @@ class ShardedModel:
     BLOCK_BYTES = 64 << 20
 
     def __init__(self, layers: List[Layer], n: int, comm: Comm, device, mode: str = "exact",
-                 blocks_per_rank="auto"):
+                 blocks_per_rank="auto", pipeline: bool = False):
         self.layers, self.n, self.comm, self.device, self.mode = layers, n, comm, device, mode
+        # pipeline: per-rank async broadcasts with one gather pass per arriving
+        # block; otherwise one all-gather, then the passes (measured on 2 B200:
+        # one in-place all-gather moves ~450 GB/s, P broadcasts ~35 % slower).
+        self.pipeline = pipeline
         R0 = (n + comm.world - 1) // comm.world
         if blocks_per_rank == "auto":
             self.bprs = [max(1, -(-(R0 * _pad4(L.W.shape[1]) * 4) // self.BLOCK_BYTES)) for L in layers]
@@ -203,6 +207,9 @@ class ShardedModel:
         """Per-block passes, each started as soon as its block has arrived."""
         A = A_gcn if self.layers[li].kind == "gcn" else A_raw
         bpr = self.bprs[li]
+        if self.comm.world > 1 and not self.pipeline:
+            self.exchange(li)
+            return self.aggregate(li, A_gcn, A_raw)
         sp = self.splits(A, bpr)
         if sp is None:
             self.exchange(li)
@@ -222,6 +229,79 @@ class ShardedModel:
                 w.wait()
         self._mark(li, "gather", "end")
         return H
+
+    def forward_from_host(self, h_rp: torch.Tensor, h_ci: torch.Tensor, h_v: torch.Tensor, h_X: torch.Tensor,
+                          h_out: torch.Tensor, bufs: dict, feature_blocks: int = 8) -> torch.Tensor:
+        """The whole call from host inputs: raw CSR rows + feature rows (pinned
+        host tensors of this rank) in, logits (pinned host tensor) out.
+
+        Uploads are queued first on a copy stream (CSR, then the features in
+        row blocks); gcn_norm runs as soon as the CSR is in, while the
+        features stream; on one GPU the first layer's GEMM and exact gather
+        pass for feature block q start when block q has landed.  ``bufs``
+        holds the device buffers across calls (filled on first use).
+        """
+        dev = self.device
+        cur = torch.cuda.current_stream()
+        cp = bufs.get("stream")
+        if cp is None:
+            cp = bufs["stream"] = torch.cuda.Stream(device=dev)
+            bufs["rp"] = torch.empty_like(h_rp, device=dev)
+            bufs["ci"] = torch.empty_like(h_ci, device=dev)
+            bufs["v"] = torch.empty_like(h_v, device=dev)
+            bufs["X"] = torch.zeros((self.rows, _pad4(h_X.shape[1])), dtype=torch.float32, device=dev)
+            bufs["dis"] = torch.zeros(self.R * self.comm.world, dtype=torch.float32, device=dev)
+        d_rp, d_ci, d_v, d_X = bufs["rp"], bufs["ci"], bufs["v"], bufs["X"][:, :h_X.shape[1]]
+        single = self.comm.world == 1 and self.layers[0].kind == "gcn"
+        nb = max(1, feature_blocks) if single else 1
+        width = (self.rows + nb - 1) // nb
+        x_ready = []
+        cp.wait_stream(cur)
+        with torch.cuda.stream(cp):
+            d_rp.copy_(h_rp, non_blocking=True)
+            d_ci.copy_(h_ci, non_blocking=True)
+            d_v.copy_(h_v, non_blocking=True)
+            csr_ready = torch.cuda.Event()
+            csr_ready.record(cp)
+            for q in range(nb):
+                a, b = q * width, min(self.rows, (q + 1) * width)
+                if a < b:
+                    d_X[a:b].copy_(h_X[a:b], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(cp)
+                x_ready.append(ev)
+        cur.wait_event(csr_ready)
+        A = CSR(self.rows, self.n, d_rp, d_ci, d_v)
+        A_gcn = (gcn_norm_rows(A, self.row0, self.R, self.comm, bufs["dis"])
+                 if any(L.kind == "gcn" for L in self.layers) else None)
+        if single and nb > 1:
+            # Layer 1 per feature block: GEMM of block q's rows, then the gather
+            # pass over the columns of block q (exact: passes in column order).
+            L = self.layers[0]
+            fo = L.W.shape[1]
+            A_gcn.order = ops.degree_order(A_gcn)
+            sp = ops.column_splits(A_gcn, nb, width)
+            B = self.full[0][:self.n, :fo]
+            for q in range(nb):
+                a, b = q * width, min(self.rows, (q + 1) * width)
+                cur.wait_event(x_ready[q])
+                if a < b:
+                    ops.matmul(d_X[a:b], L.W, out=self.full[0][a:b, :fo], mode=self.mode)
+                ops.spmm_segment(A_gcn, B, sp[q], sp[q + 1], self.outs[0], q > 0, q == nb - 1, bias=L.b,
+                                 act=L.act)
+            H = self.outs[0]
+            first = 1
+        else:
+            for ev in x_ready:
+                cur.wait_event(ev)
+            H, first = d_X, 0
+        for li in range(first, len(self.layers)):
+            self.transform(li, H)
+            H = self.exchange_and_aggregate(li, A_gcn, A)
+        ops.log_softmax_(H)
+        h_out.copy_(H, non_blocking=True)
+        cur.synchronize()
+        return h_out
 
     def forward(self, A_gcn: Optional[CSR], A_raw: Optional[CSR], X: torch.Tensor,
                 log_softmax: bool = True) -> torch.Tensor:
