@@ -325,9 +325,11 @@ TG_API tg_status tg_gat_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
                                   float* out, int64_t ldo, const int32_t* row_order,
                                   int32_t mode, void* stream);
 
-/* Reads and clears the device error word of the tensor-core GEMM (FAST mode):
- * TG_ERR_TIMEOUT when one of its bounded pipeline waits ran out since the
- * last call (that GEMM's output is then invalid).  Synchronises `stream`. */
+/* Reads and clears the device error words of the pipelined kernels (the
+ * tensor-core GEMM of FAST mode and the heavy-row gather used by every
+ * degree-ordered spmm / SAGE aggregation): TG_ERR_TIMEOUT when one of their
+ * bounded pipeline waits ran out since the last call (that call's output is
+ * then invalid).  Synchronises `stream`. */
 TG_API tg_status tg_take_device_error(void* stream);
 
 #ifdef __cplusplus

@@ -68,6 +68,19 @@ inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 // Number of SMs of the current device (cached per device).
 int num_sms();
 
+// ── Side stream ──────────────────────────────────────────────────────────
+// A high-priority stream per (host thread, device) with two events, for
+// kernels that run beside the caller's stream inside one call: record `fork`
+// on the caller's stream, make the side stream wait for it, launch there,
+// record `join`, and make the caller's stream wait for `join` before it
+// continues -- the call stays ordered on the caller's stream (and captures
+// into a CUDA graph as a fork/join).
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+SideStream& side_stream();
+
 // ── Stream-ordered scratch ────────────────────────────────────────────────
 // Scratch buffers come from the device's default memory pool with a high
 // release threshold, so repeated calls reuse the same pages.

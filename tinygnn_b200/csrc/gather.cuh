@@ -50,6 +50,10 @@ struct GatherArgs {
     const int32_t* seg_hi = nullptr;
     bool carry = false;
     bool last = true;
+    // Heavy rows: slots [0, *heavy_count) of `order` are produced by the
+    // heavy-row kernel and skipped by the sub-warp kernel (set by
+    // gather_rows, never by callers; NULL = none).
+    const int32_t* heavy_count = nullptr;
 };
 
 // Queues the gather on `s`.

@@ -95,6 +95,72 @@ __device__ __forceinline__ float reduce_step(float acc, float w, float h, bool a
     }
 }
 
+// Accumulator start for the features [fo, fo+VEC) of `row`: the chain stored
+// by the previous column-block pass (carry) or the reduction's identity.
+template <int VEC, bool CVEC>
+__device__ __forceinline__ void start_acc(const GatherArgs& a, int64_t row, int64_t fo, bool live, bool full,
+                                          float init, float (&acc)[VEC]) {
+    if (a.carry && live) {
+        if (CVEC && full) {
+            ldv_plain<VEC>(a.C + row * a.ldc + fo, acc);
+        } else {
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) acc[k] = (fo + k < a.F) ? a.C[row * a.ldc + fo + k] : init;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc[k] = init;
+    }
+}
+
+// Stores features [fo, fo+VEC) of `row`: the raw accumulator on an
+// intermediate pass, else (1/deg) -> (+ self row) -> (+ bias) -> activation,
+// one rounding each.
+template <int OP, int VEC, bool CVEC>
+__device__ __forceinline__ void finish_acc(const GatherArgs& a, int64_t row, int64_t fo, bool full, int32_t deg,
+                                           const float (&acc)[VEC]) {
+    if (!a.last) {
+        if (CVEC && full) {
+            stv<VEC>(a.C + row * a.ldc + fo, acc);
+        } else {
+#pragma unroll
+            for (int k = 0; k < VEC; ++k)
+                if (fo + k < a.F) a.C[row * a.ldc + fo + k] = acc[k];
+        }
+        return;
+    }
+    const float inv_deg = (OP == GATHER_SUM && a.mean && deg > 0) ? __fdiv_rn(1.0f, static_cast<float>(deg)) : 1.0f;
+    const bool vec_io = CVEC && full;
+    float x[VEC], sv[VEC], bv[VEC];
+    if (vec_io) {
+        if (a.self) ldv_plain<VEC>(a.self + row * a.lds + fo, sv);
+        if (a.bias) ldv_plain<VEC>(a.bias + fo, bv);
+    } else {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+            const bool in = fo + k < a.F;
+            sv[k] = (a.self && in) ? a.self[row * a.lds + fo + k] : 0.0f;
+            bv[k] = (a.bias && in) ? a.bias[fo + k] : 0.0f;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+        float v = acc[k];
+        if (OP == GATHER_MAX && deg == 0) v = 0.0f;
+        if (OP == GATHER_SUM && a.mean && deg > 0) v = __fmul_rn(v, inv_deg);
+        if (a.self) v = __fadd_rn(v, sv[k]);
+        if (a.bias) v = __fadd_rn(v, bv[k]);
+        x[k] = apply_act(a.act, v, a.alpha);
+    }
+    if (vec_io) {
+        stv<VEC>(a.C + row * a.ldc + fo, x);
+    } else {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k)
+            if (fo + k < a.F) a.C[row * a.ldc + fo + k] = x[k];
+    }
+}
+
 // VEC: floats per load; LPR: lanes per row; SPL: vectors per lane;
 // OP: GATHER_SUM / GATHER_MAX; U: gathered rows in flight per batch;
 // CVEC: C, self and bias use VEC-wide accesses (else element accesses).
@@ -108,6 +174,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherArgs a) {
 
     const int64_t slot = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW + sub;
     if (slot >= a.M) return;  // whole sub-warps leave together
+    if (a.heavy_count && slot < *a.heavy_count) return;  // the heavy-row kernel's slots
     const uint64_t keep = policy_keep(), stream = policy_stream();
     const int64_t row = a.order ? static_cast<int64_t>(ld_i32(a.order + slot, stream)) : slot;
 
@@ -124,19 +191,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherArgs a) {
     float acc[SPL][VEC];
     const float init = (OP == GATHER_SUM) ? 0.0f : -INFINITY;
 #pragma unroll
-    for (int s = 0; s < SPL; ++s) {
-        if (a.carry && live[s]) {  // continue the chain stored by the previous pass
-            if (CVEC && full[s]) {
-                ldv_plain<VEC>(a.C + row * a.ldc + fo[s], acc[s]);
-            } else {
-#pragma unroll
-                for (int k = 0; k < VEC; ++k) acc[s][k] = (fo[s] + k < a.F) ? a.C[row * a.ldc + fo[s] + k] : init;
-            }
-        } else {
-#pragma unroll
-            for (int k = 0; k < VEC; ++k) acc[s][k] = init;
-        }
-    }
+    for (int s = 0; s < SPL; ++s) start_acc<VEC, CVEC>(a, row, fo[s], live[s], full[s], init, acc[s]);
 
     bool avx[SPL][VEC];
 #pragma unroll
@@ -203,55 +258,10 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherArgs a) {
         }
     }
 
-    if (!a.last) {  // intermediate pass: store the raw accumulator
-#pragma unroll
-        for (int s = 0; s < SPL; ++s) {
-            if (!live[s]) continue;
-            if (CVEC && full[s]) {
-                stv<VEC>(a.C + row * a.ldc + fo[s], acc[s]);
-            } else {
-#pragma unroll
-                for (int k = 0; k < VEC; ++k)
-                    if (fo[s] + k < a.F) a.C[row * a.ldc + fo[s] + k] = acc[s][k];
-            }
-        }
-        return;
-    }
     const int32_t deg = row_end - row_begin;  // the whole row, whichever segment this pass covered
-    const float inv_deg = (OP == GATHER_SUM && a.mean && deg > 0) ? __fdiv_rn(1.0f, static_cast<float>(deg)) : 1.0f;
 #pragma unroll
-    for (int s = 0; s < SPL; ++s) {
-        if (!live[s]) continue;
-        const bool vec_io = CVEC && full[s];
-        float x[VEC], sv[VEC], bv[VEC];
-        if (vec_io) {
-            if (a.self) ldv_plain<VEC>(a.self + row * a.lds + fo[s], sv);
-            if (a.bias) ldv_plain<VEC>(a.bias + fo[s], bv);
-        } else {
-#pragma unroll
-            for (int k = 0; k < VEC; ++k) {
-                const bool in = fo[s] + k < a.F;
-                sv[k] = (a.self && in) ? a.self[row * a.lds + fo[s] + k] : 0.0f;
-                bv[k] = (a.bias && in) ? a.bias[fo[s] + k] : 0.0f;
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) {
-            float v = acc[s][k];
-            if (OP == GATHER_MAX && deg == 0) v = 0.0f;
-            if (OP == GATHER_SUM && a.mean && deg > 0) v = __fmul_rn(v, inv_deg);
-            if (a.self) v = __fadd_rn(v, sv[k]);
-            if (a.bias) v = __fadd_rn(v, bv[k]);
-            x[k] = apply_act(a.act, v, a.alpha);
-        }
-        if (vec_io) {
-            stv<VEC>(a.C + row * a.ldc + fo[s], x);
-        } else {
-#pragma unroll
-            for (int k = 0; k < VEC; ++k)
-                if (fo[s] + k < a.F) a.C[row * a.ldc + fo[s] + k] = x[k];
-        }
-    }
+    for (int s = 0; s < SPL; ++s)
+        if (live[s]) finish_acc<OP, VEC, CVEC>(a, row, fo[s], full[s], deg, acc[s]);
 }
 
 }  // namespace gk

@@ -184,6 +184,7 @@ void gemm_exact(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
 
 bool gemm_tc_supported(int64_t N, int64_t K, const float* A, int64_t lda);
 int gemm_tc_take_error(cudaStream_t s);
+int gather_take_error(cudaStream_t s);
 void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
              int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s);
 
@@ -233,8 +234,12 @@ TG_API tg_status tg_take_device_error(void* stream) {
     return guard([&] {
         require_device();
         const int code = gemm_tc_take_error(as_stream(stream));
+        const int gcode = gather_take_error(as_stream(stream));
         if (code)
             fail(TG_ERR_TIMEOUT, "a tensor-core GEMM pipeline wait ran out (stage code " + std::to_string(code) +
+                                     "); its output is invalid");
+        if (gcode)
+            fail(TG_ERR_TIMEOUT, "a heavy-row gather pipeline wait ran out (code " + std::to_string(gcode) +
                                      "); its output is invalid");
     });
 }

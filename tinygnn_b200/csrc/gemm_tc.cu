@@ -29,6 +29,7 @@
 #include <mutex>
 
 #include "launch.cuh"
+#include "mbarrier.cuh"
 
 namespace tg {
 
@@ -36,7 +37,6 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 32;       // fp32 per 128-byte swizzled row
-constexpr long kWaitLimit = 1L << 24;  // ~1 s of polling with back-off
 
 // Pipeline depth from the per-stage footprint (A, Al, Bh, Bl) within ~200 KB.
 constexpr int stages_for(int BN) {
@@ -45,43 +45,15 @@ constexpr int stages_for(int BN) {
 
 __device__ int g_tc_error = 0;  // first timeout code seen (0 = none)
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
+using mb::smem_u32;
 
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) { mb::init(bar, count); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) { mb::arrive_expect_tx(bar, bytes); }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) { mb::arrive(bar); }
 
 // Bounded wait; false (and the error word set) when it runs out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
-    for (long i = 0; i < kWaitLimit; ++i) {
-        if (mbar_try(bar, parity)) return true;
-        if (i > 32) __nanosleep(64);
-    }
-    atomicCAS(&g_tc_error, 0, code);
-    return false;
+    return mb::wait(bar, parity, &g_tc_error, code);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {

@@ -38,6 +38,25 @@ int num_sms() {
     return g_sms[dev];
 }
 
+SideStream& side_stream() {
+    // Per host thread, so concurrent callers never share the events; created
+    // on first use and kept for the thread's life (never destroyed: at exit
+    // the CUDA context may already be gone).
+    thread_local std::vector<SideStream*> per_dev;
+    const int dev = current_device();
+    if (static_cast<int>(per_dev.size()) <= dev) per_dev.resize(dev + 1, nullptr);
+    if (!per_dev[dev]) {
+        auto* ss = new SideStream();
+        int least = 0, greatest = 0;
+        TG_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+        TG_CUDA(cudaStreamCreateWithPriority(&ss->s, cudaStreamNonBlocking, greatest));
+        TG_CUDA(cudaEventCreateWithFlags(&ss->fork, cudaEventDisableTiming));
+        TG_CUDA(cudaEventCreateWithFlags(&ss->join, cudaEventDisableTiming));
+        per_dev[dev] = ss;
+    }
+    return *per_dev[dev];
+}
+
 // The default pool of each device keeps freed blocks (release threshold =
 // max), so scratch reuse across calls costs no new mappings.
 static void ensure_pool(int dev) {

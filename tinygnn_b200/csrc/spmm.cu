@@ -11,9 +11,13 @@
 //  spmm (nnz*(4 + 4F) + ... without values).
 // ============================================================================
 #include <algorithm>
+#include <cstdlib>
 #include <memory>
+#include <mutex>
+#include <vector>
 
 #include "gather.cuh"
+#include "gather_heavy.cuh"
 #include "gather_kernel.cuh"
 #include "launch.cuh"
 
@@ -64,9 +68,103 @@ void dispatch_cvec(const GatherArgs& a, cudaStream_t s) {
     else dispatch_lpr<VEC, false>(a, s);
 }
 
+// ── Heavy rows ───────────────────────────────────────────────────────────
+// The first slots of a schedule whose rows are long enough to be the
+// launch's critical path go to the heavy-row kernel (gather_heavy.cuh) on
+// the side stream, beside the sub-warp kernel.  heavy_prefix_kernel counts
+// them on the device (threshold from the nnz) among the first kHeavyScan
+// slots.  TINYGNN_B200_HEAVY_MIN_LEN sets a fixed threshold instead (a
+// negative value below -1 turns the heavy kernel off).
+constexpr int64_t kHeavyScan = 16384;
+constexpr size_t kHeavySmemBudget = 100 * 1024;  // two CTAs per SM
+
+__device__ int g_gather_error = 0;  // first heavy-kernel timeout code (0 = none)
+
+// -1: threshold from the nnz; >= 0: fixed; < -1: heavy kernel off.
+int32_t heavy_min_len() {
+    static const int32_t v = [] {
+        const char* e = std::getenv("TINYGNN_B200_HEAVY_MIN_LEN");
+        return e ? static_cast<int32_t>(std::atoi(e)) : -1;
+    }();
+    return v;
+}
+
+int* gather_error_word() {
+    static std::mutex mu;
+    static std::vector<int*> words;
+    int dev = 0;
+    TG_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    if (static_cast<int>(words.size()) <= dev) words.resize(dev + 1, nullptr);
+    if (!words[dev]) TG_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&words[dev]), g_gather_error));
+    return words[dev];
+}
+
+template <int VEC, int OP, bool CVEC>
+void launch_heavy_t(const GatherArgs& a, dim3 grid, int K, int bpe, cudaStream_t s) {
+    auto kern = gk::gather_heavy_kernel<VEC, OP, CVEC>;
+    const size_t smem = gk::heavy_smem_bytes(K, bpe);
+    TG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    launch("gather_heavy", kern, grid, dim3(gk::kHeavyThreads), smem, s, a, K, bpe, gather_error_word());
+}
+
+template <int VEC>
+void launch_heavy_vec(const GatherArgs& a, cudaStream_t s) {
+    const int64_t width = static_cast<int64_t>(gk::kHeavyConsumers) * VEC;  // features per pass
+    const int64_t passes = ceil_div(a.F, width);
+    const int bpe = static_cast<int>(std::min<int64_t>(width, (a.F + 3) / 4 * 4) * 4);
+    const int K = static_cast<int>(
+        std::max<size_t>(2, std::min<size_t>(16, kHeavySmemBudget / (gk::kHeavyG * (bpe + 4)))));
+    const int64_t ctas = std::min<int64_t>(std::min(kHeavyScan, a.M), 2 * static_cast<int64_t>(num_sms()));
+    const dim3 grid(static_cast<unsigned>(ctas), static_cast<unsigned>(passes));
+    bool cvec = a.ldc % VEC == 0 && aligned(a.C, 4 * VEC);
+    if (a.self) cvec = cvec && a.lds % VEC == 0 && aligned(a.self, 4 * VEC);
+    if (a.bias) cvec = cvec && aligned(a.bias, 4 * VEC);
+    if (a.op == GATHER_SUM) {
+        if (cvec) launch_heavy_t<VEC, GATHER_SUM, true>(a, grid, K, bpe, s);
+        else launch_heavy_t<VEC, GATHER_SUM, false>(a, grid, K, bpe, s);
+    } else {
+        if (cvec) launch_heavy_t<VEC, GATHER_MAX, true>(a, grid, K, bpe, s);
+        else launch_heavy_t<VEC, GATHER_MAX, false>(a, grid, K, bpe, s);
+    }
+}
+
+void launch_heavy(const GatherArgs& a, cudaStream_t s) {
+    if (a.F <= gk::kHeavyConsumers) launch_heavy_vec<1>(a, s);
+    else if (a.F <= 2 * gk::kHeavyConsumers) launch_heavy_vec<2>(a, s);
+    else launch_heavy_vec<4>(a, s);
+}
+
+void dispatch_light(const GatherArgs& a, cudaStream_t s) {
+    // Load width: the widest vector dividing B's leading dimension with B
+    // aligned, and dividing F unless B's rows are padded; narrower when it
+    // would leave fewer than 8 vectors per row.
+    auto ok = [&](int v) {
+        if (a.F % v && !a.b_padded) return false;
+        return a.ldb % v == 0 && aligned(a.B, 4 * v);
+    };
+    int vec = 4;
+    while (vec > 1 && (!ok(vec) || ceil_div(a.F, vec) < 8)) vec /= 2;
+    if (vec == 4) dispatch_cvec<4>(a, s);
+    else if (vec == 2) dispatch_cvec<2>(a, s);
+    else dispatch_cvec<1>(a, s);
+}
+
 }  // namespace
 
 void csr_degree_order(int64_t M, const int32_t* rp, int32_t* out, cudaStream_t s);
+
+// Reads and clears the heavy-row kernel's error word (synchronises `s`).
+int gather_take_error(cudaStream_t s) {
+    int h = 0;
+    TG_CUDA(cudaStreamSynchronize(s));
+    TG_CUDA(cudaMemcpyFromSymbol(&h, g_gather_error, sizeof(int)));
+    if (h) {
+        const int zero = 0;
+        TG_CUDA(cudaMemcpyToSymbol(g_gather_error, &zero, sizeof(int)));
+    }
+    return h;
+}
 
 void gather_rows(const GatherArgs& args, cudaStream_t s) {
     if (args.M == 0 || args.F == 0) return;
@@ -80,18 +178,25 @@ void gather_rows(const GatherArgs& args, cudaStream_t s) {
         csr_degree_order(a.M, a.rp, order->p, s);
         a.order = order->p;
     }
-    // Load width: the widest vector dividing B's leading dimension with B
-    // aligned, and dividing F unless B's rows are padded; narrower when it
-    // would leave fewer than 8 vectors per row.
-    auto ok = [&](int v) {
-        if (a.F % v && !a.b_padded) return false;
-        return a.ldb % v == 0 && aligned(a.B, 4 * v);
-    };
-    int vec = 4;
-    while (vec > 1 && (!ok(vec) || ceil_div(a.F, vec) < 8)) vec /= 2;
-    if (vec == 4) dispatch_cvec<4>(a, s);
-    else if (vec == 2) dispatch_cvec<2>(a, s);
-    else dispatch_cvec<1>(a, s);
+    // Long rows go to the heavy-row kernel on the side stream, launched
+    // first so its CTAs are placed before the sub-warp kernel's.
+    const int32_t minlen = heavy_min_len();
+    const bool heavy = a.order && minlen >= -1 && a.ldb % 4 == 0 && aligned(a.B, 16);
+    SideStream* side = nullptr;
+    std::unique_ptr<Scratch<int32_t>> count;
+    if (heavy) {
+        count.reset(new Scratch<int32_t>(1, s));
+        launch("heavy_prefix", gk::heavy_prefix_kernel, dim3(1), dim3(gk::kHeavyScanThreads), 0, s, a.M, a.rp,
+               a.order, std::min(kHeavyScan, a.M), minlen, count->p);
+        a.heavy_count = count->p;
+        side = &side_stream();
+        TG_CUDA(cudaEventRecord(side->fork, s));
+        TG_CUDA(cudaStreamWaitEvent(side->s, side->fork, 0));
+        launch_heavy(a, side->s);
+        TG_CUDA(cudaEventRecord(side->join, side->s));
+    }
+    dispatch_light(a, s);
+    if (side) TG_CUDA(cudaStreamWaitEvent(s, side->join, 0));
 }
 
 // ── Degree order: a stable bucket sort of rows by decreasing length ─────────
