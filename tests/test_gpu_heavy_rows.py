@@ -2,7 +2,7 @@
 
 The leading slots of a degree schedule whose rows have at least
 max(1023, ~nnz/16384) entries (1023 for these graphs) are produced by the
-heavy-row kernel (bulk copies into a shared-memory ring) on a side stream,
+heavy-row kernel (async copies into a shared-memory ring) on a side stream,
 the rest by the sub-warp kernel.  Every
 result must be bit-identical to the oracle's sequential chain, whichever
 kernel produced a row: rows right at the threshold (1022 / 1023 / 1024
@@ -58,7 +58,7 @@ def test_spmm_hub_rows_vs_oracle(tg, F):
     n = rp.size - 1
     A = tg.CSR.from_numpy(rp, ci, v)
     Fp = (F + 3) // 4 * 4
-    Bbuf = torch.zeros((n, Fp), device="cuda")  # ldb % 4 == 0: the heavy kernel's bulk copies apply
+    Bbuf = torch.zeros((n, Fp), device="cuda")  # ldb % 4 == 0: the heavy kernel's 16-byte copies apply
     B = rng.standard_normal((n, F)).astype(np.float32)
     Bbuf[:, :F] = torch.as_tensor(B).cuda()
     ref = P.spmm(rp, ci, v, B)

@@ -64,9 +64,9 @@ __device__ __forceinline__ bool try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, int* err, int code) {
     if (try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    for (int i = 0;; ++i) {
+    for (uint32_t i = 1;; ++i) {
         if (try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > kWaitNs) break;
+        if ((i & 15) == 0 && global_ns() - t0 > kWaitNs) break;  // the timer read is not free
         if (i > 32) __nanosleep(64);
     }
     atomicCAS(err, 0, code);
@@ -81,6 +81,20 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
         ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
+}
+
+// 16-byte global -> shared async copy through the load/store units (L1
+// bypassed, L2 policy hint); both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint64_t policy) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;"
+                 ::"r"(smem_u32(dst)), "l"(src), "l"(policy)
+                 : "memory");
+}
+
+// One arrival on `bar` once every cp.async this thread issued so far has
+// landed (counts against the barrier's expected arrivals: no increment).
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 }  // namespace mb

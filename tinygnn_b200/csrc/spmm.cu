@@ -100,39 +100,24 @@ int* gather_error_word() {
     return words[dev];
 }
 
-template <int VEC, int OP, bool CVEC>
+template <int OP>
 void launch_heavy_t(const GatherArgs& a, dim3 grid, int K, int bpe, cudaStream_t s) {
-    auto kern = gk::gather_heavy_kernel<VEC, OP, CVEC>;
+    auto kern = gk::gather_heavy_kernel<OP>;
     const size_t smem = gk::heavy_smem_bytes(K, bpe);
     TG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
     launch("gather_heavy", kern, grid, dim3(gk::kHeavyThreads), smem, s, a, K, bpe, gather_error_word());
 }
 
-template <int VEC>
-void launch_heavy_vec(const GatherArgs& a, cudaStream_t s) {
-    const int64_t width = static_cast<int64_t>(gk::kHeavyConsumers) * VEC;  // features per pass
+void launch_heavy(const GatherArgs& a, cudaStream_t s) {
+    const int64_t width = gk::kHeavyConsumers;  // features per pass (one per consumer thread)
     const int64_t passes = ceil_div(a.F, width);
     const int bpe = static_cast<int>(std::min<int64_t>(width, (a.F + 3) / 4 * 4) * 4);
-    const int K = static_cast<int>(
-        std::max<size_t>(2, std::min<size_t>(16, kHeavySmemBudget / (gk::kHeavyG * (bpe + 4)))));
+    const size_t stage = static_cast<size_t>(gk::kHeavyG) * (bpe + 4) + sizeof(gk::HeavyDesc);
+    const int K = static_cast<int>(std::max<size_t>(2, std::min<size_t>(16, kHeavySmemBudget / stage)));
     const int64_t ctas = std::min<int64_t>(std::min(kHeavyScan, a.M), 2 * static_cast<int64_t>(num_sms()));
     const dim3 grid(static_cast<unsigned>(ctas), static_cast<unsigned>(passes));
-    bool cvec = a.ldc % VEC == 0 && aligned(a.C, 4 * VEC);
-    if (a.self) cvec = cvec && a.lds % VEC == 0 && aligned(a.self, 4 * VEC);
-    if (a.bias) cvec = cvec && aligned(a.bias, 4 * VEC);
-    if (a.op == GATHER_SUM) {
-        if (cvec) launch_heavy_t<VEC, GATHER_SUM, true>(a, grid, K, bpe, s);
-        else launch_heavy_t<VEC, GATHER_SUM, false>(a, grid, K, bpe, s);
-    } else {
-        if (cvec) launch_heavy_t<VEC, GATHER_MAX, true>(a, grid, K, bpe, s);
-        else launch_heavy_t<VEC, GATHER_MAX, false>(a, grid, K, bpe, s);
-    }
-}
-
-void launch_heavy(const GatherArgs& a, cudaStream_t s) {
-    if (a.F <= gk::kHeavyConsumers) launch_heavy_vec<1>(a, s);
-    else if (a.F <= 2 * gk::kHeavyConsumers) launch_heavy_vec<2>(a, s);
-    else launch_heavy_vec<4>(a, s);
+    if (a.op == GATHER_SUM) launch_heavy_t<GATHER_SUM>(a, grid, K, bpe, s);
+    else launch_heavy_t<GATHER_MAX>(a, grid, K, bpe, s);
 }
 
 void dispatch_light(const GatherArgs& a, cudaStream_t s) {
