@@ -73,6 +73,21 @@ __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, int* err, i
     return false;
 }
 
+// Bounded wait for a thread whose wait is not on the critical path: it
+// sleeps from the first failed poll, leaving issue slots to the warps that
+// share its SM sub-partition.
+__device__ __forceinline__ bool wait_sleepy(uint64_t* bar, uint32_t parity, int* err, int code, uint32_t sleep_ns) {
+    if (try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
+        __nanosleep(sleep_ns);
+        if (try_wait(bar, parity)) return true;
+        if ((i & 15) == 0 && global_ns() - t0 > kWaitNs) break;
+    }
+    atomicCAS(err, 0, code);
+    return false;
+}
+
 // Global -> shared bulk copy of `bytes` (multiple of 16, both addresses
 // 16-byte aligned), completion counted on `bar`.  No multicast.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
@@ -87,6 +102,13 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 // bypassed, L2 policy hint); both addresses 16-byte aligned.
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint64_t policy) {
     asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;"
+                 ::"r"(smem_u32(dst)), "l"(src), "l"(policy)
+                 : "memory");
+}
+
+// 4-byte global -> shared async copy (L1-allocating form; 4-byte aligned).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, uint64_t policy) {
+    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2;"
                  ::"r"(smem_u32(dst)), "l"(src), "l"(policy)
                  : "memory");
 }

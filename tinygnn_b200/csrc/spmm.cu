@@ -76,7 +76,6 @@ void dispatch_cvec(const GatherArgs& a, cudaStream_t s) {
 // slots.  TINYGNN_B200_HEAVY_MIN_LEN sets a fixed threshold instead (a
 // negative value below -1 turns the heavy kernel off).
 constexpr int64_t kHeavyScan = 16384;
-constexpr size_t kHeavySmemBudget = 100 * 1024;  // two CTAs per SM
 
 __device__ int g_gather_error = 0;  // first heavy-kernel timeout code (0 = none)
 
@@ -101,23 +100,21 @@ int* gather_error_word() {
 }
 
 template <int OP>
-void launch_heavy_t(const GatherArgs& a, dim3 grid, int K, int bpe, cudaStream_t s) {
+void launch_heavy_t(const GatherArgs& a, int passes, int64_t groups, cudaStream_t s) {
     auto kern = gk::gather_heavy_kernel<OP>;
-    const size_t smem = gk::heavy_smem_bytes(K, bpe);
+    const size_t smem = sizeof(gk::HeavySmem);
     TG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    launch("gather_heavy", kern, grid, dim3(gk::kHeavyThreads), smem, s, a, K, bpe, gather_error_word());
+    launch("gather_heavy", kern, dim3(static_cast<unsigned>(passes * groups)), dim3(gk::kHeavyThreads), smem, s, a,
+           passes, gather_error_word());
 }
 
+// One CTA per (row group, 32-feature slice); all of them resident at once.
 void launch_heavy(const GatherArgs& a, cudaStream_t s) {
-    const int64_t width = gk::kHeavyConsumers;  // features per pass (one per consumer thread)
-    const int64_t passes = ceil_div(a.F, width);
-    const int bpe = static_cast<int>(std::min<int64_t>(width, (a.F + 3) / 4 * 4) * 4);
-    const size_t stage = static_cast<size_t>(gk::kHeavyG) * (bpe + 4) + sizeof(gk::HeavyDesc);
-    const int K = static_cast<int>(std::max<size_t>(2, std::min<size_t>(16, kHeavySmemBudget / stage)));
-    const int64_t ctas = std::min<int64_t>(std::min(kHeavyScan, a.M), 2 * static_cast<int64_t>(num_sms()));
-    const dim3 grid(static_cast<unsigned>(ctas), static_cast<unsigned>(passes));
-    if (a.op == GATHER_SUM) launch_heavy_t<GATHER_SUM>(a, grid, K, bpe, s);
-    else launch_heavy_t<GATHER_MAX>(a, grid, K, bpe, s);
+    const int passes = static_cast<int>(ceil_div(a.F, gk::kHeavySlice));
+    const int64_t resident = static_cast<int64_t>(gk::kHeavyCtasPerSm) * num_sms();
+    const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(std::min(kHeavyScan, a.M), resident / passes));
+    if (a.op == GATHER_SUM) launch_heavy_t<GATHER_SUM>(a, passes, groups, s);
+    else launch_heavy_t<GATHER_MAX>(a, passes, groups, s);
 }
 
 void dispatch_light(const GatherArgs& a, cudaStream_t s) {
