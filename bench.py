@@ -59,6 +59,8 @@ def parse():
                     help="fast: 3xTF32 tensor-core GEMMs (within fp32 tolerance); exact: bit-identical GEMMs")
     ap.add_argument("--small", action="store_true", help="a 20k-node graph (quick functional run)")
     ap.add_argument("--edges", type=int, default=0, help="override the edge count (profiling on a smaller graph)")
+    ap.add_argument("--passes", default="auto",
+                    help="column passes per gather after the all-gather (auto: operand bytes / 64 MB)")
     ap.add_argument("--pipeline", action="store_true",
                     help="N > 1: per-rank async broadcasts with a gather pass per arriving block")
     ap.add_argument("--blocks-per-rank", default="auto",
@@ -338,7 +340,8 @@ def run_ours(args):
     n, rp, ci, v = make_graph(args.small, dev, args.edges)
     w = make_weights(args.workload, dev)
     bpr = args.blocks_per_rank if args.blocks_per_rank == "auto" else int(args.blocks_per_rank)
-    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode, blocks_per_rank=bpr,
+    passes = args.passes if args.passes == "auto" else int(args.passes)
+    model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode, blocks_per_rank=bpr, passes=passes,
                          pipeline=args.pipeline)
     R, r0, r1 = model.R, model.row0, model.row1
     rows = r1 - r0

@@ -42,8 +42,8 @@ def main() -> int:
         full = tg.CSR(n, n, rp, ci, v)
         one = ShardedModel(layers, n, Comm(1, 0), dev, mode="exact")
         ref = one.forward(gcn_norm_rows(full, 0, n, Comm(1, 0)), full, X).clone()
-    for pipeline in (False, True):  # one all-gather / per-block broadcasts
-        model = ShardedModel(layers, n, comm, dev, mode="exact", pipeline=pipeline)
+    for pipeline, passes in ((False, 1), (False, 3), (True, "auto")):  # all-gather + passes / broadcasts
+        model = ShardedModel(layers, n, comm, dev, mode="exact", pipeline=pipeline, passes=passes)
         out = model.forward(An, A, X[r0:r1].contiguous())
         parts = [torch.zeros((R, 9), device=dev) for _ in range(world)]
         mine = torch.zeros((R, 9), device=dev)
@@ -51,7 +51,7 @@ def main() -> int:
         dist.all_gather(parts, mine)
         if rank == 0:
             same = bool(torch.equal(torch.cat(parts, 0)[:n], ref))
-            print(f"pipeline={pipeline} same={same}", flush=True)
+            print(f"pipeline={pipeline} passes={passes} same={same}", flush=True)
             ok = ok and same
     if rank == 0:
         print(f"world={world} bit-identical={ok}", flush=True)

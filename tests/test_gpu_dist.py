@@ -68,7 +68,7 @@ def test_row_block_gcn_norm_matches_global(tg, world):
 
 
 @pytest.mark.parametrize("workload,bpr", [("gcn", 2), ("gcn", 3), ("sage", 4)])
-def test_single_gpu_column_blocks_are_bit_identical(tg, workload, bpr):
+def test_single_gpu_column_passes_are_bit_identical(tg, workload, bpr):
     from tinygnn_b200.dist import Comm, Layer, ShardedModel, gcn_norm_rows
     rng, rp, ci, v, X = _graph(seed=bpr)
     n = rp.size - 1
@@ -82,10 +82,12 @@ def test_single_gpu_column_blocks_are_bit_identical(tg, workload, bpr):
     A = tg.CSR.from_numpy(rp, ci, v)
     An = gcn_norm_rows(A, 0, n, Comm(1, 0)) if not sage else None
     Xd = torch.as_tensor(X).cuda()
-    one = ShardedModel(layers, n, Comm(1, 0), "cuda").forward(An, A, Xd).clone()
-    blk = ShardedModel(layers, n, Comm(1, 0), "cuda", blocks_per_rank=bpr).forward(An, A, Xd)
+    one = ShardedModel(layers, n, Comm(1, 0), "cuda", passes=1).forward(An, A, Xd).clone()
+    blk = ShardedModel(layers, n, Comm(1, 0), "cuda", passes=bpr).forward(An, A, Xd)
+    pip = ShardedModel(layers, n, Comm(1, 0), "cuda", blocks_per_rank=bpr, pipeline=True).forward(An, A, Xd)
     torch.cuda.synchronize()
-    assert_bits_equal(blk.cpu().numpy(), one.cpu().numpy(), f"{workload} {bpr} blocks")
+    assert_bits_equal(blk.cpu().numpy(), one.cpu().numpy(), f"{workload} {bpr} passes")
+    assert_bits_equal(pip.cpu().numpy(), one.cpu().numpy(), f"{workload} {bpr} blocks (pipelined path)")
 
 
 @pytest.mark.parametrize("workload,mode,blocks", [("gcn", "exact", 8), ("gcn", "fast", 5), ("sage", "fast", 1)])

@@ -118,20 +118,27 @@ class ShardedModel:
     BLOCK_BYTES = 64 << 20
 
     def __init__(self, layers: List[Layer], n: int, comm: Comm, device, mode: str = "exact",
-                 blocks_per_rank="auto", pipeline: bool = False):
+                 blocks_per_rank="auto", pipeline: bool = False, passes="auto"):
         self.layers, self.n, self.comm, self.device, self.mode = layers, n, comm, device, mode
         # pipeline: per-rank async broadcasts with one gather pass per arriving
-        # block; otherwise one all-gather, then the passes (measured on 2 B200:
-        # one in-place all-gather moves ~450 GB/s, P broadcasts ~35 % slower).
+        # column block (blocks_per_rank blocks per rank); otherwise one
+        # all-gather, then `passes` column passes over the whole operand
+        # (measured on 2 B200: one in-place all-gather moves ~450 GB/s, P
+        # broadcasts ~35 % slower).
         self.pipeline = pipeline
         R0 = (n + comm.world - 1) // comm.world
         if blocks_per_rank == "auto":
             self.bprs = [max(1, -(-(R0 * _pad4(L.W.shape[1]) * 4) // self.BLOCK_BYTES)) for L in layers]
         else:
             self.bprs = [max(1, int(blocks_per_rank))] * len(layers)
+        if passes == "auto":
+            self.passes = [max(1, -(-(n * _pad4(L.W.shape[1]) * 4) // self.BLOCK_BYTES)) for L in layers]
+        else:
+            self.passes = [max(1, int(passes))] * len(layers)
         multiple = 1
-        for b in self.bprs:
-            multiple = multiple * b // math.gcd(multiple, b)
+        if pipeline:  # rank blocks split evenly into column blocks
+            for b in self.bprs:
+                multiple = multiple * b // math.gcd(multiple, b)
         self.R, self.row0, self.row1 = row_block(n, comm.world, comm.rank, multiple)
         self.rows = self.row1 - self.row0
         P = comm.world
@@ -150,18 +157,28 @@ class ShardedModel:
         if self.timing is not None:
             self.timing(li, what, edge)
 
-    def splits(self, A: CSR, bpr: int) -> Optional[torch.Tensor]:
-        """Column-block split points of A's rows for `bpr` blocks per rank (cached on A)."""
-        nblocks = self.comm.world * bpr
-        if nblocks == 1:
-            return None
-        key = (nblocks, self.R // bpr)
+    @staticmethod
+    def _cached_splits(A: CSR, nblocks: int, width: int) -> torch.Tensor:
         cache = getattr(A, "_splits", None)
         if cache is None:
             cache = A._splits = {}
+        key = (nblocks, width)
         if key not in cache:
-            cache[key] = ops.column_splits(A, nblocks, self.R // bpr)
+            cache[key] = ops.column_splits(A, nblocks, width)
         return cache[key]
+
+    def splits(self, A: CSR, bpr: int) -> Optional[torch.Tensor]:
+        """Split points of A's rows into `bpr` column blocks per rank (pipelined exchange; cached on A)."""
+        nblocks = self.comm.world * bpr
+        if nblocks == 1:
+            return None
+        return self._cached_splits(A, nblocks, self.R // bpr)
+
+    def pass_splits(self, A: CSR, passes: int) -> Optional[torch.Tensor]:
+        """Split points of A's rows into `passes` equal column ranges of the whole operand (cached on A)."""
+        if passes == 1:
+            return None
+        return self._cached_splits(A, passes, -(-self.n // passes))
 
     # The phases of a layer; forward() runs them in order.  Tests that
     # emulate several ranks in one process interleave them across shards.
@@ -204,12 +221,22 @@ class ShardedModel:
         return H
 
     def exchange_and_aggregate(self, li: int, A_gcn: Optional[CSR], A_raw: Optional[CSR]) -> torch.Tensor:
-        """Per-block passes, each started as soon as its block has arrived."""
+        """The exchange, then the gather: passes over column ranges in increasing
+        order (one all-gather first), or -- pipelined -- one pass per rank block
+        as soon as that block has arrived."""
         A = A_gcn if self.layers[li].kind == "gcn" else A_raw
-        bpr = self.bprs[li]
-        if self.comm.world > 1 and not self.pipeline:
+        if not self.pipeline:
             self.exchange(li)
-            return self.aggregate(li, A_gcn, A_raw)
+            sp = self.pass_splits(A, self.passes[li])
+            if sp is None:
+                return self.aggregate(li, A_gcn, A_raw)
+            self._mark(li, "gather", "start")
+            nb = self.passes[li]
+            for q in range(nb):
+                H = self._pass(li, A, sp[q], sp[q + 1], q > 0, q == nb - 1)
+            self._mark(li, "gather", "end")
+            return H
+        bpr = self.bprs[li]
         sp = self.splits(A, bpr)
         if sp is None:
             self.exchange(li)
