@@ -65,6 +65,10 @@ def parse():
                     help="N > 1: per-rank async broadcasts with a gather pass per arriving block")
     ap.add_argument("--blocks-per-rank", default="auto",
                     help="column blocks per rank for the gathers: 'auto' or a count")
+    ap.add_argument("--micro", choices=["hub"], default=None,
+                    help="hub: time one long row through spmm (the heavy-row path) instead of the benchmark")
+    ap.add_argument("--micro-entries", type=int, default=13_531)
+    ap.add_argument("--micro-features", type=int, default=128)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
@@ -479,8 +483,42 @@ def run_ours(args):
     return 0
 
 
+def run_micro_hub(args):
+    """One long row through the public spmm: the critical path the heavy-row
+    kernel exists for (a Reddit-shaped hub has 13,531 entries).  Prints its
+    own JSON line; not the benchmark contract's line."""
+    import tinygnn_b200 as tg
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(1)
+    n, F, reps = 240_000, args.micro_features, 20
+    rp = np.zeros(n + 1, np.int32)
+    rp[1:] = args.micro_entries  # row 0 holds every entry, the other rows are empty
+    ci = np.sort(rng.choice(n, args.micro_entries, replace=False)).astype(np.int32)
+    A = tg.CSR.from_numpy(rp, ci, np.ones(ci.size, np.float32)).with_degree_order()
+    Fp = (F + 3) // 4 * 4
+    B = torch.randn(n, Fp, device="cuda")[:, :F]
+    out = torch.empty(n, F, device="cuda")
+    for _ in range(3):
+        tg.spmm(A, B, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        tg.spmm(A, B, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000 / reps
+    print(json.dumps({"micro": "hub_row", "entries": args.micro_entries, "features": F, "us_per_call": us,
+                      "ns_per_entry": us * 1000 / args.micro_entries,
+                      "heavy_min_len": os.environ.get("TINYGNN_B200_HEAVY_MIN_LEN", "auto")}))
+    tg.ops.take_device_error()
+    return 0
+
+
 def main():
     args = parse()
+    if args.micro == "hub":
+        return run_micro_hub(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -95,9 +95,9 @@ __device__ __forceinline__ float tf32_rn(float x) {
     return __uint_as_float(r);
 }
 
-template <int BN>
+template <int BN, int STAGES_>
 struct TcSmem {
-    static constexpr int STAGES = stages_for(BN);
+    static constexpr int STAGES = STAGES_;
     float A[STAGES][BM * BK];     // raw tile, split in place into Ah
     float Al[STAGES][BM * BK];
     float Bh[STAGES][BN * BK];
@@ -114,14 +114,15 @@ struct TcArgs {
     float alpha;
 };
 
-template <int BN>
+template <int BN, int STAGES_>
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmBh,
                                                          const __grid_constant__ CUtensorMap tmBl,
                                                          const TcArgs g) {
     extern __shared__ uint8_t raw[];
-    TcSmem<BN>& s = *reinterpret_cast<TcSmem<BN>*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
-    constexpr int STAGES = TcSmem<BN>::STAGES;
+    using Smem = TcSmem<BN, STAGES_>;
+    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    constexpr int STAGES = STAGES_;
     constexpr uint32_t TMEM_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
     constexpr uint32_t STAGE_BYTES = (BM * BK + 2 * BN * BK) * 4;
     // tf32 x tf32 -> f32, K-major A and B, M = 128, N = BN.
@@ -213,9 +214,15 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         }
         if (ok && mbar_wait(&s.acc, 0, 5)) {
             asm volatile("tcgen05.fence::after_thread_sync;");
-            const int q = warp & 3;  // this warp's TMEM lane quarter
-            const int64_t row = m0 + q * 32 + lane;
+            const int q = warp & 3;  // this warp's TMEM lane quarter = its 32 rows of the tile
             const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+            // The accumulator complete means every MMA has read its operands
+            // and every copy has landed: the pipeline's shared memory is free.
+            // Each warp stages its 32 rows there (row stride BN + 1: the
+            // column-wise writes hit 32 banks), then stores them row by row
+            // -- 32 consecutive columns per instruction, coalesced.
+            static_assert(BM * (BN + 1) <= STAGES * (2 * BM * BK + 2 * BN * BK), "staging tile exceeds the ring");
+            float* tile = reinterpret_cast<float*>(&s) + static_cast<size_t>(q) * 32 * (BN + 1);  // the ring's start
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 uint32_t r[16];
@@ -227,16 +234,28 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                       "=r"(r[15])
                     : "r"(taddr + c0));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (row < g.M) {
-                    float* crow = g.C + row * g.ldc;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int64_t col = c0 + j;
-                        if (col < g.N) {
-                            float v = __uint_as_float(r[j]);
-                            if (g.bias) v = __fadd_rn(v, __ldg(g.bias + col));
-                            crow[col] = apply_act(g.act, v, g.alpha);
-                        }
+                for (int j = 0; j < 16; ++j) tile[lane * (BN + 1) + c0 + j] = __uint_as_float(r[j]);
+            }
+            __syncwarp();
+            constexpr int CPL = (BN + 31) / 32;  // columns per lane: lane + 32k
+            float bv[CPL];
+#pragma unroll
+            for (int k = 0; k < CPL; ++k) {
+                const int col = lane + 32 * k;
+                bv[k] = (g.bias && col < g.N) ? __ldg(g.bias + col) : 0.0f;
+            }
+            const int rows = static_cast<int>(g.M - (m0 + q * 32) < 32 ? g.M - (m0 + q * 32) : 32);
+#pragma unroll 4
+            for (int rr = 0; rr < rows; ++rr) {
+                float* crow = g.C + (m0 + q * 32 + rr) * g.ldc;
+#pragma unroll
+                for (int k = 0; k < CPL; ++k) {
+                    const int col = lane + 32 * k;
+                    if (col < g.N) {
+                        float v = tile[rr * (BN + 1) + col];
+                        if (g.bias) v = __fadd_rn(v, bv[k]);
+                        crow[col] = apply_act(g.act, v, g.alpha);
                     }
                 }
             }
@@ -299,11 +318,24 @@ CUtensorMap make_map(const float* base, int64_t inner, int64_t outer, int64_t ro
     return m;
 }
 
+template <int BN, int STAGES>
+void launch_tc_s(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g, cudaStream_t s) {
+    const size_t smem = sizeof(TcSmem<BN, STAGES>) + 1024;
+    auto kern = gemm_tc_kernel<BN, STAGES>;
+    TG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    launch("gemm_tc", kern, dim3(static_cast<unsigned>(ceil_div(g.M, BM))), dim3(192), smem, s, a, bh, bl, g);
+}
+
+// A deep ring for long K; for short K (a few k-blocks per tile, where one
+// tile's pipeline fill and epilogue dominate) two stages, so that two CTAs
+// share an SM and one's epilogue overlaps the other's main loop (measured:
+// the K = 128, N = 41 layer-2 GEMM is latency-bound at one CTA per SM).
 template <int BN>
 void launch_tc(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g, cudaStream_t s) {
-    const size_t smem = sizeof(TcSmem<BN>) + 1024;
-    TG_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    launch("gemm_tc", gemm_tc_kernel<BN>, dim3(static_cast<unsigned>(ceil_div(g.M, BM))), dim3(192), smem, s, a, bh, bl, g);
+    constexpr int kShallow = 2;
+    constexpr bool two_fit = 2 * (sizeof(TcSmem<BN, kShallow>) + 1024) <= 227 * 1024;
+    if (two_fit && g.K <= 8 * BK) launch_tc_s<BN, two_fit ? kShallow : stages_for(BN)>(a, bh, bl, g, s);
+    else launch_tc_s<BN, stages_for(BN)>(a, bh, bl, g, s);
 }
 
 }  // namespace
