@@ -61,8 +61,9 @@ def parse():
     ap.add_argument("--edges", type=int, default=0, help="override the edge count (profiling on a smaller graph)")
     ap.add_argument("--passes", default="auto",
                     help="column passes per gather after the all-gather (auto: operand bytes / 64 MB)")
-    ap.add_argument("--pipeline", action="store_true",
-                    help="N > 1: per-rank async broadcasts with a gather pass per arriving block")
+    ap.add_argument("--pipeline", choices=["auto", "on", "off"], default="auto",
+                    help="N > 1: per-rank async broadcasts with a gather pass per arriving block "
+                         "(auto: on 2-4 GPUs, for the layers whose exchanged operand is >= 64 MB)")
     ap.add_argument("--blocks-per-rank", default="auto",
                     help="column blocks per rank for the gathers: 'auto' or a count")
     ap.add_argument("--micro", choices=["hub"], default=None,
@@ -310,10 +311,14 @@ def metric_name(workload):
 def config_dict(args, n, nnz):
     return {"workload": f"{args.workload}-reddit-shape" + ("-small" if args.small else ""),
             "nodes": n, "nnz": nnz, "features": FEATS, "hidden": HIDDEN, "classes": CLASSES,
-            "partition": ("1-D equal row blocks; each layer's transformed rows broadcast per rank block "
-                          "(NCCL, async) with one exact gather pass per arriving column block" if args.pipeline else
-                          "1-D equal row blocks; each layer's transformed rows exchanged by one in-place NCCL "
-                          "all-gather, then exact gather passes over column blocks"),
+            "partition": "1-D equal row blocks; " + {
+                "on": "each layer's transformed rows broadcast per rank block (NCCL, async), one exact gather "
+                      "pass per arriving block",
+                "off": "each layer's transformed rows exchanged by one in-place NCCL all-gather, then exact "
+                       "gather passes over column ranges",
+                "auto": "on 2-4 GPUs, layers whose exchanged operand is >= 64 MB broadcast per rank block "
+                        "(NCCL, async) with one exact gather pass per arriving block; otherwise one in-place NCCL "
+                        "all-gather, then exact gather passes over column ranges"}[args.pipeline],
             "parallelism": f"row-partition x{args.gpus}",
             "l2": "inputs larger than L2 (CSR 918 MB, features 561 MB); no flush between steps",
             "mode": ("fast: 3xTF32 tcgen05 GEMMs, order-preserving fp32 gathers" if args.mode == "fast"
@@ -346,7 +351,7 @@ def run_ours(args):
     bpr = args.blocks_per_rank if args.blocks_per_rank == "auto" else int(args.blocks_per_rank)
     passes = args.passes if args.passes == "auto" else int(args.passes)
     model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode, blocks_per_rank=bpr, passes=passes,
-                         pipeline=args.pipeline)
+                         pipeline={"auto": "auto", "on": True, "off": False}[args.pipeline])
     R, r0, r1 = model.R, model.row0, model.row1
     rows = r1 - r0
     A_raw = slice_rows(rp, ci, v, r0, r1, n)

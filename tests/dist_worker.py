@@ -42,7 +42,7 @@ def main() -> int:
         full = tg.CSR(n, n, rp, ci, v)
         one = ShardedModel(layers, n, Comm(1, 0), dev, mode="exact")
         ref = one.forward(gcn_norm_rows(full, 0, n, Comm(1, 0)), full, X).clone()
-    for pipeline, passes in ((False, 1), (False, 3), (True, "auto")):  # all-gather + passes / broadcasts
+    for pipeline, passes in ((False, 1), (False, 3), (True, "auto"), ("auto", "auto")):  # all-gather + passes / broadcasts
         model = ShardedModel(layers, n, comm, dev, mode="exact", pipeline=pipeline, passes=passes)
         out = model.forward(An, A, X[r0:r1].contiguous())
         parts = [torch.zeros((R, 9), device=dev) for _ in range(world)]

@@ -118,14 +118,23 @@ class ShardedModel:
     BLOCK_BYTES = 64 << 20
 
     def __init__(self, layers: List[Layer], n: int, comm: Comm, device, mode: str = "exact",
-                 blocks_per_rank="auto", pipeline: bool = False, passes="auto"):
+                 blocks_per_rank="auto", pipeline="auto", passes="auto"):
         self.layers, self.n, self.comm, self.device, self.mode = layers, n, comm, device, mode
         # pipeline: per-rank async broadcasts with one gather pass per arriving
         # column block (blocks_per_rank blocks per rank); otherwise one
-        # all-gather, then `passes` column passes over the whole operand
-        # (measured on 2 B200: one in-place all-gather moves ~450 GB/s, P
-        # broadcasts ~35 % slower).
-        self.pipeline = pipeline
+        # all-gather, then `passes` column passes over the whole operand.
+        # "auto" pipelines, on 2-4 ranks, the layers whose exchanged operand
+        # is at least BLOCK_BYTES.  Measured on B200 (GCN, Reddit-shaped):
+        # P = 2 forward 3.52 -> 3.34 ms; P = 4 layer 1 (exchange + gather)
+        # 1.25 -> 1.19 ms but the 41 MB layer 2 0.62 -> 0.72 ms; P = 8 layer
+        # 1 0.82 -> 1.09 ms (eight serial broadcasts and eight passes).  P
+        # broadcasts move less than one all-gather, which pays only where the
+        # passes they overlap are long.
+        if pipeline == "auto":
+            self.pipe = [2 <= comm.world <= 4 and n * _pad4(L.W.shape[1]) * 4 >= self.BLOCK_BYTES for L in layers]
+        else:
+            self.pipe = [bool(pipeline)] * len(layers)
+        self.pipeline = any(self.pipe)
         R0 = (n + comm.world - 1) // comm.world
         if blocks_per_rank == "auto":
             self.bprs = [max(1, -(-(R0 * _pad4(L.W.shape[1]) * 4) // self.BLOCK_BYTES)) for L in layers]
@@ -136,7 +145,7 @@ class ShardedModel:
         else:
             self.passes = [max(1, int(passes))] * len(layers)
         multiple = 1
-        if pipeline:  # rank blocks split evenly into column blocks
+        if self.pipeline:  # rank blocks split evenly into column blocks
             for b in self.bprs:
                 multiple = multiple * b // math.gcd(multiple, b)
         self.R, self.row0, self.row1 = row_block(n, comm.world, comm.rank, multiple)
@@ -225,7 +234,7 @@ class ShardedModel:
         order (one all-gather first), or -- pipelined -- one pass per rank block
         as soon as that block has arrived."""
         A = A_gcn if self.layers[li].kind == "gcn" else A_raw
-        if not self.pipeline:
+        if not self.pipe[li]:
             self.exchange(li)
             sp = self.pass_splits(A, self.passes[li])
             if sp is None:
