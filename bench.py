@@ -61,6 +61,9 @@ def parse():
     ap.add_argument("--edges", type=int, default=0, help="override the edge count (profiling on a smaller graph)")
     ap.add_argument("--passes", default="auto",
                     help="column passes per gather after the all-gather (auto: operand bytes / 64 MB)")
+    ap.add_argument("--exchange", choices=["auto", "peer", "nccl"], default="auto",
+                    help="N > 1: peer = the GEMM stores its tiles into every GPU's gather buffer over NVLink; "
+                         "nccl = GEMM then NCCL all-gather / broadcasts (auto: peer in fast mode)")
     ap.add_argument("--pipeline", choices=["auto", "on", "off"], default="auto",
                     help="N > 1: per-rank async broadcasts with a gather pass per arriving block "
                          "(auto: on 2-4 GPUs, for the layers whose exchanged operand is >= 64 MB)")
@@ -308,10 +311,16 @@ def metric_name(workload):
             f"{NODES} nodes / {EDGES} edges)")
 
 
-def config_dict(args, n, nnz):
+def config_dict(args, n, nnz, exchange="nccl"):
+    if args.gpus > 1 and exchange == "peer":
+        partition = ("1-D equal row blocks; each layer's GEMM stores its output tiles into every GPU's gather "
+                     "buffer over NVLink (peer memory) and signals per tile; each GPU waits for its peers' tiles "
+                     "on the device, then exact gather passes over column ranges")
+    else:
+        partition = None
     return {"workload": f"{args.workload}-reddit-shape" + ("-small" if args.small else ""),
             "nodes": n, "nnz": nnz, "features": FEATS, "hidden": HIDDEN, "classes": CLASSES,
-            "partition": "1-D equal row blocks; " + {
+            "partition": partition or "1-D equal row blocks; " + {
                 "on": "each layer's transformed rows broadcast per rank block (NCCL, async), one exact gather "
                       "pass per arriving block",
                 "off": "each layer's transformed rows exchanged by one in-place NCCL all-gather, then exact "
@@ -351,7 +360,7 @@ def run_ours(args):
     bpr = args.blocks_per_rank if args.blocks_per_rank == "auto" else int(args.blocks_per_rank)
     passes = args.passes if args.passes == "auto" else int(args.passes)
     model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode, blocks_per_rank=bpr, passes=passes,
-                         pipeline={"auto": "auto", "on": True, "off": False}[args.pipeline])
+                         pipeline={"auto": "auto", "on": True, "off": False}[args.pipeline], exchange=args.exchange)
     R, r0, r1 = model.R, model.row0, model.row1
     rows = r1 - r0
     A_raw = slice_rows(rp, ci, v, r0, r1, n)
@@ -470,7 +479,7 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded Chung-Lu graph, N(0,1) features, Glorot weights, zero bias)",
-            "config": config_dict(args, n, nnz_total),
+            "config": config_dict(args, n, nnz_total, model.exchange_kind),
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "edges/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": None if e2e_ms is None else e2e_ms / args.steps,
@@ -481,6 +490,8 @@ def run_ours(args):
             "phase_ms_per_rank": rank_phases if world > 1 else None,
         }
         print(json.dumps(line))
+    torch.cuda.synchronize()
+    model.close()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

@@ -325,11 +325,49 @@ TG_API tg_status tg_gat_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
                                   float* out, int64_t ldo, const int32_t* row_order,
                                   int32_t mode, void* stream);
 
+/* ── Fused GEMM -> exchange over NVLink (one process per GPU) ────────────
+ * No counterpart in the reference (it has no multi-GPU path); these replace
+ * the NCCL all-gather between a row-partitioned layer's GEMM and its gather.
+ *
+ * tg_ipc_get_handle: a CUDA IPC handle (TG_IPC_HANDLE_BYTES bytes) of the
+ * allocation holding `ptr`, and ptr's offset in it.  tg_ipc_open_handle maps
+ * another process's allocation into this one (its base; add the offset);
+ * tg_ipc_close_handle unmaps it. */
+#define TG_IPC_HANDLE_BYTES 64
+#define TG_MAX_PEERS 7
+TG_API tg_status tg_ipc_get_handle(const void* ptr, void* handle_out, int64_t* offset_out);
+TG_API tg_status tg_ipc_open_handle(const void* handle, void** base_out);
+TG_API tg_status tg_ipc_close_handle(void* base);
+
+/* C = act(A . B + bias) on the tensor cores (FAST mode arithmetic), with
+ * every stored row also written at the same offset of peer_C[p] (another
+ * GPU's copy of C's buffer, same ldc), for p < npeers (<= TG_MAX_PEERS); once
+ * a 128-row tile has landed in every copy, *peer_flags[p] += 1 (a 64-bit
+ * counter in that GPU's memory; release, system scope).  Requires N <= 256,
+ * lda % 4 == 0 and A 16-byte aligned.  flags: TG_FLAG_C_COLS_PADDED = the
+ * rows of C and of its copies have room up to round_up(N, 4) columns, which
+ * may then be written (with act(0)) so that rows are stored 16 bytes at a
+ * time. */
+#define TG_FLAG_C_COLS_PADDED 0x200
+TG_API tg_status tg_gemm_peers_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+                                   const float* B, int64_t ldb, float* C, int64_t ldc,
+                                   const float* bias, int32_t act, float alpha, int32_t npeers,
+                                   float* const* peer_C, uint64_t* const* peer_flags, int32_t flags,
+                                   void* stream);
+
+/* Waits on the device, in stream order, until flags[i] >= targets[i] for
+ * every i < n (n <= 8; targets is a host array, 0 = skip), reading with
+ * acquire semantics at system scope.  A flag that has not reached its target
+ * after timeout_ns gives up: tg_take_device_error then reports
+ * TG_ERR_TIMEOUT. */
+TG_API tg_status tg_wait_flags(const uint64_t* flags, const uint64_t* targets, int32_t n,
+                               int64_t timeout_ns, void* stream);
+
 /* Reads and clears the device error words of the pipelined kernels (the
- * tensor-core GEMM of FAST mode and the heavy-row gather used by every
- * degree-ordered spmm / SAGE aggregation): TG_ERR_TIMEOUT when one of their
- * bounded pipeline waits ran out since the last call (that call's output is
- * then invalid).  Synchronises `stream`. */
+ * tensor-core GEMM of FAST mode, the heavy-row gather used by every
+ * degree-ordered spmm / SAGE aggregation, tg_wait_flags): TG_ERR_TIMEOUT
+ * when one of their bounded waits ran out since the last call (that call's
+ * output is then invalid).  Synchronises `stream`. */
 TG_API tg_status tg_take_device_error(void* stream);
 
 #ifdef __cplusplus

@@ -53,6 +53,22 @@ def main() -> int:
             same = bool(torch.equal(torch.cat(parts, 0)[:n], ref))
             print(f"pipeline={pipeline} passes={passes} same={same}", flush=True)
             ok = ok and same
+    # FAST mode: the fused GEMM -> NVLink exchange (IPC-mapped peer buffers,
+    # counters, device-side waits) against GEMM + NCCL all-gather.  Same
+    # tensor-core GEMM and gathers, so the logits must match bit for bit;
+    # three forwards use both buffer parities.
+    nccl = ShardedModel(layers, n, comm, dev, mode="fast", exchange="nccl")
+    peer = ShardedModel(layers, n, comm, dev, mode="fast", exchange="peer")
+    for step in range(3):
+        a = nccl.forward(An, A, X[r0:r1].contiguous()).clone()
+        b = peer.forward(An, A, X[r0:r1].contiguous())
+        torch.cuda.synchronize()
+        same = bool(torch.equal(a, b))
+        if rank == 0:
+            print(f"peer exchange step {step} same={same}", flush=True)
+        ok = ok and same
+    tg.ops.take_device_error()
+    peer.close()
     if rank == 0:
         print(f"world={world} bit-identical={ok}", flush=True)
     flag = torch.tensor([1 if ok else 0], device=dev)

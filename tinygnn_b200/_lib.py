@@ -66,6 +66,12 @@ SIGNATURES = {
     "tg_gat_layer_f32": (i32, [i64, i64, vp, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp, f32, i32, i32, vp, i64,
                                vp, i32, vp]),
     "tg_take_device_error": (i32, [vp]),
+    "tg_ipc_get_handle": (i32, [vp, vp, P64]),
+    "tg_ipc_open_handle": (i32, [vp, C.POINTER(vp)]),
+    "tg_ipc_close_handle": (i32, [vp]),
+    "tg_gemm_peers_f32": (i32, [i64, i64, i64, vp, i64, vp, i64, vp, i64, vp, i32, f32, i32, C.POINTER(vp),
+                                C.POINTER(vp), i32, vp]),
+    "tg_wait_flags": (i32, [vp, C.POINTER(u64), i32, i64, vp]),
     "tg_gcn_layer_noalloc_f32": (i32, [i64, i64, vp, vp, vp, vp, i64, i64, i64, vp, vp, i32, vp, i64, vp, vp]),
 }
 

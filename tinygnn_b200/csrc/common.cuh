@@ -68,6 +68,17 @@ inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 // Number of SMs of the current device (cached per device).
 int num_sms();
 
+// ── Peer outputs of a fused GEMM -> exchange ─────────────────────────────
+// Up to kMaxPeers other GPUs' copies of an output (same offsets and leading
+// dimension, mapped into this process), and for each of them the address of
+// this rank's completion counter in that GPU's memory.
+constexpr int kMaxPeers = 7;
+struct PeerOut {
+    float* c[kMaxPeers] = {};
+    unsigned long long* flag[kMaxPeers] = {};
+    int n = 0;
+};
+
 // ── Side stream ──────────────────────────────────────────────────────────
 // A high-priority stream per (host thread, device) with two events, for
 // kernels that run beside the caller's stream inside one call: record `fork`

@@ -185,8 +185,10 @@ void gemm_exact(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
 bool gemm_tc_supported(int64_t N, int64_t K, const float* A, int64_t lda);
 int gemm_tc_take_error(cudaStream_t s);
 int gather_take_error(cudaStream_t s);
+int peer_take_error(cudaStream_t s);
 void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
-             int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s);
+             int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s, const PeerOut& peers = PeerOut{},
+             bool c_cols_padded = false);
 
 // FAST: tensor cores (3xTF32) when the operands allow TMA; otherwise, and in
 // EXACT mode, the k-sequential FMA kernel.
@@ -235,12 +237,16 @@ TG_API tg_status tg_take_device_error(void* stream) {
         require_device();
         const int code = gemm_tc_take_error(as_stream(stream));
         const int gcode = gather_take_error(as_stream(stream));
+        const int pcode = peer_take_error(as_stream(stream));
         if (code)
             fail(TG_ERR_TIMEOUT, "a tensor-core GEMM pipeline wait ran out (stage code " + std::to_string(code) +
                                      "); its output is invalid");
         if (gcode)
             fail(TG_ERR_TIMEOUT, "a heavy-row gather pipeline wait ran out (code " + std::to_string(gcode) +
                                      "); its output is invalid");
+        if (pcode)
+            fail(TG_ERR_TIMEOUT, "tg_wait_flags: flag " + std::to_string(pcode - 20) +
+                                     " did not reach its target in time (a peer's tiles are missing)");
     });
 }
 

@@ -81,6 +81,99 @@ class Comm:
             return None
         return dist.broadcast(full[src * R:(src + 1) * R], src=src, group=self.group, async_op=True)
 
+    def all_gather_object(self, obj) -> list:
+        out = [None] * self.world
+        dist.all_gather_object(out, obj, group=self.group)
+        return out
+
+    def barrier(self) -> None:
+        dist.barrier(group=self.group)
+
+    @property
+    def distributed(self) -> bool:
+        return self.world > 1 and dist.is_available() and dist.is_initialized()
+
+
+class PeerExchange:
+    """Exchange memory shared over NVLink by the ranks of a ShardedModel.
+
+    One allocation per rank holds, per layer, two gather buffers
+    ((P*R) x pad4(F_out); a layer's forward uses buffer epoch % 2) and a
+    (layers x P) table of 64-bit completion counters: counter [l, q] counts
+    the 128-row tiles of layer l that rank q has stored here.  Every rank maps
+    every other rank's allocation (CUDA IPC), so the fused GEMM stores its
+    tiles into all copies and bumps its counter in each.  Two buffers per
+    layer are enough without a "consumed" handshake: a rank writes epoch e+1
+    into a buffer that its peers last read at epoch e-1, and none of them can
+    still be there -- the writer finished epoch e's gather, which waited for
+    every peer's epoch-e tiles, which each peer stored after its epoch e-1
+    gather.
+    """
+
+    TILE = 128  # rows per GEMM tile (one counter increment)
+    ALIGN = 256
+
+    def __init__(self, comm: "Comm", R: int, widths: List[int], device):
+        self.comm, self.R, self.widths = comm, R, widths
+        P = comm.world
+        off, self.buf_off = 0, []
+        for w in widths:
+            pair = []
+            for _ in range(2):
+                pair.append(off)
+                off += -(-P * R * w * 4 // self.ALIGN) * self.ALIGN
+            self.buf_off.append(pair)
+        self.cnt_off = off
+        off += -(-len(widths) * P * 8 // self.ALIGN) * self.ALIGN
+        self.blob = torch.zeros(off, dtype=torch.uint8, device=device)
+        self.bufs = [[self.blob[o:o + P * R * w * 4].view(torch.float32).view(P * R, w) for o in pair]
+                     for pair, w in zip(self.buf_off, widths)]
+        self.counters = self.blob[self.cnt_off:self.cnt_off + len(widths) * P * 8].view(torch.int64).view(
+            len(widths), P)
+        torch.cuda.synchronize()  # zeroed before any peer may write here
+        handle, offset = ops.ipc_get_handle(self.blob)
+        table = comm.all_gather_object((handle, offset))
+        self.opened, self.peer_base = [], {}
+        for q, (h, o) in enumerate(table):
+            if q == comm.rank:
+                continue
+            base = ops.ipc_open_handle(h)
+            self.opened.append(base)
+            self.peer_base[q] = base + o
+        comm.barrier()
+        self.epoch = [0] * len(widths)
+        self.peers = [q for q in range(P) if q != comm.rank]
+        self.tiles = [0] * P
+
+    def set_rows(self, n: int) -> None:
+        """Tiles each rank stores per layer, from the global node count."""
+        P, R = self.comm.world, self.R
+        self.tiles = [-(-max(0, min(R, n - q * R)) // self.TILE) for q in range(P)]
+
+    def next_epoch(self, li: int) -> torch.Tensor:
+        """Start layer li's next forward: its gather buffer (this epoch's parity)."""
+        self.epoch[li] += 1
+        return self.bufs[li][self.epoch[li] % 2]
+
+    def peer_targets(self, li: int, row_off_floats: int):
+        """(peer output addresses, peer counter addresses) for layer li's current buffer."""
+        par = self.epoch[li] % 2
+        P, me = self.comm.world, self.comm.rank
+        outs = [self.peer_base[q] + self.buf_off[li][par] + row_off_floats * 4 for q in self.peers]
+        flags = [self.peer_base[q] + self.cnt_off + (li * P + me) * 8 for q in self.peers]
+        return outs, flags
+
+    def wait(self, li: int) -> None:
+        """In stream order: every peer's tiles of layer li's current epoch have landed here."""
+        e = self.epoch[li]
+        targets = [0 if q == self.comm.rank else self.tiles[q] * e for q in range(self.comm.world)]
+        ops.wait_flags(self.counters[li], targets)
+
+    def close(self) -> None:
+        for base in self.opened:
+            ops.ipc_close_handle(base)
+        self.opened = []
+
 
 def gcn_norm_rows(A: CSR, row0: int, R: int, comm: Comm, dis_all: Optional[torch.Tensor] = None) -> CSR:
     """gcn_norm of this rank's row block (global columns), bit-identical to the
@@ -118,8 +211,20 @@ class ShardedModel:
     BLOCK_BYTES = 64 << 20
 
     def __init__(self, layers: List[Layer], n: int, comm: Comm, device, mode: str = "exact",
-                 blocks_per_rank="auto", pipeline="auto", passes="auto"):
+                 blocks_per_rank="auto", pipeline="auto", passes="auto", exchange="auto"):
         self.layers, self.n, self.comm, self.device, self.mode = layers, n, comm, device, mode
+        # exchange: "peer" = the GEMM stores its tiles straight into every
+        # rank's gather buffer over NVLink (PeerExchange; FAST mode, the
+        # tensor-core GEMM); "nccl" = GEMM, then an NCCL all-gather or
+        # broadcasts.  "auto" = peer when FAST under a real process group.
+        if exchange == "auto":
+            exchange = ("peer" if mode == "fast" and getattr(comm, "distributed", False)
+                        and all(L.W.shape[1] <= 256 for L in layers) else "nccl")
+        if exchange == "peer" and mode != "fast":
+            raise ValueError("exchange='peer' runs the tensor-core GEMM: mode must be 'fast'")
+        self.exchange_kind = exchange
+        if exchange == "peer":
+            pipeline = False
         # pipeline: per-rank async broadcasts with one gather pass per arriving
         # column block (blocks_per_rank blocks per rank); otherwise one
         # all-gather, then `passes` column passes over the whole operand.
@@ -151,12 +256,18 @@ class ShardedModel:
         self.R, self.row0, self.row1 = row_block(n, comm.world, comm.rank, multiple)
         self.rows = self.row1 - self.row0
         P = comm.world
+        self.pex = None
+        if exchange == "peer":
+            self.pex = PeerExchange(comm, self.R, [_pad4(L.W.shape[1]) for L in layers], device)
+            self.pex.set_rows(n)
+        self.hpad = [None] * len(layers)  # 16-byte-aligned copies of unaligned layer inputs (peer exchange)
         self.full = []   # gathered operand per layer: (P*R) x pad4(F_out)
         self.outs = []
         self.selfs = []
-        for L in layers:
+        for li, L in enumerate(layers):
             fo = L.W.shape[1]
-            self.full.append(torch.zeros((P * self.R, _pad4(fo)), dtype=torch.float32, device=device))
+            self.full.append(self.pex.bufs[li][0] if self.pex else
+                             torch.zeros((P * self.R, _pad4(fo)), dtype=torch.float32, device=device))
             self.outs.append(torch.empty((self.rows, fo), dtype=torch.float32, device=device))
             self.selfs.append(torch.empty((self.rows, _pad4(fo)), dtype=torch.float32, device=device)
                               if L.kind == "sage" else None)
@@ -197,16 +308,37 @@ class ShardedModel:
         fo = L.W.shape[1]
         r = self.comm.rank
         self._mark(li, "gemm", "start")
-        ops.matmul(H, L.W, out=self.full[li][r * self.R:r * self.R + self.rows, :fo], mode=self.mode)
+        if self.pex is not None:
+            self.full[li] = buf = self.pex.next_epoch(li)
+            if H.stride(1) != 1 or H.stride(0) % 4 or H.data_ptr() % 16:
+                # the tensor-core GEMM reads H with TMA: 16-byte aligned rows
+                if self.hpad[li] is None or self.hpad[li].shape[0] != H.shape[0]:
+                    self.hpad[li] = torch.zeros((H.shape[0], _pad4(H.shape[1])), dtype=torch.float32,
+                                                device=H.device)
+                self.hpad[li][:, :H.shape[1]] = H
+                H = self.hpad[li][:, :H.shape[1]]
+            outs, flags = self.pex.peer_targets(li, r * self.R * buf.shape[1])
+            ops.gemm_peers(H, L.W, buf[r * self.R:r * self.R + self.rows, :fo], outs, flags, cols_padded=True)
+        else:
+            ops.matmul(H, L.W, out=self.full[li][r * self.R:r * self.R + self.rows, :fo], mode=self.mode)
         if L.kind == "sage":
             ops.matmul(H, L.W_self, out=self.selfs[li][:, :fo], mode=self.mode)
         self._mark(li, "gemm", "end")
 
     def exchange(self, li: int) -> None:
-        """Blocking all-gather (used by single-pass aggregation)."""
+        """Every rank's rows into this rank's gather buffer: the wait for the
+        peers' tiles (peer exchange) or an NCCL all-gather."""
         self._mark(li, "exchange", "start")
-        self.comm.all_gather_rows(self.full[li], self.R)
+        if self.pex is not None:
+            self.pex.wait(li)
+        else:
+            self.comm.all_gather_rows(self.full[li], self.R)
         self._mark(li, "exchange", "end")
+
+    def close(self) -> None:
+        """Unmap the peers' exchange memory (call before the process group ends)."""
+        if self.pex is not None:
+            self.pex.close()
 
     def _pass(self, li: int, A: CSR, lo, hi, carry: bool, last: bool) -> torch.Tensor:
         L = self.layers[li]

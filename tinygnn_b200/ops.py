@@ -423,3 +423,48 @@ def gat_layer(A_sl: CSR, H: torch.Tensor, W: torch.Tensor, a_left: torch.Tensor,
 def take_device_error() -> None:
     """Raise if a tensor-core GEMM pipeline wait timed out since the last call."""
     check(lib.tg_take_device_error(_stream()))
+
+
+# ── Fused GEMM -> exchange over NVLink ──────────────────────────────────────
+def ipc_get_handle(t: torch.Tensor):
+    """(handle bytes, offset): a CUDA IPC handle of the allocation holding t, and t's offset in it."""
+    h = C.create_string_buffer(64)
+    off = C.c_int64()
+    check(lib.tg_ipc_get_handle(_p(t), h, C.byref(off)))
+    return h.raw, off.value
+
+
+def ipc_open_handle(handle: bytes) -> int:
+    """Map another process's allocation; returns its base address here."""
+    base = C.c_void_p()
+    check(lib.tg_ipc_open_handle(C.create_string_buffer(handle, 64), C.byref(base)))
+    return base.value
+
+
+def ipc_close_handle(base: int) -> None:
+    check(lib.tg_ipc_close_handle(C.c_void_p(base)))
+
+
+def gemm_peers(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, peer_out, peer_flags, bias=None, act=None,
+               alpha: float = 0.0, cols_padded: bool = False) -> torch.Tensor:
+    """out = act(A . B + bias) on the tensor cores, every row also stored at
+    the same offset of each peer_out[p] (device addresses of other GPUs'
+    copies, same leading dimension); after each 128-row tile the counter at
+    peer_flags[p] is incremented (release, system scope)."""
+    A, B = _dense(A, "A"), _dense(B, "B")
+    M, K = A.shape
+    N = B.shape[1]
+    n = len(peer_out)
+    pc = (C.c_void_p * max(1, n))(*peer_out)
+    pf = (C.c_void_p * max(1, n))(*peer_flags)
+    b = _vec(bias)
+    check(lib.tg_gemm_peers_f32(M, N, K, _p(A), _ld(A), _p(B), _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha,
+                                n, pc, pf, 0x200 if cols_padded else 0, _stream()))
+    return out
+
+
+def wait_flags(flags: torch.Tensor, targets, timeout_ns: int = 2_000_000_000) -> None:
+    """Device-side wait (in stream order) until flags[i] >= targets[i] for every i (0 = skip)."""
+    n = len(targets)
+    t = (C.c_uint64 * max(1, n))(*targets)
+    check(lib.tg_wait_flags(_p(flags), t, n, int(timeout_ns), _stream()))
