@@ -26,6 +26,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "launch.cuh"
@@ -352,6 +354,236 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
     }
 }
 
+// ── Persistent form ──────────────────────────────────────────────────────
+// One CTA per SM walks the tiles t = blockIdx.x, + gridDim.x, ...  Two TMEM
+// accumulators let tile t's epilogue (including its stores to peer copies)
+// run while tile t+1's k-blocks are loaded, split and multiplied:
+//   warp 0      TMA producer (one ring across tiles);
+//   warp 1      TMEM (2 accumulators) and the MMAs into accumulator t % 2;
+//   warps 2-5   the 3xTF32 split of each A stage;
+//   warps 6-9   the epilogue: 32-column chunks TMEM -> registers -> a
+//               per-warp 32 x 33 staging buffer -> one 128-byte row segment
+//               per store instruction (+ bias, activation), to C and to every
+//               peer copy; the accumulator is released as soon as its last
+//               chunk is read; a tile's peer counters are bumped after its
+//               stores (system-scope fence, release add).
+template <int BN, int STAGES>
+struct TcpSmem {
+    float A[STAGES][BM * BK];
+    float Al[STAGES][BM * BK];
+    float Bh[STAGES][BN * BK];
+    float Bl[STAGES][BN * BK];
+    float out[4][32 * 33];
+    uint64_t full[STAGES], split[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain;
+    uint32_t tmem;
+};
+
+// 128 epilogue threads agree (named barrier 2): true iff every one passed `mine`.
+__device__ __forceinline__ bool epilogue_all(bool mine) {
+    uint32_t all;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.cta.red.and.pred q, 2, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(all)
+        : "r"(static_cast<uint32_t>(mine))
+        : "memory");
+    return all != 0;
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                          const __grid_constant__ CUtensorMap tmBh,
+                                                          const __grid_constant__ CUtensorMap tmBl,
+                                                          const TcArgs g) {
+    extern __shared__ uint8_t raw[];
+    using Smem = TcpSmem<BN, STAGES>;
+    Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+    constexpr uint32_t ACC_COLS = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+    constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+    constexpr uint32_t STAGE_BYTES = (BM * BK + 2 * BN * BK) * 4;
+    constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(BN >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KB = static_cast<int>((g.K + BK - 1) / BK);
+    const int64_t ntiles = (g.M + BM - 1) / BM;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&s.full[i], 1);
+            mbar_init(&s.split[i], 128);
+            mbar_init(&s.empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s.acc_full[i], 1);
+            mbar_init(&s.acc_empty[i], 4);  // lane 0 of each epilogue warp
+        }
+        mbar_init(&s.drain, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s.tmem)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = s.tmem;
+
+    if (warp == 0) {
+        // ── TMA producer ──
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const int st = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (it >= STAGES && !(ok = mbar_wait(&s.empty[st], ph ^ 1, 1))) break;
+                    mbar_expect_tx(&s.full[st], STAGE_BYTES);
+                    tma_load_2d(s.A[st], &tmA, kb * BK, static_cast<int>(tile * BM), &s.full[st]);
+                    tma_load_2d(s.Bh[st], &tmBh, kb * BK, 0, &s.full[st]);
+                    tma_load_2d(s.Bl[st], &tmBl, kb * BK, 0, &s.full[st]);
+                }
+            }
+            // Every copy issued must have landed before the CTA may exit.
+            for (int q = (it > STAGES ? it - STAGES : 0); q < it; ++q)
+                mbar_wait(&s.full[q % STAGES], (q / STAGES) & 1, 2);
+        }
+    } else if (warp == 1) {
+        // ── MMA issuer ──
+        if (lane == 0) {
+            int it = 0, lt = 0;
+            bool ok = true;
+            for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++lt) {
+                const int acc = lt & 1;
+                if (lt >= 2 && !(ok = mbar_wait(&s.acc_empty[acc], ((lt >> 1) & 1) ^ 1, 7))) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t d = tmem + static_cast<uint32_t>(acc) * ACC_COLS;
+                for (int kb = 0; kb < KB; ++kb, ++it) {
+                    const int st = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1;
+                    if (!(ok = mbar_wait(&s.split[st], ph, 3))) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+#pragma unroll
+                    for (int k = 0; k < BK / 8; ++k) {
+                        const uint64_t ah = sw128_desc(s.A[st] + k * 8), al = sw128_desc(s.Al[st] + k * 8);
+                        const uint64_t bh = sw128_desc(s.Bh[st] + k * 8), bl = sw128_desc(s.Bl[st] + k * 8);
+                        mma_tf32(d, al, bh, IDESC, (kb | k) != 0);
+                        mma_tf32(d, ah, bl, IDESC, 1);
+                        mma_tf32(d, ah, bh, IDESC, 1);
+                    }
+                    mma_commit(&s.empty[st]);
+                }
+                if (ok) mma_commit(&s.acc_full[acc]);
+            }
+        }
+    } else if (warp < 6) {
+        // ── split: 128 threads ──
+        const int t = threadIdx.x - 64;
+        int it = 0;
+        bool ok = true;
+        for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            for (int kb = 0; kb < KB; ++kb, ++it) {
+                const int st = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1;
+                if (!(ok = mbar_wait(&s.full[st], ph, 4))) break;
+                float4* a = reinterpret_cast<float4*>(s.A[st]);
+                float4* l = reinterpret_cast<float4*>(s.Al[st]);
+#pragma unroll 4
+                for (int i = t; i < BM * BK / 4; i += 128) {
+                    const float4 x = a[i];
+                    const float4 h = make_float4(tf32_rn(x.x), tf32_rn(x.y), tf32_rn(x.z), tf32_rn(x.w));
+                    a[i] = h;
+                    l[i] = make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z),
+                                       __fsub_rn(x.w, h.w));
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(&s.split[st]);
+            }
+        }
+    } else {
+        // ── epilogue: 128 threads ──
+        const int e = threadIdx.x - 192;
+        const int q = warp & 3;  // this warp's TMEM lane quarter = its 32 rows of a tile
+        float* buf = s.out[warp - 6];
+        int lt = 0;
+        for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
+            const int acc = lt & 1;
+            const bool w = mbar_wait(&s.acc_full[acc], (lt >> 1) & 1, 5);
+            if (!epilogue_all(w)) break;  // all 128 leave together
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t taddr = tmem + static_cast<uint32_t>(acc) * ACC_COLS + (static_cast<uint32_t>(q * 32) << 16);
+            const int64_t r0 = tile * BM + q * 32;
+            const int rows = static_cast<int>(g.M - r0 < 32 ? g.M - r0 : 32);
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                uint32_t r[32];
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+                    "%13, %14, %15}, [%16];"
+                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                      "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                      "=r"(r[15])
+                    : "r"(taddr + c0));
+                if (c0 + 16 < BN)
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+                        "%12, %13, %14, %15}, [%16];"
+                        : "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
+                          "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+                          "=r"(r[30]), "=r"(r[31])
+                        : "r"(taddr + c0 + 16));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (c0 + 32 >= BN) {  // the accumulator is read: the MMA warp may reuse it
+                    asm volatile("tcgen05.fence::before_thread_sync;");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (c0 + j < BN) buf[lane * 33 + j] = __uint_as_float(r[j]);
+                __syncwarp();
+                const int col = c0 + lane;
+                const float bv = (g.bias && col < g.N) ? __ldg(g.bias + col) : 0.0f;
+#pragma unroll 4
+                for (int rr = 0; rr < rows; ++rr) {
+                    if (col < g.ncols) {
+                        float v = buf[rr * 33 + lane];
+                        if (g.bias) v = __fadd_rn(v, bv);
+                        v = apply_act(g.act, v, g.alpha);
+                        const int64_t off = (r0 + rr) * g.ldc + col;
+                        g.C[off] = v;
+                        for (int p = 0; p < g.peers.n; ++p) g.peers.c[p][off] = v;
+                    }
+                }
+                __syncwarp();  // buf is rewritten by the next chunk
+            }
+            if (g.peers.n > 0) {
+                __threadfence_system();
+                if (epilogue_all(true) && e == 0)
+                    for (int p = 0; p < g.peers.n; ++p)
+                        asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(g.peers.flag[p]) : "memory");
+            }
+        }
+    }
+
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 1) {
+        if (lane == 0) {
+            mma_commit(&s.drain);
+            mbar_wait(&s.drain, 0, 6);
+        }
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    }
+}
+
 // B (K x N, ld ldb) -> Bt_hi, Bt_lo (N x Kp, K-major), tf32 round-to-nearest split.
 __global__ void split_bt_kernel(const float* B, int64_t ldb, int64_t K, int64_t N, int64_t Kp, float* hi, float* lo) {
     const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -401,6 +633,35 @@ void launch_tc_s(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap&
     launch("gemm_tc", kern, dim3(static_cast<unsigned>(ceil_div(g.M, BM))), dim3(192), smem, s, a, bh, bl, g);
 }
 
+constexpr int tcp_stages(int BN) {
+    return (192 * 1024) / ((2 * BM * BK + 2 * BN * BK) * 4) > 4 ? 4 : (192 * 1024) / ((2 * BM * BK + 2 * BN * BK) * 4);
+}
+
+template <int BN>
+void launch_tcp(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g, cudaStream_t s) {
+    constexpr int S = tcp_stages(BN);
+    const size_t smem = sizeof(TcpSmem<BN, S>) + 1024;
+    auto kern = gemm_tcp_kernel<BN, S>;
+    TG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    const int64_t tiles = ceil_div(g.M, BM);
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, num_sms()));
+    launch("gemm_tc", kern, dim3(grid), dim3(320), smem, s, a, bh, bl, g);
+}
+
+// Which kernel: the per-tile one unless TINYGNN_B200_GEMM_PERSISTENT=1.  The
+// persistent kernel is correct but measured slower in the GCN forward on
+// B200, both for local output (232,965 x 602 x 128: 0.36 vs 0.33 ms;
+// 232,965 x 128 x 41: 0.16 vs 0.11 ms) and with a peer copy over NVLink
+// (2-GPU forward 3.49 vs 3.37 ms) -- its overlap of epilogue and main loop
+// does not yet pay for its one-CTA-per-SM ring.
+bool use_persistent(bool) {
+    static const bool v = [] {
+        const char* e = std::getenv("TINYGNN_B200_GEMM_PERSISTENT");
+        return e && e[0] == '1';
+    }();
+    return v;
+}
+
 // A deep ring for long K; for short K (a few k-blocks per tile, where one
 // tile's pipeline fill and epilogue dominate) two stages, so that two CTAs
 // share an SM and one's epilogue overlaps the other's main loop (measured:
@@ -439,6 +700,17 @@ void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const
                (N % 4 == 0 || (c_cols_padded && ldc >= n4));
     for (int p = 0; p < peers.n; ++p) vec = vec && reinterpret_cast<uintptr_t>(peers.c[p]) % 16 == 0;
     const TcArgs g{C, ldc, M, N, K, bias, act, alpha, peers, vec ? n4 : N, vec ? 1 : 0};
+    if (use_persistent(peers.n > 0)) {
+        switch (BN) {
+            case 16: launch_tcp<16>(ma, mh, ml, g, s); break;
+            case 32: launch_tcp<32>(ma, mh, ml, g, s); break;
+            case 48: launch_tcp<48>(ma, mh, ml, g, s); break;
+            case 64: launch_tcp<64>(ma, mh, ml, g, s); break;
+            case 128: launch_tcp<128>(ma, mh, ml, g, s); break;
+            default: launch_tcp<256>(ma, mh, ml, g, s); break;
+        }
+        return;
+    }
     switch (BN) {
         case 16: launch_tc<16>(ma, mh, ml, g, s); break;
         case 32: launch_tc<32>(ma, mh, ml, g, s); break;
