@@ -311,11 +311,14 @@ def metric_name(workload):
             f"{NODES} nodes / {EDGES} edges)")
 
 
-def config_dict(args, n, nnz, exchange="nccl"):
+def config_dict(args, n, nnz, exchange="nccl", peer_layers=()):
     if args.gpus > 1 and exchange == "peer":
-        partition = ("1-D equal row blocks; each layer's GEMM stores its output tiles into every GPU's gather "
-                     "buffer over NVLink (peer memory) and signals per tile; each GPU waits for its peers' tiles "
-                     "on the device, then exact gather passes over column ranges")
+        which = "every layer's" if all(peer_layers) else (
+            "layer " + ", ".join(str(i + 1) for i, p in enumerate(peer_layers) if p) + "'s")
+        partition = (f"1-D equal row blocks; {which} GEMM stores its output tiles into every GPU's gather "
+                     "buffer over NVLink (peer memory) and signals per tile, each GPU waiting for its peers' tiles "
+                     "on the device" + ("" if all(peer_layers) else "; the other layers exchange by one in-place "
+                                        "NCCL all-gather") + "; then exact gather passes over column ranges")
     else:
         partition = None
     return {"workload": f"{args.workload}-reddit-shape" + ("-small" if args.small else ""),
@@ -479,7 +482,7 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded Chung-Lu graph, N(0,1) features, Glorot weights, zero bias)",
-            "config": config_dict(args, n, nnz_total, model.exchange_kind),
+            "config": config_dict(args, n, nnz_total, model.exchange_kind, model.peer_layers),
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "edges/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": None if e2e_ms is None else e2e_ms / args.steps,

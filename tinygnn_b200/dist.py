@@ -216,13 +216,23 @@ class ShardedModel:
         # exchange: "peer" = the GEMM stores its tiles straight into every
         # rank's gather buffer over NVLink (PeerExchange; FAST mode, the
         # tensor-core GEMM); "nccl" = GEMM, then an NCCL all-gather or
-        # broadcasts.  "auto" = peer when FAST under a real process group.
+        # broadcasts.  "auto" = peer when FAST under a real process group,
+        # except, on 8+ ranks, for operands under BLOCK_BYTES.  Measured on
+        # B200 (GCN, Reddit-shaped; forward, peer vs NCCL): P = 2 3.37 vs
+        # 3.42 ms, P = 4 2.08 vs 2.20 ms, P = 8 1.443 vs 1.440 ms -- at P = 8
+        # the 119 MB layer-1 exchange is faster fused (GEMM + exchange 0.29
+        # vs 0.32 ms) and the 41 MB layer-2 one slower (0.16 vs 0.13 ms).
         if exchange == "auto":
             exchange = ("peer" if mode == "fast" and getattr(comm, "distributed", False)
                         and all(L.W.shape[1] <= 256 for L in layers) else "nccl")
+            peer_layers = [exchange == "peer" and (comm.world < 8 or n * _pad4(L.W.shape[1]) * 4 >= self.BLOCK_BYTES)
+                           for L in layers]
+        else:
+            peer_layers = [exchange == "peer"] * len(layers)
         if exchange == "peer" and mode != "fast":
             raise ValueError("exchange='peer' runs the tensor-core GEMM: mode must be 'fast'")
         self.exchange_kind = exchange
+        self.peer_layers = peer_layers
         if exchange == "peer":
             pipeline = False
         # pipeline: per-rank async broadcasts with one gather pass per arriving
@@ -308,7 +318,7 @@ class ShardedModel:
         fo = L.W.shape[1]
         r = self.comm.rank
         self._mark(li, "gemm", "start")
-        if self.pex is not None:
+        if self.pex is not None and self.peer_layers[li]:
             self.full[li] = buf = self.pex.next_epoch(li)
             if H.stride(1) != 1 or H.stride(0) % 4 or H.data_ptr() % 16:
                 # the tensor-core GEMM reads H with TMA: 16-byte aligned rows
@@ -329,7 +339,7 @@ class ShardedModel:
         """Every rank's rows into this rank's gather buffer: the wait for the
         peers' tiles (peer exchange) or an NCCL all-gather."""
         self._mark(li, "exchange", "start")
-        if self.pex is not None:
+        if self.pex is not None and self.peer_layers[li]:
             self.pex.wait(li)
         else:
             self.comm.all_gather_rows(self.full[li], self.R)
