@@ -114,16 +114,18 @@ struct TcArgs {
     const float* bias;
     int act;
     float alpha;
-    PeerOut peers;  // n = 0: local output only
     int64_t ncols;  // columns stored: N, or round_up(N, 4) when the rows are padded (vec)
     int vec;        // 16-byte stores (peer copies; ldc % 4 == 0, outputs 16-byte aligned, ncols % 4 == 0)
 };
 
-template <int BN, int STAGES_>
+// PEERS: the epilogue also stores to peer copies (and may use 16-byte
+// stores); false compiles the lean local-only epilogue.
+template <int BN, int STAGES_, bool PEERS>
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                          const __grid_constant__ CUtensorMap tmBh,
                                                          const __grid_constant__ CUtensorMap tmBl,
-                                                         const TcArgs g) {
+                                                         const TcArgs g,
+                                                         const __grid_constant__ PeerOut peers) {
     extern __shared__ uint8_t raw[];
     using Smem = TcSmem<BN, STAGES_>;
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -232,7 +234,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             // slower for local-only output, 0.42 vs 0.33 ms, and faster with
             // one peer, 0.31 vs 0.38 ms.)
             static_assert(BM * (BN + 4) <= STAGES * (2 * BM * BK + 2 * BN * BK), "staging tile exceeds the ring");
-            const int SB = g.vec ? BN + 4 : BN + 1;
+            const bool vec = PEERS && g.vec;
+            const int SB = vec ? BN + 4 : BN + 1;
             float* tile = reinterpret_cast<float*>(&s) + static_cast<size_t>(q) * 32 * SB;  // the ring's start
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                       "=r"(r[15])
                     : "r"(taddr + c0));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (g.vec) {
+                if (vec) {
 #pragma unroll
                     for (int j = 0; j < 16; j += 4)
                         *reinterpret_cast<float4*>(tile + lane * SB + c0 + j) =
@@ -258,7 +261,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             }
             __syncwarp();
             const int rows = static_cast<int>(g.M - (m0 + q * 32) < 32 ? g.M - (m0 + q * 32) : 32);
-            if (g.vec) {
+            if (vec) {
                 constexpr int V4 = (BN / 4 + 31) / 32;  // 4-column groups per lane: lane + 32k
                 float bv[V4][4];
 #pragma unroll
@@ -288,7 +291,9 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                             v.w = apply_act(g.act, v.w, g.alpha);
                             *reinterpret_cast<float4*>(g.C + off + col) = v;
                             // The same row into every peer's copy of the output (NVLink stores).
-                            for (int p = 0; p < g.peers.n; ++p) *reinterpret_cast<float4*>(g.peers.c[p] + off + col) = v;
+                            if (PEERS)
+                                for (int p = 0; p < peers.n; ++p)
+                                    *reinterpret_cast<float4*>(peers.c[p] + off + col) = v;
                         }
                     }
                 }
@@ -311,14 +316,15 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                             if (g.bias) v = __fadd_rn(v, bv[k]);
                             v = apply_act(g.act, v, g.alpha);
                             g.C[off + col] = v;
-                            for (int p = 0; p < g.peers.n; ++p) g.peers.c[p][off + col] = v;
+                            if (PEERS)
+                                for (int p = 0; p < peers.n; ++p) peers.c[p][off + col] = v;
                         }
                     }
                 }
             }
             stored = true;
         }
-        if (g.peers.n > 0) {
+        if (PEERS && peers.n > 0) {
             // Signal each peer once this tile is in its memory: every epilogue
             // thread fences its stores at system scope, the 128 threads meet
             // (and agree that all of them stored), then one thread adds 1 to
@@ -334,8 +340,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                 : "r"(static_cast<uint32_t>(stored))
                 : "memory");
             if (t == 0 && all_stored)
-                for (int p = 0; p < g.peers.n; ++p)
-                    asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(g.peers.flag[p]) : "memory");
+                for (int p = 0; p < peers.n; ++p)
+                    asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(peers.flag[p]) : "memory");
         }
     }
 
@@ -396,7 +402,8 @@ template <int BN, int STAGES>
 __global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant__ CUtensorMap tmA,
                                                           const __grid_constant__ CUtensorMap tmBh,
                                                           const __grid_constant__ CUtensorMap tmBl,
-                                                          const TcArgs g) {
+                                                          const TcArgs g,
+                                                          const __grid_constant__ PeerOut peers) {
     extern __shared__ uint8_t raw[];
     using Smem = TcpSmem<BN, STAGES>;
     Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
@@ -557,16 +564,16 @@ __global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant_
                         v = apply_act(g.act, v, g.alpha);
                         const int64_t off = (r0 + rr) * g.ldc + col;
                         g.C[off] = v;
-                        for (int p = 0; p < g.peers.n; ++p) g.peers.c[p][off] = v;
+                        for (int p = 0; p < peers.n; ++p) peers.c[p][off] = v;
                     }
                 }
                 __syncwarp();  // buf is rewritten by the next chunk
             }
-            if (g.peers.n > 0) {
+            if (peers.n > 0) {
                 __threadfence_system();
                 if (epilogue_all(true) && e == 0)
-                    for (int p = 0; p < g.peers.n; ++p)
-                        asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(g.peers.flag[p]) : "memory");
+                    for (int p = 0; p < peers.n; ++p)
+                        asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(peers.flag[p]) : "memory");
             }
         }
     }
@@ -626,11 +633,12 @@ CUtensorMap make_map(const float* base, int64_t inner, int64_t outer, int64_t ro
 }
 
 template <int BN, int STAGES>
-void launch_tc_s(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g, cudaStream_t s) {
+void launch_tc_s(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g,
+                 const PeerOut& peers, cudaStream_t s) {
     const size_t smem = sizeof(TcSmem<BN, STAGES>) + 1024;
-    auto kern = gemm_tc_kernel<BN, STAGES>;
+    auto kern = peers.n > 0 ? gemm_tc_kernel<BN, STAGES, true> : gemm_tc_kernel<BN, STAGES, false>;
     TG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    launch("gemm_tc", kern, dim3(static_cast<unsigned>(ceil_div(g.M, BM))), dim3(192), smem, s, a, bh, bl, g);
+    launch("gemm_tc", kern, dim3(static_cast<unsigned>(ceil_div(g.M, BM))), dim3(192), smem, s, a, bh, bl, g, peers);
 }
 
 constexpr int tcp_stages(int BN) {
@@ -638,14 +646,15 @@ constexpr int tcp_stages(int BN) {
 }
 
 template <int BN>
-void launch_tcp(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g, cudaStream_t s) {
+void launch_tcp(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g,
+                const PeerOut& peers, cudaStream_t s) {
     constexpr int S = tcp_stages(BN);
     const size_t smem = sizeof(TcpSmem<BN, S>) + 1024;
     auto kern = gemm_tcp_kernel<BN, S>;
     TG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
     const int64_t tiles = ceil_div(g.M, BM);
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, num_sms()));
-    launch("gemm_tc", kern, dim3(grid), dim3(320), smem, s, a, bh, bl, g);
+    launch("gemm_tc", kern, dim3(grid), dim3(320), smem, s, a, bh, bl, g, peers);
 }
 
 // Which kernel: the per-tile one unless TINYGNN_B200_GEMM_PERSISTENT=1.  The
@@ -667,11 +676,12 @@ bool use_persistent(bool) {
 // share an SM and one's epilogue overlaps the other's main loop (measured:
 // the K = 128, N = 41 layer-2 GEMM is latency-bound at one CTA per SM).
 template <int BN>
-void launch_tc(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g, cudaStream_t s) {
+void launch_tc(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g,
+               const PeerOut& peers, cudaStream_t s) {
     constexpr int kShallow = 2;
     constexpr bool two_fit = 2 * (sizeof(TcSmem<BN, kShallow>) + 1024) <= 227 * 1024;
-    if (two_fit && g.K <= 8 * BK) launch_tc_s<BN, two_fit ? kShallow : stages_for(BN)>(a, bh, bl, g, s);
-    else launch_tc_s<BN, stages_for(BN)>(a, bh, bl, g, s);
+    if (two_fit && g.K <= 8 * BK) launch_tc_s<BN, two_fit ? kShallow : stages_for(BN)>(a, bh, bl, g, peers, s);
+    else launch_tc_s<BN, stages_for(BN)>(a, bh, bl, g, peers, s);
 }
 
 }  // namespace
@@ -699,25 +709,25 @@ void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const
     bool vec = peers.n > 0 && ldc % 4 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
                (N % 4 == 0 || (c_cols_padded && ldc >= n4));
     for (int p = 0; p < peers.n; ++p) vec = vec && reinterpret_cast<uintptr_t>(peers.c[p]) % 16 == 0;
-    const TcArgs g{C, ldc, M, N, K, bias, act, alpha, peers, vec ? n4 : N, vec ? 1 : 0};
+    const TcArgs g{C, ldc, M, N, K, bias, act, alpha, vec ? n4 : N, vec ? 1 : 0};
     if (use_persistent(peers.n > 0)) {
         switch (BN) {
-            case 16: launch_tcp<16>(ma, mh, ml, g, s); break;
-            case 32: launch_tcp<32>(ma, mh, ml, g, s); break;
-            case 48: launch_tcp<48>(ma, mh, ml, g, s); break;
-            case 64: launch_tcp<64>(ma, mh, ml, g, s); break;
-            case 128: launch_tcp<128>(ma, mh, ml, g, s); break;
-            default: launch_tcp<256>(ma, mh, ml, g, s); break;
+            case 16: launch_tcp<16>(ma, mh, ml, g, peers, s); break;
+            case 32: launch_tcp<32>(ma, mh, ml, g, peers, s); break;
+            case 48: launch_tcp<48>(ma, mh, ml, g, peers, s); break;
+            case 64: launch_tcp<64>(ma, mh, ml, g, peers, s); break;
+            case 128: launch_tcp<128>(ma, mh, ml, g, peers, s); break;
+            default: launch_tcp<256>(ma, mh, ml, g, peers, s); break;
         }
         return;
     }
     switch (BN) {
-        case 16: launch_tc<16>(ma, mh, ml, g, s); break;
-        case 32: launch_tc<32>(ma, mh, ml, g, s); break;
-        case 48: launch_tc<48>(ma, mh, ml, g, s); break;
-        case 64: launch_tc<64>(ma, mh, ml, g, s); break;
-        case 128: launch_tc<128>(ma, mh, ml, g, s); break;
-        default: launch_tc<256>(ma, mh, ml, g, s); break;
+        case 16: launch_tc<16>(ma, mh, ml, g, peers, s); break;
+        case 32: launch_tc<32>(ma, mh, ml, g, peers, s); break;
+        case 48: launch_tc<48>(ma, mh, ml, g, peers, s); break;
+        case 64: launch_tc<64>(ma, mh, ml, g, peers, s); break;
+        case 128: launch_tc<128>(ma, mh, ml, g, peers, s); break;
+        default: launch_tc<256>(ma, mh, ml, g, peers, s); break;
     }
 }
 
