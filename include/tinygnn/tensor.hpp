@@ -70,6 +70,19 @@ struct Tensor {
     const int32_t* device_col_ind() const;
     std::size_t device_ld() const noexcept;  // dense: device row stride (>= cols)
 
+    // Tensors over caller-owned device memory on the current device (zero
+    // copy; DLPack / torch interop).  The tensor reads and writes that
+    // memory in place and never frees it; `owner` (may be null) is kept
+    // alive while the tensor exists and released after the tensor's pending
+    // device work has finished.  Copies of such a tensor own their memory.
+    // Dense: rows x cols at row stride `ld` >= cols floats.
+    static Tensor dense_from_device(std::size_t rows, std::size_t cols, std::size_t ld, float* data,
+                                    std::shared_ptr<void> owner);
+    // CSR: row_ptr[rows + 1], col_ind[nnz], values[nnz]; validated on the
+    // device with Tensor::sparse_csr's checks and messages.
+    static Tensor sparse_csr_from_device(std::size_t rows, std::size_t cols, std::size_t nnz, int32_t* row_ptr,
+                                         int32_t* col_ind, float* values, std::shared_ptr<void> owner);
+
     struct Impl;
 
 private:

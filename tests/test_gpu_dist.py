@@ -90,12 +90,17 @@ def test_single_gpu_column_passes_are_bit_identical(tg, workload, bpr):
     assert_bits_equal(pip.cpu().numpy(), one.cpu().numpy(), f"{workload} {bpr} blocks (pipelined path)")
 
 
-@pytest.mark.parametrize("workload,mode,blocks", [("gcn", "exact", 8), ("gcn", "fast", 5), ("sage", "fast", 1)])
-def test_forward_from_host_equals_resident_forward(tg, workload, mode, blocks):
+@pytest.mark.parametrize("workload,mode,blocks,unweighted", [("gcn", "exact", 8, False), ("gcn", "fast", 5, False),
+                                                              ("sage", "fast", 1, False), ("gcn", "exact", 8, True),
+                                                              ("sage", "fast", 1, True)])
+def test_forward_from_host_equals_resident_forward(tg, workload, mode, blocks, unweighted):
     """The pipelined host-input call (uploads overlapped with gcn_norm and the
-    per-block layer-1 passes) returns exactly the resident forward's logits."""
+    per-block layer-1 passes) returns exactly the resident forward's logits;
+    an unweighted graph passes no values (1.0 written on the device)."""
     from tinygnn_b200.dist import Comm, Layer, ShardedModel, gcn_norm_rows
     rng, rp, ci, v, X = _graph(seed=11)
+    if unweighted:
+        v = np.ones_like(v)
     n = rp.size - 1
     W0 = torch.as_tensor((rng.standard_normal((40, 32)) * 0.2).astype(np.float32)).cuda()
     W1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
@@ -115,8 +120,8 @@ def test_forward_from_host_equals_resident_forward(tg, workload, mode, blocks):
     h_out = torch.empty((n, 11)).pin_memory()
     bufs = {}
     for _ in range(2):  # buffers reused on the second call
-        model.forward_from_host(pin(A.row_ptr), pin(A.col_ind), pin(A.values), pin(Xd), h_out, bufs,
-                                feature_blocks=blocks)
+        model.forward_from_host(pin(A.row_ptr), pin(A.col_ind), None if unweighted else pin(A.values), pin(Xd),
+                                h_out, bufs, feature_blocks=blocks)
         assert_bits_equal(h_out.numpy(), ref, f"{workload} {mode} from host")
 
 

@@ -296,3 +296,53 @@ def test_loaders_match_the_oracle(tg, tmp_path):
     assert list(cd.labels) == labels.tolist() and list(cd.test_mask) == masks[2].tolist()
     for g_, r_, k in zip(_arrays(cd.adjacency), ref, ("row_ptr", "col_ind", "values")):
         assert_bits_equal(g_, r_, f"CoraData.adjacency.{k}")
+
+
+def test_dlpack_zero_copy_with_torch(tg):
+    """torch CUDA tensors in and out without copies: the same device memory,
+    ops on imported tensors bit-identical to the oracle, in-place ops visible
+    to torch, the producer kept alive by the tensor."""
+    import gc
+
+    import torch
+    rng = np.random.default_rng(21)
+    n, f = 1500, 41
+    rp, ci, v = rand_csr(rng, n, n, 6)
+    X = rng.standard_normal((n, 44)).astype(np.float32)
+    xt = torch.as_tensor(X).cuda()
+    view = xt[:, :f]                        # row stride 44, 41 columns
+    T = tg.Tensor.from_dlpack(view)
+    assert (T.rows, T.cols) == (n, f)
+    back = torch.from_dlpack(T)
+    assert back.data_ptr() == view.data_ptr() and back.stride() == (44, 1)
+    # CSR arrays from torch, used in place and validated on the device
+    d = lambda a: torch.as_tensor(a).cuda()  # noqa: E731
+    A = tg.Tensor.sparse_csr_from_dlpack(n, n, d(rp), d(ci), d(v))
+    ref = P.spmm(rp, ci, v, X[:, :f].copy())
+    assert_bits_equal(tg.spmm(A, T).to_numpy(), ref, "spmm on DLPack tensors")
+    An = tg.gcn_norm(A)
+    for arr, r_, k in zip((An.row_ptr_dlpack(), An.col_ind_dlpack(), An.values_dlpack()),
+                          P.gcn_norm(rp, ci, v), ("row_ptr", "col_ind", "values")):
+        assert_bits_equal(torch.from_dlpack(arr).cpu().numpy(), r_, f"gcn_norm.{k} via DLPack")
+    with pytest.raises(ValueError, match="out of bounds"):
+        bad = ci.copy()
+        bad[7] = n
+        tg.Tensor.sparse_csr_from_dlpack(n, n, d(rp), d(bad), d(v))
+    # in place through the shared memory; the producer outlives its name
+    tg.relu_inplace(T)
+    assert_bits_equal(xt[:, :f].cpu().numpy(), np.maximum(X[:, :f], 0), "relu_inplace seen by torch")
+    assert_bits_equal(xt[:, f:].cpu().numpy(), X[:, f:], "padding columns untouched")
+    del view, back, xt
+    gc.collect()
+    torch.cuda.empty_cache()
+    assert_bits_equal(T.to_numpy(), np.maximum(X[:, :f], 0), "tensor alive after the producer's name is gone")
+    # a host-created tensor exports after its upload
+    H = tg.Tensor.from_numpy(X)
+    assert_bits_equal(torch.from_dlpack(H).cpu().numpy(), X, "export of a host tensor")
+    # a GCN layer whose operands all come from torch
+    W = (rng.standard_normal((f, 16)) * 0.2).astype(np.float32)
+    g = tg.GCNLayer(f, 16, False, tg.Activation.RELU)
+    g.set_weight(tg.Tensor.from_dlpack(d(W)))
+    Xc = np.maximum(X[:, :f], 0)
+    got = torch.from_dlpack(g.forward(An, tg.Tensor.from_dlpack(d(Xc)))).cpu().numpy()
+    assert_bits_equal(got, P.gcn_layer(*P.gcn_norm(rp, ci, v), Xc, W, None, True), "GCNLayer on DLPack tensors")

@@ -210,3 +210,26 @@ def test_host_mirrors_and_csv_parsing(tmp_path):
     assert np.array_equal(tg.GraphLoader.parse_features(str(f)).to_numpy(), [[1, 2], [5, 6], [3, 4]])
     tg.set_num_threads(4)
     assert tg.get_max_threads() == 1
+
+
+def test_dlpack_host_import_copies():
+    """Tensor.from_dlpack of host arrays (NumPy, torch CPU; any strides)
+    copies into a new tensor; the DLPack methods exist with their names."""
+    torch = pytest.importorskip("torch")
+    a = np.arange(12, dtype=np.float32).reshape(3, 4)
+    assert np.array_equal(tg.Tensor.from_dlpack(a).to_numpy(), a)
+    assert np.array_equal(tg.Tensor.from_dlpack(a[:, ::2]).to_numpy(), a[:, ::2])
+    tt = torch.arange(6, dtype=torch.float32).reshape(2, 3).t()
+    assert np.array_equal(tg.Tensor.from_dlpack(tt).to_numpy(), tt.numpy())
+    assert tg.Tensor.from_dlpack(torch.arange(5, dtype=torch.float32)).to_numpy().shape == (1, 5)
+    with pytest.raises(ValueError, match="must be float32"):
+        tg.Tensor.from_dlpack(np.zeros((2, 2), np.float64))
+    with pytest.raises(ValueError, match="expected 1D or 2D array, got 3D"):
+        tg.Tensor.from_dlpack(np.zeros((2, 2, 2), np.float32))
+    with pytest.raises(ValueError, match="DLPack capsule"):
+        tg.Tensor.from_dlpack(object())
+    assert _params(tg.Tensor.from_dlpack) == [("array", None)]
+    assert _params(tg.Tensor.sparse_csr_from_dlpack) == [("rows", None), ("cols", None), ("row_ptr", None),
+                                                         ("col_ind", None), ("values", None)]
+    for name in ("__dlpack__", "__dlpack_device__", "row_ptr_dlpack", "col_ind_dlpack", "values_dlpack"):
+        assert callable(getattr(tg.Tensor, name))

@@ -8,12 +8,19 @@
 //  loaders, GraphData / GraphLoader, set_num_threads / get_max_threads --
 //  same names, argument names and defaults -- bound to this library's C++
 //  mirror (include/tinygnn/*.hpp), so every call runs on the GPU.  Device
-//  work runs with the GIL released.  Additions: set_fast_math / fast_math.
+//  work runs with the GIL released.  Additions: set_fast_math / fast_math,
+//  and zero-copy DLPack interop (torch, CuPy, ...): Tensor.from_dlpack,
+//  Tensor.sparse_csr_from_dlpack, Tensor.__dlpack__ / __dlpack_device__ and
+//  the CSR arrays' *_dlpack capsules.
 // ============================================================================
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -96,6 +103,217 @@ py::array_t<int32_t> int_vector(const std::vector<int32_t>& v) {
     return py::array_t<int32_t>(static_cast<py::ssize_t>(v.size()), v.data());
 }
 
+// ── DLPack (the data-api exchange ABI, v0.8 unversioned capsules) ──────────
+// The structures below are DLPack's published C ABI (dlpack.h), declared
+// here because the toolchain ships no copy of the header.
+enum : int32_t { kDLCPU = 1, kDLCUDA = 2, kDLCUDAHost = 3 };
+enum : uint8_t { kDLInt = 0, kDLFloat = 2 };
+struct DLDevice {
+    int32_t device_type;
+    int32_t device_id;
+};
+struct DLDataType {
+    uint8_t code;
+    uint8_t bits;
+    uint16_t lanes;
+};
+struct DLTensor {
+    void* data;
+    DLDevice device;
+    int32_t ndim;
+    DLDataType dtype;
+    int64_t* shape;
+    int64_t* strides;
+    uint64_t byte_offset;
+};
+struct DLManagedTensor {
+    DLTensor dl_tensor;
+    void* manager_ctx;
+    void (*deleter)(DLManagedTensor*);
+};
+
+int current_device() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) {
+        cudaGetLastError();
+        throw std::runtime_error("tinygnn: no CUDA device (DLPack interop needs one)");
+    }
+    return d;
+}
+
+// Takes ownership of a "dltensor" capsule: renames it "used_dltensor" and
+// returns the managed tensor with a releaser that runs its deleter.
+std::shared_ptr<DLManagedTensor> consume_capsule(const py::object& cap, const char* who) {
+    PyObject* c = cap.ptr();
+    if (!PyCapsule_IsValid(c, "dltensor"))
+        throw std::invalid_argument(std::string(who) + ": expected an unconsumed DLPack capsule (\"dltensor\")");
+    auto* m = static_cast<DLManagedTensor*>(PyCapsule_GetPointer(c, "dltensor"));
+    PyCapsule_SetName(c, "used_dltensor");
+    return std::shared_ptr<DLManagedTensor>(m, [](DLManagedTensor* mt) {
+        if (mt && mt->deleter) {
+            py::gil_scoped_acquire gil;
+            mt->deleter(mt);
+        }
+    });
+}
+
+// The producer's capsule for `obj` (an object with __dlpack__, or a capsule).
+// CUDA producers are asked to order their work before the legacy default
+// stream (DLPack stream 1), which the API's per-thread stream waits on.
+py::object capsule_of(const py::object& obj, bool& on_cuda) {
+    on_cuda = false;
+    if (!py::hasattr(obj, "__dlpack__")) return obj;
+    const auto dev = obj.attr("__dlpack_device__")().cast<std::pair<int, int>>();
+    on_cuda = dev.first == kDLCUDA;
+    if (on_cuda) return obj.attr("__dlpack__")(py::arg("stream") = 1);
+    return obj.attr("__dlpack__")();
+}
+
+void check_dtype(const DLTensor& t, uint8_t code, const char* what, const char* who) {
+    if (t.dtype.code != code || t.dtype.bits != 32 || t.dtype.lanes != 1)
+        throw std::invalid_argument(std::string(who) + ": " + what + " must be " +
+                                    (code == kDLFloat ? "float32" : "int32"));
+}
+
+// A contiguous 1-D int32 / float32 device array of `n` elements.
+template <class T>
+T* device_vector(const DLTensor& t, std::size_t n, uint8_t code, const char* what, const char* who) {
+    check_dtype(t, code, what, who);
+    if (t.device.device_type != kDLCUDA || t.device.device_id != current_device())
+        throw std::invalid_argument(std::string(who) + ": " + what + " must be on the current CUDA device");
+    if (t.ndim != 1 || static_cast<std::size_t>(t.shape[0]) != n)
+        throw std::invalid_argument(std::string(who) + ": " + what + " must be 1-D with " + std::to_string(n) +
+                                    " elements");
+    if (t.strides && t.shape[0] > 1 && t.strides[0] != 1)
+        throw std::invalid_argument(std::string(who) + ": " + what + " must be contiguous");
+    return reinterpret_cast<T*>(static_cast<char*>(t.data) + t.byte_offset);
+}
+
+// Tensor.from_dlpack: CUDA memory is used in place (the producer stays alive
+// as the tensor's owner); host memory is copied into a new tensor.
+Tensor tensor_from_dlpack(const py::object& obj) {
+    const char* who = "Tensor.from_dlpack";
+    bool on_cuda = false;
+    auto m = consume_capsule(capsule_of(obj, on_cuda), who);
+    const DLTensor& t = m->dl_tensor;
+    check_dtype(t, kDLFloat, "the array", who);
+    if (t.ndim != 1 && t.ndim != 2)
+        throw std::invalid_argument(std::string(who) + ": expected 1D or 2D array, got " + std::to_string(t.ndim) +
+                                    "D");
+    const std::size_t rows = t.ndim == 2 ? static_cast<std::size_t>(t.shape[0]) : 1;
+    const std::size_t cols = static_cast<std::size_t>(t.shape[t.ndim - 1]);
+    const int64_t s_col = t.strides ? t.strides[t.ndim - 1] : 1;
+    const int64_t s_row = t.ndim == 2 ? (t.strides ? t.strides[0] : static_cast<int64_t>(cols))
+                                      : static_cast<int64_t>(cols);
+    float* base = reinterpret_cast<float*>(static_cast<char*>(t.data) + t.byte_offset);
+    if (t.device.device_type == kDLCPU || t.device.device_type == kDLCUDAHost) {
+        std::vector<float> host(rows * cols);
+        for (std::size_t r = 0; r < rows; ++r)
+            for (std::size_t c = 0; c < cols; ++c) host[r * cols + c] = base[r * s_row + c * s_col];
+        return Tensor::dense(rows, cols, std::move(host));
+    }
+    if (t.device.device_type != kDLCUDA)
+        throw std::invalid_argument(std::string(who) + ": unsupported device type " +
+                                    std::to_string(t.device.device_type));
+    if (t.device.device_id != current_device())
+        throw std::invalid_argument(std::string(who) + ": the array is on CUDA device " +
+                                    std::to_string(t.device.device_id) + ", not the current device " +
+                                    std::to_string(current_device()));
+    if ((s_col != 1 && cols > 1) || (rows > 1 && s_row < static_cast<int64_t>(cols)))
+        throw std::invalid_argument(std::string(who) + ": a CUDA array needs unit column stride and row stride "
+                                    ">= cols (use .contiguous())");
+    const std::size_t ld = rows > 1 ? static_cast<std::size_t>(s_row) : cols;
+    return Tensor::dense_from_device(rows, cols, ld, base, std::static_pointer_cast<void>(m));
+}
+
+Tensor csr_from_dlpack(std::size_t rows, std::size_t cols, const py::object& rp, const py::object& ci,
+                       const py::object& vals) {
+    const char* who = "Tensor.sparse_csr_from_dlpack";
+    bool c0 = false, c1 = false, c2 = false;
+    auto mrp = consume_capsule(capsule_of(rp, c0), who);
+    auto mci = consume_capsule(capsule_of(ci, c1), who);
+    auto mv = consume_capsule(capsule_of(vals, c2), who);
+    const std::size_t nnz = mci->dl_tensor.ndim == 1 ? static_cast<std::size_t>(mci->dl_tensor.shape[0]) : 0;
+    int32_t* d_rp = device_vector<int32_t>(mrp->dl_tensor, rows + 1, kDLInt, "row_ptr", who);
+    int32_t* d_ci = device_vector<int32_t>(mci->dl_tensor, nnz, kDLInt, "col_ind", who);
+    float* d_v = device_vector<float>(mv->dl_tensor, nnz, kDLFloat, "values", who);
+    auto owner = std::make_shared<std::vector<std::shared_ptr<DLManagedTensor>>>(
+        std::vector<std::shared_ptr<DLManagedTensor>>{mrp, mci, mv});
+    py::gil_scoped_release release;
+    return Tensor::sparse_csr_from_device(rows, cols, nnz, d_rp, d_ci, d_v, std::static_pointer_cast<void>(owner));
+}
+
+// Export: a capsule over the tensor's device memory that keeps the Python
+// tensor alive until the consumer releases it.  Work queued on the API's
+// per-thread stream is ordered before `stream` (DLPack numbering: None or 1
+// = legacy default stream, 2 = per-thread default stream, -1 = no sync,
+// else a cudaStream_t handle).
+struct ExportCtx {
+    py::object keep;
+    int64_t shape[2];
+    int64_t strides[2];
+};
+
+void order_before(const py::object& stream) {
+    if (!stream.is_none() && stream.cast<int64_t>() == -1) return;
+    const int64_t s = stream.is_none() ? 1 : stream.cast<int64_t>();
+    if (s == 2) return;  // the same stream
+    cudaStream_t consumer = s == 1 ? cudaStreamLegacy : reinterpret_cast<cudaStream_t>(s);
+    cudaEvent_t ev;
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventRecord(ev, cudaStreamPerThread) != cudaSuccess || cudaStreamWaitEvent(consumer, ev, 0) != cudaSuccess)
+        throw std::runtime_error("tinygnn: DLPack stream synchronisation failed: " +
+                                 std::string(cudaGetErrorString(cudaGetLastError())));
+    cudaEventDestroy(ev);
+}
+
+py::capsule export_capsule(const py::object& self, void* data, int ndim, int64_t d0, int64_t d1, int64_t s0,
+                           uint8_t code) {
+    auto* ctx = new ExportCtx{self, {d0, d1}, {s0, 1}};
+    auto* m = new DLManagedTensor{};
+    m->dl_tensor.data = data;
+    m->dl_tensor.device = DLDevice{kDLCUDA, current_device()};
+    m->dl_tensor.ndim = ndim;
+    m->dl_tensor.dtype = DLDataType{code, 32, 1};
+    m->dl_tensor.shape = ctx->shape;
+    m->dl_tensor.strides = ndim == 2 ? ctx->strides : nullptr;
+    m->manager_ctx = ctx;
+    m->deleter = [](DLManagedTensor* mt) {
+        py::gil_scoped_acquire gil;
+        delete static_cast<ExportCtx*>(mt->manager_ctx);
+        delete mt;
+    };
+    return py::capsule(m, "dltensor", [](PyObject* cap) {
+        if (PyCapsule_IsValid(cap, "dltensor")) {  // never consumed
+            auto* mt = static_cast<DLManagedTensor*>(PyCapsule_GetPointer(cap, "dltensor"));
+            mt->deleter(mt);
+        }
+    });
+}
+
+py::capsule dense_dlpack(const py::object& self, const py::object& stream) {
+    Tensor& t = self.cast<Tensor&>();
+    if (t.format() != StorageFormat::Dense)
+        throw py::buffer_error("__dlpack__: only Dense tensors export as one array (use the *_dlpack methods of "
+                               "a SparseCSR tensor)");
+    float* p = t.mutable_device_data();  // uploads if needed; the consumer may write
+    order_before(stream);
+    return export_capsule(self, p, 2, static_cast<int64_t>(t.rows()), static_cast<int64_t>(t.cols()),
+                          static_cast<int64_t>(t.device_ld()), kDLFloat);
+}
+
+py::capsule csr_part_dlpack(const py::object& self, int which) {
+    Tensor& t = self.cast<Tensor&>();
+    if (t.format() != StorageFormat::SparseCSR)
+        throw std::invalid_argument("row_ptr_dlpack / col_ind_dlpack / values_dlpack: SparseCSR tensors only");
+    void* p = which == 0 ? static_cast<void*>(const_cast<int32_t*>(t.device_row_ptr()))
+                         : which == 1 ? static_cast<void*>(const_cast<int32_t*>(t.device_col_ind()))
+                                      : static_cast<void*>(const_cast<float*>(t.device_data()));
+    order_before(py::int_(1));
+    const int64_t n = which == 0 ? static_cast<int64_t>(t.rows()) + 1 : static_cast<int64_t>(t.nnz());
+    return export_capsule(self, p, 1, n, 0, 1, which == 2 ? kDLFloat : kDLInt);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(_core, m) {
@@ -145,7 +363,21 @@ PYBIND11_MODULE(_core, m) {
         .def("at", py::overload_cast<std::size_t, std::size_t>(&Tensor::at, py::const_), py::arg("row"),
              py::arg("col"))
         .def("repr", &Tensor::repr)
-        .def("__repr__", &Tensor::repr);
+        .def("__repr__", &Tensor::repr)
+        .def_static("from_dlpack", &tensor_from_dlpack, py::arg("array"))
+        .def_static("sparse_csr_from_dlpack", &csr_from_dlpack, py::arg("rows"), py::arg("cols"),
+                    py::arg("row_ptr"), py::arg("col_ind"), py::arg("values"))
+        .def(
+            "__dlpack__",
+            [](const py::object& self, const py::object& stream, const py::kwargs&) {
+                return dense_dlpack(self, stream);
+            },
+            py::kw_only(), py::arg("stream") = py::none())
+        .def("__dlpack_device__",
+             [](const Tensor&) { return std::make_pair(static_cast<int>(kDLCUDA), current_device()); })
+        .def("row_ptr_dlpack", [](const py::object& self) { return csr_part_dlpack(self, 0); })
+        .def("col_ind_dlpack", [](const py::object& self) { return csr_part_dlpack(self, 1); })
+        .def("values_dlpack", [](const py::object& self) { return csr_part_dlpack(self, 2); });
 
     m.def("matmul", &matmul, py::arg("A"), py::arg("B"), Release());
     m.def("spmm", &spmm, py::arg("A"), py::arg("B"), Release());

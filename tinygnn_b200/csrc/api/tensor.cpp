@@ -53,7 +53,17 @@ struct Tensor::Impl {
     mutable bool device_valid = false;
     std::size_t ld = 0;  // dense device row stride
 
+    // Set for tensors over caller-owned device memory: the buffers are not
+    // ours to free, and the owner goes only after our queued work is done.
+    std::shared_ptr<void> owner;
+    bool external = false;
+
     ~Impl() {
+        if (external) {
+            if (cudaStreamSynchronize(detail::cstream()) != cudaSuccess) cudaGetLastError();
+            owner.reset();
+            return;
+        }
         dev_free(d_data);
         dev_free(d_rp);
         dev_free(d_ci);
@@ -240,6 +250,47 @@ Tensor Tensor::sparse_csr(std::size_t rows, std::size_t cols, std::vector<int32_
     p->h_rp = std::move(row_ptr);
     p->h_ci = std::move(col_ind);
     p->h_data = std::move(values);
+    return Tensor(std::move(p));
+}
+
+Tensor Tensor::dense_from_device(std::size_t rows, std::size_t cols, std::size_t ld, float* data,
+                                 std::shared_ptr<void> owner) {
+    if (ld < cols)
+        throw std::invalid_argument("Tensor::dense_from_device: row stride " + std::to_string(ld) + " < cols (" +
+                                    std::to_string(cols) + ")");
+    if (!data && rows && cols) throw std::invalid_argument("Tensor::dense_from_device: null data");
+    auto p = std::make_unique<Impl>();
+    p->format = StorageFormat::Dense;
+    p->shape = {rows, cols};
+    p->strides = {cols, 1};
+    p->ld = ld;
+    p->d_data = data;
+    p->device_valid = true;
+    p->host_valid = false;
+    p->owner = std::move(owner);
+    p->external = true;
+    return Tensor(std::move(p));
+}
+
+Tensor Tensor::sparse_csr_from_device(std::size_t rows, std::size_t cols, std::size_t nnz, int32_t* row_ptr,
+                                      int32_t* col_ind, float* values, std::shared_ptr<void> owner) {
+    if (!row_ptr || ((!col_ind || !values) && nnz))
+        throw std::invalid_argument("Tensor::sparse_csr_from_device: null array");
+    detail::check(tg_csr_validate(static_cast<int64_t>(rows), static_cast<int64_t>(cols), static_cast<int64_t>(nnz),
+                                  row_ptr, col_ind, detail::stream()));
+    auto p = std::make_unique<Impl>();
+    p->format = StorageFormat::SparseCSR;
+    p->shape = {rows, cols};
+    p->strides = {};
+    p->nnz = nnz;
+    p->d_rp = row_ptr;
+    p->d_ci = col_ind;
+    p->d_data = values;
+    p->device_valid = true;
+    p->host_valid = false;
+    p->host_struct_valid = false;
+    p->owner = std::move(owner);
+    p->external = true;
     return Tensor(std::move(p));
 }
 

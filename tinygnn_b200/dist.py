@@ -408,16 +408,20 @@ class ShardedModel:
         self._mark(li, "gather", "end")
         return H
 
-    def forward_from_host(self, h_rp: torch.Tensor, h_ci: torch.Tensor, h_v: torch.Tensor, h_X: torch.Tensor,
-                          h_out: torch.Tensor, bufs: dict, feature_blocks: int = 8) -> torch.Tensor:
+    def forward_from_host(self, h_rp: torch.Tensor, h_ci: torch.Tensor, h_v: Optional[torch.Tensor],
+                          h_X: torch.Tensor, h_out: torch.Tensor, bufs: dict,
+                          feature_blocks: int = 8) -> torch.Tensor:
         """The whole call from host inputs: raw CSR rows + feature rows (pinned
         host tensors of this rank) in, logits (pinned host tensor) out.
 
-        Uploads are queued first on a copy stream (CSR, then the features in
-        row blocks); gcn_norm runs as soon as the CSR is in, while the
-        features stream; on one GPU the first layer's GEMM and exact gather
-        pass for feature block q start when block q has landed.  ``bufs``
-        holds the device buffers across calls (filled on first use).
+        ``h_v = None`` is an unweighted graph: every stored value is 1.0 (what
+        edge_list_to_csr and from_edge_index produce), written on the device
+        instead of crossing PCIe.  Uploads are queued first on a copy stream
+        (CSR, then the features in row blocks); gcn_norm runs as soon as the
+        CSR is in, while the features stream; on one GPU the first layer's
+        GEMM and exact gather pass for feature block q start when block q has
+        landed.  ``bufs`` holds the device buffers across calls (filled on
+        first use).
         """
         dev = self.device
         cur = torch.cuda.current_stream()
@@ -426,7 +430,7 @@ class ShardedModel:
             cp = bufs["stream"] = torch.cuda.Stream(device=dev)
             bufs["rp"] = torch.empty_like(h_rp, device=dev)
             bufs["ci"] = torch.empty_like(h_ci, device=dev)
-            bufs["v"] = torch.empty_like(h_v, device=dev)
+            bufs["v"] = torch.empty(h_ci.shape, dtype=torch.float32, device=dev)
             bufs["X"] = torch.zeros((self.rows, _pad4(h_X.shape[1])), dtype=torch.float32, device=dev)
             bufs["dis"] = torch.zeros(self.R * self.comm.world, dtype=torch.float32, device=dev)
         d_rp, d_ci, d_v, d_X = bufs["rp"], bufs["ci"], bufs["v"], bufs["X"][:, :h_X.shape[1]]
@@ -438,7 +442,8 @@ class ShardedModel:
         with torch.cuda.stream(cp):
             d_rp.copy_(h_rp, non_blocking=True)
             d_ci.copy_(h_ci, non_blocking=True)
-            d_v.copy_(h_v, non_blocking=True)
+            if h_v is not None:
+                d_v.copy_(h_v, non_blocking=True)
             csr_ready = torch.cuda.Event()
             csr_ready.record(cp)
             for q in range(nb):
@@ -448,6 +453,8 @@ class ShardedModel:
                 ev = torch.cuda.Event()
                 ev.record(cp)
                 x_ready.append(ev)
+        if h_v is None:  # on the compute stream, while the uploads run
+            d_v.fill_(1.0)
         cur.wait_event(csr_ready)
         A = CSR(self.rows, self.n, d_rp, d_ci, d_v)
         A_gcn = (gcn_norm_rows(A, self.row0, self.R, self.comm, bufs["dis"])
