@@ -90,21 +90,23 @@ def test_single_gpu_column_passes_are_bit_identical(tg, workload, bpr):
     assert_bits_equal(pip.cpu().numpy(), one.cpu().numpy(), f"{workload} {bpr} blocks (pipelined path)")
 
 
-@pytest.mark.parametrize("workload,mode,blocks,unweighted", [("gcn", "exact", 8, False), ("gcn", "fast", 5, False),
-                                                              ("sage", "fast", 1, False), ("gcn", "exact", 8, True),
-                                                              ("sage", "fast", 1, True)])
-def test_forward_from_host_equals_resident_forward(tg, workload, mode, blocks, unweighted):
+@pytest.mark.parametrize("workload,mode,blocks,unweighted,fin,chunks", [
+    ("gcn", "exact", 8, False, 40, 4), ("gcn", "fast", 5, False, 40, 1), ("sage", "fast", 1, False, 40, 4),
+    ("gcn", "exact", 8, True, 37, 3), ("gcn", "fast", 8, True, 37, 4), ("sage", "fast", 1, True, 37, 7)])
+def test_forward_from_host_equals_resident_forward(tg, workload, mode, blocks, unweighted, fin, chunks):
     """The pipelined host-input call (uploads overlapped with gcn_norm and the
-    per-block layer-1 passes) returns exactly the resident forward's logits;
-    an unweighted graph passes no values (1.0 written on the device)."""
+    per-block layer-1 passes; features of a width that is not a multiple of 4
+    repacked on the device; the last layer in row chunks whose logits stream
+    back) returns exactly the resident forward's logits; an unweighted graph
+    passes no values (1.0 written on the device)."""
     from tinygnn_b200.dist import Comm, Layer, ShardedModel, gcn_norm_rows
     rng, rp, ci, v, X = _graph(seed=11)
     if unweighted:
         v = np.ones_like(v)
     n = rp.size - 1
-    W0 = torch.as_tensor((rng.standard_normal((40, 32)) * 0.2).astype(np.float32)).cuda()
+    W0 = torch.as_tensor((rng.standard_normal((fin, 32)) * 0.2).astype(np.float32)).cuda()
     W1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
-    S0 = torch.as_tensor((rng.standard_normal((40, 32)) * 0.2).astype(np.float32)).cuda()
+    S0 = torch.as_tensor((rng.standard_normal((fin, 32)) * 0.2).astype(np.float32)).cuda()
     S1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
     b0 = torch.as_tensor((rng.standard_normal(32) * 0.1).astype(np.float32)).cuda()
     sage = workload == "sage"
@@ -112,16 +114,17 @@ def test_forward_from_host_equals_resident_forward(tg, workload, mode, blocks, u
               Layer(workload, W1, None, None, S1 if sage else None)]
     model = ShardedModel(layers, n, Comm(1, 0), "cuda", mode=mode)
     A = tg.CSR.from_numpy(rp, ci, v)
-    Xd = torch.zeros((n, 40), device="cuda")
-    Xd[:] = torch.as_tensor(X).cuda()
+    Xd = torch.zeros((n, (fin + 3) // 4 * 4), device="cuda")[:, :fin]
+    Xd[:] = torch.as_tensor(X[:, :fin]).cuda()
     An = gcn_norm_rows(A, 0, n, Comm(1, 0)) if not sage else None
     ref = model.forward(An, A, Xd).cpu().numpy().copy()
     pin = lambda t: t.cpu().pin_memory()  # noqa: E731
     h_out = torch.empty((n, 11)).pin_memory()
     bufs = {}
     for _ in range(2):  # buffers reused on the second call
+        h_out.zero_()
         model.forward_from_host(pin(A.row_ptr), pin(A.col_ind), None if unweighted else pin(A.values), pin(Xd),
-                                h_out, bufs, feature_blocks=blocks)
+                                h_out, bufs, feature_blocks=blocks, out_chunks=chunks)
         assert_bits_equal(h_out.numpy(), ref, f"{workload} {mode} from host")
 
 

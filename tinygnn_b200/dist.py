@@ -410,7 +410,7 @@ class ShardedModel:
 
     def forward_from_host(self, h_rp: torch.Tensor, h_ci: torch.Tensor, h_v: Optional[torch.Tensor],
                           h_X: torch.Tensor, h_out: torch.Tensor, bufs: dict,
-                          feature_blocks: int = 8) -> torch.Tensor:
+                          feature_blocks: int = 8, out_chunks: int = 2) -> torch.Tensor:
         """The whole call from host inputs: raw CSR rows + feature rows (pinned
         host tensors of this rank) in, logits (pinned host tensor) out.
 
@@ -420,8 +420,14 @@ class ShardedModel:
         (CSR, then the features in row blocks); gcn_norm runs as soon as the
         CSR is in, while the features stream; on one GPU the first layer's
         GEMM and exact gather pass for feature block q start when block q has
-        landed.  ``bufs`` holds the device buffers across calls (filled on
-        first use).
+        landed.  Feature rows whose width is not a multiple of 4 land in a
+        contiguous buffer and are repacked on the device to the 16-byte row
+        stride the tensor-core GEMM reads (a pitched host-to-device copy of
+        2,408-byte rows is slower than the repack).  The last layer's gather,
+        when it is one pass, runs in ``out_chunks`` row chunks, each with its
+        own longest-rows-first schedule, and each chunk's logits go back to
+        the host while the next chunk gathers.  ``bufs`` holds the device
+        buffers across calls (filled on first use).
         """
         dev = self.device
         cur = torch.cuda.current_stream()
@@ -432,8 +438,12 @@ class ShardedModel:
             bufs["ci"] = torch.empty_like(h_ci, device=dev)
             bufs["v"] = torch.empty(h_ci.shape, dtype=torch.float32, device=dev)
             bufs["X"] = torch.zeros((self.rows, _pad4(h_X.shape[1])), dtype=torch.float32, device=dev)
+            if h_X.shape[1] % 4:
+                bufs["X_landing"] = torch.empty((self.rows, h_X.shape[1]), dtype=torch.float32, device=dev)
             bufs["dis"] = torch.zeros(self.R * self.comm.world, dtype=torch.float32, device=dev)
         d_rp, d_ci, d_v, d_X = bufs["rp"], bufs["ci"], bufs["v"], bufs["X"][:, :h_X.shape[1]]
+        landing = bufs.get("X_landing")
+        x_dst = d_X if landing is None else landing
         single = self.comm.world == 1 and self.layers[0].kind == "gcn"
         nb = max(1, feature_blocks) if single else 1
         width = (self.rows + nb - 1) // nb
@@ -449,7 +459,7 @@ class ShardedModel:
             for q in range(nb):
                 a, b = q * width, min(self.rows, (q + 1) * width)
                 if a < b:
-                    d_X[a:b].copy_(h_X[a:b], non_blocking=True)
+                    x_dst[a:b].copy_(h_X[a:b], non_blocking=True)
                 ev = torch.cuda.Event()
                 ev.record(cp)
                 x_ready.append(ev)
@@ -471,6 +481,8 @@ class ShardedModel:
                 a, b = q * width, min(self.rows, (q + 1) * width)
                 cur.wait_event(x_ready[q])
                 if a < b:
+                    if landing is not None:
+                        d_X[a:b].copy_(landing[a:b])
                     ops.matmul(d_X[a:b], L.W, out=self.full[0][a:b, :fo], mode=self.mode)
                 ops.spmm_segment(A_gcn, B, sp[q], sp[q + 1], self.outs[0], q > 0, q == nb - 1, bias=L.b,
                                  act=L.act)
@@ -479,14 +491,58 @@ class ShardedModel:
         else:
             for ev in x_ready:
                 cur.wait_event(ev)
+            if landing is not None:
+                d_X.copy_(landing)
             H, first = d_X, 0
-        for li in range(first, len(self.layers)):
+        last = len(self.layers) - 1
+        for li in range(first, last):
             self.transform(li, H)
             H = self.exchange_and_aggregate(li, A_gcn, A)
-        ops.log_softmax_(H)
-        h_out.copy_(H, non_blocking=True)
+        if first > last:
+            ops.log_softmax_(H)
+            h_out.copy_(H, non_blocking=True)
+        elif self.pipe[last] or self.pass_splits(A_gcn if self.layers[last].kind == "gcn" else A,
+                                                 self.passes[last]) is not None or out_chunks <= 1:
+            self.transform(last, H)
+            H = self.exchange_and_aggregate(last, A_gcn, A)
+            ops.log_softmax_(H)
+            h_out.copy_(H, non_blocking=True)
+        else:
+            self.transform(last, H)
+            self.exchange(last)
+            self._chunked_last_layer(A_gcn, A, h_out, cp, out_chunks)
         cur.synchronize()
         return h_out
+
+    def _chunked_last_layer(self, A_gcn: Optional[CSR], A_raw: CSR, h_out: torch.Tensor,
+                            cp: torch.cuda.Stream, chunks: int) -> None:
+        """The last layer's single-pass gather over row chunks (row-offset
+        views of the CSR, each with its own degree order), log_softmax per
+        chunk, and each chunk's logits copied out on `cp` while the next
+        chunk gathers.  Per row the same arithmetic as one launch."""
+        li = len(self.layers) - 1
+        L = self.layers[li]
+        fo = L.W.shape[1]
+        A = A_gcn if L.kind == "gcn" else A_raw
+        B = self.full[li][:self.n, :fo]
+        cur = torch.cuda.current_stream()
+        step = -(-self.rows // chunks)
+        for a in range(0, self.rows, step):
+            b = min(self.rows, a + step)
+            Ak = CSR(b - a, A.n_cols, A.row_ptr[a:b + 1], A.col_ind, A.values)
+            Ak.order = ops.degree_order(Ak)
+            out = self.outs[li][a:b]
+            if L.kind == "gcn":
+                ops.spmm(Ak, B, bias=L.b, act=L.act, out=out)
+            else:
+                ops.sage_mean_combine(Ak, B, self.selfs[li][a:b, :fo], bias=L.b, act=L.act, out=out)
+            ops.log_softmax_(out)
+            done = torch.cuda.Event()
+            done.record(cur)
+            cp.wait_event(done)
+            with torch.cuda.stream(cp):
+                h_out[a:b].copy_(out, non_blocking=True)
+        cur.wait_stream(cp)
 
     def forward(self, A_gcn: Optional[CSR], A_raw: Optional[CSR], X: torch.Tensor,
                 log_softmax: bool = True) -> torch.Tensor:
