@@ -67,6 +67,29 @@ def main() -> int:
         if rank == 0:
             print(f"peer exchange step {step} same={same}", flush=True)
         ok = ok and same
+    # The host-input call on every rank (its rows from pinned host memory,
+    # features of a width that is not a multiple of 4, the last layer in row
+    # chunks) against the same model's resident forward, with either exchange.
+    Xh = synth.normal_rows(r0, r1 - r0, 61, 8, 0, dev)
+    Xd = torch.zeros((r1 - r0, 64), device=dev)[:, :61]
+    Xd[:] = Xh
+    W61 = synth.glorot(61, 32, 7, 3, dev)
+    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+    h_v = None if bool(torch.all(A.values == 1.0)) else pin(A.values)
+    for kind in ("nccl", "peer"):
+        m = ShardedModel([Layer("gcn", W61, b0, "relu"), Layer("gcn", W1, b1, None)], n, comm, dev, mode="fast",
+                         exchange=kind)
+        want = m.forward(An, A, Xd).clone()
+        h_out = torch.empty((r1 - r0, 9)).pin_memory()
+        bufs = {}
+        for step in range(2):
+            h_out.zero_()
+            m.forward_from_host(pin(A.row_ptr), pin(A.col_ind), h_v, pin(Xd), h_out, bufs)
+            same = bool(torch.equal(h_out.to(dev), want))
+            if rank == 0:
+                print(f"forward_from_host {kind} step {step} same={same}", flush=True)
+            ok = ok and same
+        m.close()
     tg.ops.take_device_error()
     peer.close()
     if rank == 0:
