@@ -8,7 +8,7 @@ import::
     import tinygnn_b200.tinygnn as tinygnn
 
     X = tinygnn.Tensor.from_numpy(features)            # copied into HBM
-    A = tinygnn.gcn_norm(tinygnn.Tensor.from_scipy_csr(adj))
+    A = tinygnn.Tensor.from_scipy_csr(adj)            # raw adjacency
     model = tinygnn.Model()
     model.add_gcn_layer(1433, 16)
     model.add_gcn_layer(16, 7, act=tinygnn.Activation.NONE)
