@@ -14,7 +14,8 @@ Sizes (the configurations of the headline benchmark's suite): R-MAT
 SAGE on a symmetrised R-MAT of 2^18 nodes, 128 -> 128 -> 40; GAT on an
 R-MAT of 2^20 nodes stored incoming plus self-loops, 256 -> 8 heads x 8
 (concat, ELU) -> 16; GCN layer 1 of the Reddit-shaped graph (232,965 nodes,
-114,615,892 edges, 602 -> 128).
+114,615,892 edges, 602 -> 128); and the Cora-shaped GCN model whole
+(2,708 nodes, 1433 -> 16 -> 7), every row.
 """
 import numpy as np
 import pytest
@@ -157,3 +158,25 @@ def test_gcn_layer1_reddit_shape(tg):
     assert_bits_equal(_host(out[rows]), ref, "gather rows (nnz 114,848,857, F = 128)")
     fused = tg.gcn_layer(An, X, W, b, "relu")
     assert torch.equal(fused.view(torch.int32), out.view(torch.int32)), "gcn_layer != matmul + spmm"
+
+
+def test_gcn_cora_shape_full_model(tg):
+    """The Cora-shaped configuration whole: gcn_norm, GCN 1433 -> 16 (ReLU)
+    -> 7, log_softmax, exact mode -- every row against the oracle (and the
+    reference library itself where it was built)."""
+    from tinygnn_b200 import synth
+    n, rp, ci, v, X = synth.cora_like(device="cuda")
+    W0, W1 = synth.glorot(1433, 16, 2, 1, "cuda"), synth.glorot(16, 7, 2, 2, "cuda")
+    b0, b1 = torch.zeros(16, device="cuda"), torch.zeros(7, device="cuda")
+    An = tg.gcn_norm(tg.CSR(n, n, rp, ci, v))
+    H1 = tg.gcn_layer(An, X, W0, b0, "relu")
+    logits = tg.gcn_layer(An, H1, W1, b1, None)
+    out = tg.log_softmax_(logits.clone())
+    hrp, hci, hv = _host(rp).astype(np.int32), _host(ci).astype(np.int32), _host(v)
+    spec = [dict(type="gcn", **{"in": 1433, "out": 16}, act="relu"), dict(type="gcn", **{"in": 16, "out": 7})]
+    w = {"layer0.weight": _host(W0), "layer0.bias": _host(b0), "layer1.weight": _host(W1), "layer1.bias": _host(b1)}
+    for impl in [P] + ([oracle.ref] if oracle.ref is not None else []):
+        ref = oracle.model_forward(impl, spec, w, hrp, hci, hv, _host(X))
+        assert_bits_equal(_host(logits), ref, f"Cora-shaped GCN logits vs {impl.name}")
+        assert_close(_host(out), impl.activation("log_softmax", ref), f"Cora-shaped log_softmax vs {impl.name}")
+    assert int(An.nnz) == 13_264 and n == 2708
