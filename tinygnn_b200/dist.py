@@ -526,7 +526,7 @@ class ShardedModel:
         A = A_gcn if L.kind == "gcn" else A_raw
         B = self.full[li][:self.n, :fo]
         cur = torch.cuda.current_stream()
-        step = -(-self.rows // chunks)
+        step = max(1, -(-self.rows // chunks))  # a rank may own no rows
         for a in range(0, self.rows, step):
             b = min(self.rows, a + step)
             Ak = CSR(b - a, A.n_cols, A.row_ptr[a:b + 1], A.col_ind, A.values)
