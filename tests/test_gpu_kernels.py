@@ -362,6 +362,23 @@ def test_activations_and_softmax_vs_oracle(tg):
         tg.softmax_(torch.zeros((3, 0), device="cuda"))
 
 
+@pytest.mark.parametrize("rows,cols,ld", [(1, 1, 1), (129, 7, 7), (1000, 41, 44), (300, 64, 64), (300, 65, 65),
+                                          (257, 128, 130), (100, 129, 129), (70, 256, 256), (33, 257, 257),
+                                          (5, 600, 602)])
+def test_row_softmax_shapes(tg, rows, cols, ld):
+    """Row softmax / log_softmax across the staged-tile sizes (128 / 64 / 32
+    rows for up to 64 / 128 / 256 columns, partial last tiles, strided rows)
+    and the wide-row kernel, against the oracle; padding columns untouched."""
+    rng = np.random.default_rng(rows * 1000 + cols)
+    X = (rng.standard_normal((rows, ld)) * 4).astype(np.float32)
+    for kind, fn in (("softmax", tg.softmax_), ("log_softmax", tg.log_softmax_)):
+        T = dev(X)
+        fn(T[:, :cols])
+        got = host(T)
+        assert_close(got[:, :cols], P.activation(kind, X[:, :cols].copy()), f"{kind} {rows}x{cols}")
+        assert_bits_equal(got[:, cols:], X[:, cols:], "padding columns")
+
+
 def test_edge_softmax_vs_oracle(tg):
     rng = np.random.default_rng(4)
     rp, ci, v = powerlaw_csr(rng, 5000, 12)

@@ -35,12 +35,10 @@ __global__ void add_bias_kernel(float* X, int64_t rows, int64_t cols, int64_t ld
     }
 }
 
-// softmax (ops.cpp:525-547) / log_softmax (ops.cpp:584-604), one row per thread.
+// softmax (ops.cpp:525-547) / log_softmax (ops.cpp:584-604) of one row in
+// place, in the reference's order: max, then the exp sum left to right.
 template <bool LOG>
-__global__ void row_softmax_kernel(float* X, int64_t rows, int64_t cols, int64_t ld) {
-    const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (r >= rows) return;
-    float* row = X + r * ld;
+__device__ __forceinline__ void softmax_row(float* row, int64_t cols) {
     float mx = row[0];
     for (int64_t j = 1; j < cols; ++j)
         if (row[j] > mx) mx = row[j];
@@ -58,6 +56,86 @@ __global__ void row_softmax_kernel(float* X, int64_t rows, int64_t cols, int64_t
         const float inv = __fdiv_rn(1.0f, s);
         for (int64_t j = 0; j < cols; ++j) row[j] = __fmul_rn(row[j], inv);
     }
+}
+
+// Rows of up to 256 columns: a block of TR threads stages TR rows in shared
+// memory (TR = 128 / 64 / 32 for up to 64 / 128 / 256 columns, ~33 KB),
+// each thread runs softmax_row on its row there (odd stride: no bank
+// conflicts), and the rows go back.  Both copies walk the block's elements
+// in row-major order, TR threads apart (consecutive threads touch
+// consecutive columns: coalesced), eight independent loads ahead.
+constexpr int kCopyAhead = 8;
+
+// Element position (row, col) of flat index t + k * step, advanced without
+// a division per step.
+struct TilePos {
+    int r, c, qr, qc, cols;
+    __device__ TilePos(int t, int cols_, int step) : r(t / cols_), c(t % cols_), qr(step / cols_),
+                                                     qc(step % cols_), cols(cols_) {}
+    __device__ void next() {
+        r += qr;
+        c += qc;
+        if (c >= cols) {
+            c -= cols;
+            ++r;
+        }
+    }
+};
+
+template <bool LOG, int TR>
+__global__ void __launch_bounds__(TR) row_softmax_tile_kernel(float* X, int64_t rows, int64_t cols, int64_t ld) {
+    extern __shared__ float tile[];
+    const int nc = static_cast<int>(cols);
+    const int stride = nc | 1;
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * TR;
+    const int nr = static_cast<int>(min(static_cast<int64_t>(TR), rows - r0));
+    const int total = nr * nc;
+    float* base = X + r0 * ld;
+    {
+        TilePos p(threadIdx.x, nc, TR);
+        for (int i = threadIdx.x; i < total; i += kCopyAhead * TR) {
+            float v[kCopyAhead];
+            TilePos q = p;
+#pragma unroll
+            for (int u = 0; u < kCopyAhead; ++u) {
+                if (i + u * TR < total) v[u] = base[q.r * ld + q.c];
+                q.next();
+            }
+#pragma unroll
+            for (int u = 0; u < kCopyAhead; ++u) {
+                if (i + u * TR < total) tile[p.r * stride + p.c] = v[u];
+                p.next();
+            }
+        }
+    }
+    __syncthreads();
+    if (static_cast<int>(threadIdx.x) < nr) softmax_row<LOG>(tile + threadIdx.x * stride, cols);
+    __syncthreads();
+    {
+        TilePos p(threadIdx.x, nc, TR);
+        for (int i = threadIdx.x; i < total; i += kCopyAhead * TR) {
+            float v[kCopyAhead];
+            TilePos q = p;
+#pragma unroll
+            for (int u = 0; u < kCopyAhead; ++u) {
+                if (i + u * TR < total) v[u] = tile[q.r * stride + q.c];
+                q.next();
+            }
+#pragma unroll
+            for (int u = 0; u < kCopyAhead; ++u) {
+                if (i + u * TR < total) base[p.r * ld + p.c] = v[u];
+                p.next();
+            }
+        }
+    }
+}
+
+// Wider rows: one row per thread in global memory.
+template <bool LOG>
+__global__ void row_softmax_kernel(float* X, int64_t rows, int64_t cols, int64_t ld) {
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    softmax_row<LOG>(X + r * ld, cols);
 }
 
 // edge_softmax (layers.cpp:791-812), one CSR row per thread.
@@ -101,6 +179,17 @@ void add_bias(float* X, int64_t rows, int64_t cols, int64_t ld, const float* b, 
 void row_softmax(bool log, float* X, int64_t rows, int64_t cols, int64_t ld, cudaStream_t s) {
     if (rows == 0) return;
     const dim3 grid(static_cast<unsigned>(ceil_div(rows, 128)));
+    if (cols <= 256) {
+        const int tr = cols <= 64 ? 128 : (cols <= 128 ? 64 : 32);
+        const dim3 tgrid(static_cast<unsigned>(ceil_div(rows, tr)));
+        const size_t smem = static_cast<size_t>(tr) * (static_cast<size_t>(cols) | 1) * sizeof(float);
+        auto kern = log ? (tr == 128 ? row_softmax_tile_kernel<true, 128>
+                           : tr == 64 ? row_softmax_tile_kernel<true, 64> : row_softmax_tile_kernel<true, 32>)
+                        : (tr == 128 ? row_softmax_tile_kernel<false, 128>
+                           : tr == 64 ? row_softmax_tile_kernel<false, 64> : row_softmax_tile_kernel<false, 32>);
+        launch(log ? "log_softmax" : "softmax", kern, tgrid, dim3(tr), smem, s, X, rows, cols, ld);
+        return;
+    }
     if (log) launch("log_softmax", row_softmax_kernel<true>, grid, dim3(128), 0, s, X, rows, cols, ld);
     else launch("softmax", row_softmax_kernel<false>, grid, dim3(128), 0, s, X, rows, cols, ld);
 }
