@@ -22,7 +22,8 @@ Reported (rank 0, one JSON line):
           nnz*(8+4F) + rows*(4+4F) + 4 per launch / its CUDA-event time,
           against the measured HBM copy bandwidth (MEASURED_PEAKS.json);
   cpu_baseline  the reference library (oracle/_ref) Model::forward on the
-          same graph on this host's cores (rank 0, N = 1).
+          same graph on this host's cores (rank 0, N = 1), and beside it
+          (layers_only) its layer objects on an adjacency normalised once.
 --impl reference times that reference forward alone (rank 0 only).
 """
 from __future__ import annotations
@@ -257,6 +258,48 @@ def reference_forward_timer(workload, n, rp, ci, v, X, weights):
     return run, free
 
 
+def reference_layers_timer(workload, n, rp, ci, v, X, weights):
+    """A callable running the reference's layer objects (GCNLayer / SAGELayer)
+    + log_softmax once on an adjacency normalised beforehand: the layer
+    forwards of Model::forward without its per-call gcn_norm."""
+    import oracle
+    R = oracle.ref
+    if R is None:
+        return None, None
+    st = R.stack(ref_spec(workload), {k: t.cpu().numpy() for k, t in weights.items()})
+    rp_h = np.ascontiguousarray(rp.cpu().numpy(), dtype=np.int32)
+    ci_h = np.ascontiguousarray(ci.cpu().numpy(), dtype=np.int32)
+    v_h = np.ascontiguousarray(v.cpu().numpy(), dtype=np.float32)
+    X_h = np.ascontiguousarray(X.cpu().numpy(), dtype=np.float32)
+    lib = R.lib
+    A = lib.ref_tensor_csr(n, ci_h.size, rp_h.ctypes.data, ci_h.ctypes.data, v_h.ctypes.data)
+    Xt = lib.ref_tensor_dense(X_h.shape[0], X_h.shape[1], X_h.ctypes.data)
+    del rp_h, ci_h, v_h, X_h
+    An = st.gcn_norm_tensor(A) if workload == "gcn" else None
+
+    def run():
+        st.forward_tensors(An if An is not None else A, A, Xt, True)
+
+    def free():
+        for t in (A, Xt, An):
+            if t:
+                lib.ref_tensor_free(t)
+
+    return run, free
+
+
+def time_reference(run, budget_s: float):
+    """1 warm-up, then up to 5 timed calls within ``budget_s`` (at least 1):
+    (median seconds per call, calls)."""
+    run()
+    times, t0 = [], time.perf_counter()
+    while not times or (time.perf_counter() - t0 < budget_s and len(times) < 5):
+        t = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t)
+    return statistics.median(times), len(times)
+
+
 def nnz_normalized(rp, ci, n):
     """nnz of gcn_norm(A) = nnz(A) + rows without a diagonal entry."""
     rows = torch.repeat_interleave(torch.arange(n, device=rp.device), (rp[1:] - rp[:-1]).long())
@@ -467,16 +510,19 @@ def run_ours(args):
         run, free = reference_forward_timer(args.workload, n, rp, ci, v, Xfull, w)
         if run is not None:
             import oracle
-            run()  # warm-up
-            reps, t0 = 0, time.perf_counter()
-            while reps < 1 or (time.perf_counter() - t0 < args.cpu_seconds and reps < 5):
-                run()
-                reps += 1
-            dt = (time.perf_counter() - t0) / reps
+            dt, reps = time_reference(run, args.cpu_seconds)
             free()
             cpu = {"value": nnz_total / dt, "unit": "edges/s", "cores": oracle.ref.max_threads(),
                    "kind": "reference", "ms_per_forward": dt * 1e3,
-                   "sample": f"{reps} full Model::forward + log_softmax calls (after 1 warm-up) on the same graph"}
+                   "sample": f"median of {reps} full Model::forward + log_softmax calls (after 1 warm-up) on "
+                             "the same graph"}
+            run, free = reference_layers_timer(args.workload, n, rp, ci, v, Xfull, w)
+            dt, reps = time_reference(run, args.cpu_seconds)
+            free()
+            cpu["layers_only"] = {
+                "value": nnz_total / dt, "unit": "edges/s", "ms_per_forward": dt * 1e3,
+                "sample": f"median of {reps} calls of the reference's layer objects + log_softmax on an "
+                          "adjacency normalised once (Model::forward without its per-call gcn_norm)"}
 
     if rank == 0:
         value = nnz_total / (ms / args.steps * 1e-3)

@@ -219,6 +219,13 @@ class _Ref:
         L.ref_tensor_free.argtypes = [_vp]
         L.ref_model_forward_tensors.argtypes = [_vp, _vp, _vp, _vp, _i32]
         L.ref_spmm_tensors.argtypes = [_vp, _vp, _vp]
+        L.ref_stack_create.restype = _vp
+        L.ref_stack_free.argtypes = [_vp]
+        L.ref_stack_add_gcn.argtypes = [_vp, _i64, _i64, _i32, _i32, _vp, _vp]
+        L.ref_stack_add_sage.argtypes = [_vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp]
+        L.ref_gcn_norm_tensor.argtypes = [_vp]
+        L.ref_gcn_norm_tensor.restype = _vp
+        L.ref_stack_forward_tensors.argtypes = [_vp, _vp, _vp, _vp, _i32, _vp]
 
     def _chk(self, rc: int) -> None:
         if rc:
@@ -333,6 +340,10 @@ class _Ref:
         """A reference ``Model`` built from a layer spec and named weights."""
         return RefModel(self, spec, weights)
 
+    def stack(self, spec, weights):
+        """The same GCN / SAGE layers as reference layer objects (RefStack)."""
+        return RefStack(self, spec, weights)
+
 
 class RefModel:
     """The reference ``Model`` (src/model.cpp) driven through the shim.
@@ -383,6 +394,53 @@ class RefModel:
     def __del__(self):
         try:
             self.lib.ref_model_free(self.h)
+        except Exception:
+            pass
+
+
+class RefStack:
+    """The reference's GCNLayer / SAGELayer objects of a GCN or SAGE ``spec``
+    (as for :class:`RefModel`), run on pre-built Tensors: ``forward`` takes
+    the normalised adjacency (GCN) and the raw one (SAGE) prepared once --
+    the layer forwards of Model::forward without its per-call gcn_norm."""
+
+    def __init__(self, ref: _Ref, spec, weights):
+        self.ref, self.lib = ref, ref.lib
+        self.h = self.lib.ref_stack_create()
+        self._keep = []
+        for li, L in enumerate(spec):
+            act = 1 if L.get("act") == "relu" else 0
+            post = RefModel.POST[L.get("post")]
+            b = _f(weights[f"layer{li}.bias"]).reshape(-1) if L.get("bias", True) else None
+            self._keep.append(b)
+            if L["type"] == "gcn":
+                W = _f(weights[f"layer{li}.weight"])
+                self._keep.append(W)
+                rc = self.lib.ref_stack_add_gcn(self.h, L["in"], L["out"], act, post, _p(W), _p(b))
+            elif L["type"] == "sage":
+                Wn, Ws = _f(weights[f"layer{li}.weight_neigh"]), _f(weights[f"layer{li}.weight_self"])
+                self._keep += [Wn, Ws]
+                rc = self.lib.ref_stack_add_sage(self.h, L["in"], L["out"], int(L.get("agg", "mean") == "max"),
+                                                 act, post, _p(Wn), _p(Ws), _p(b))
+            else:
+                raise ValueError("RefStack: GCN and SAGE layers only")
+            ref._chk(rc)
+        self.out_cols = spec[-1]["out"]
+
+    def gcn_norm_tensor(self, A):
+        t = self.lib.ref_gcn_norm_tensor(A)
+        if not t:
+            raise OracleError(3, self.lib.ref_last_error().decode())
+        return t
+
+    def forward_tensors(self, A_norm, A_raw, X, log_softmax=True, rows=None):
+        out = None if rows is None else np.empty((rows, self.out_cols), np.float32)
+        self.ref._chk(self.lib.ref_stack_forward_tensors(self.h, A_norm, A_raw, X, int(log_softmax), _p(out)))
+        return out
+
+    def __del__(self):
+        try:
+            self.lib.ref_stack_free(self.h)
         except Exception:
             pass
 

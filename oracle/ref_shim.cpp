@@ -339,6 +339,80 @@ int ref_model_forward_tensors(void* m, const void* adj, const void* X, float* ou
     });
 }
 
+// ── The layers alone ──────────────────────────────────────────────────────
+// A stack of the reference's GCN / SAGE layer objects run on an adjacency
+// prepared once (gcn_norm for GCN layers, the raw one for SAGE): what
+// Model::forward does per layer, without its per-call normalisation
+// (src/model.cpp:365-381), for timing the layer forwards by themselves.
+struct RefStack {
+    std::vector<int> kind;     // 0 GCN, 1 SAGE
+    std::vector<int> post;     // 0 none, 1 ReLU, 2 ELU (alpha 1)
+    std::vector<R::GCNLayer> gcn;
+    std::vector<R::SAGELayer> sage;
+};
+
+void* ref_stack_create(void) { return new RefStack(); }
+void ref_stack_free(void* s) { delete static_cast<RefStack*>(s); }
+
+int ref_stack_add_gcn(void* s, int64_t in_f, int64_t out_f, int act, int post, const float* W,
+                      const float* b) {
+    return guarded([&] {
+        auto* st = static_cast<RefStack*>(s);
+        R::GCNLayer L(static_cast<std::size_t>(in_f), static_cast<std::size_t>(out_f), b != nullptr,
+                      act_of(act));
+        L.set_weight(dense(in_f, out_f, W));
+        if (b) L.set_bias(dense(1, out_f, b));
+        st->gcn.push_back(std::move(L));
+        st->kind.push_back(0);
+        st->post.push_back(post);
+    });
+}
+
+int ref_stack_add_sage(void* s, int64_t in_f, int64_t out_f, int agg_max, int act, int post,
+                       const float* Wn, const float* Ws, const float* b) {
+    return guarded([&] {
+        auto* st = static_cast<RefStack*>(s);
+        R::SAGELayer L(static_cast<std::size_t>(in_f), static_cast<std::size_t>(out_f),
+                       agg_max ? R::SAGELayer::Aggregator::Max : R::SAGELayer::Aggregator::Mean,
+                       b != nullptr, act_of(act));
+        L.set_weight_neigh(dense(in_f, out_f, Wn));
+        L.set_weight_self(dense(in_f, out_f, Ws));
+        if (b) L.set_bias(dense(1, out_f, b));
+        st->sage.push_back(std::move(L));
+        st->kind.push_back(1);
+        st->post.push_back(post);
+    });
+}
+
+// gcn_norm of a pre-built CSR Tensor, as a new Tensor (free with ref_tensor_free).
+void* ref_gcn_norm_tensor(const void* A) {
+    try {
+        return new R::Tensor(R::gcn_norm(*static_cast<const R::Tensor*>(A)));
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return nullptr;
+    }
+}
+
+int ref_stack_forward_tensors(void* s, const void* A_norm, const void* A_raw, const void* X,
+                              int log_softmax, float* out) {
+    return guarded([&] {
+        auto* st = static_cast<RefStack*>(s);
+        const R::Tensor* H = static_cast<const R::Tensor*>(X);
+        R::Tensor cur;
+        std::size_t ig = 0, is = 0;
+        for (std::size_t l = 0; l < st->kind.size(); ++l) {
+            cur = st->kind[l] == 0 ? st->gcn[ig++].forward(*static_cast<const R::Tensor*>(A_norm), *H)
+                                   : st->sage[is++].forward(*static_cast<const R::Tensor*>(A_raw), *H);
+            if (st->post[l] == 1) R::relu_inplace(cur);
+            if (st->post[l] == 2) R::elu_inplace(cur, 1.0f);
+            H = &cur;
+        }
+        if (log_softmax) R::log_softmax_inplace(cur);
+        if (out) out_dense(cur, out);
+    });
+}
+
 int ref_spmm_tensors(const void* A, const void* B, float* out) {
     return guarded([&] {
         R::Tensor y = R::spmm(*static_cast<const R::Tensor*>(A),

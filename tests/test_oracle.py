@@ -222,3 +222,38 @@ def test_port_edge_cases():
         P.edge_list_to_csr(np.array([0], np.int32), np.array([3], np.int32), 3)
     with pytest.raises(oracle.OracleError):
         P.activation("softmax", np.zeros((2, 0), np.float32))
+
+
+@pytest.mark.skipif(oracle.ref is None, reason="the reference library is not built")
+@pytest.mark.parametrize("kind", ["gcn", "sage"])
+def test_reference_layer_stack_equals_model_forward(kind):
+    """The reference's layer objects run on an adjacency normalised once (the
+    CPU baseline's layers-only figure) give Model::forward's logits bit for
+    bit."""
+    rng = np.random.default_rng(17)
+    n = 1500
+    rp, ci, v = powerlaw_csr(rng, n, 9, weighted=False, diag=False)
+    X = rng.standard_normal((n, 24)).astype(np.float32)
+    if kind == "gcn":
+        spec = [dict(type="gcn", **{"in": 24, "out": 16}, act="relu"), dict(type="gcn", **{"in": 16, "out": 5})]
+        w = {"layer0.weight": rng.standard_normal((24, 16)).astype(np.float32) * 0.3,
+             "layer0.bias": rng.standard_normal(16).astype(np.float32) * 0.1,
+             "layer1.weight": rng.standard_normal((16, 5)).astype(np.float32) * 0.3,
+             "layer1.bias": rng.standard_normal(5).astype(np.float32) * 0.1}
+    else:
+        spec = [dict(type="sage", **{"in": 24, "out": 16}, act="relu"), dict(type="sage", **{"in": 16, "out": 5})]
+        w = {f"layer{i}.{k}": rng.standard_normal(s).astype(np.float32) * 0.3
+             for i, (a, b) in enumerate([(24, 16), (16, 5)])
+             for k, s in (("weight_neigh", (a, b)), ("weight_self", (a, b)), ("bias", (b,)))}
+    R = oracle.ref
+    ref = R.activation("log_softmax", R.model(spec, w).forward(rp, ci, v, X))
+    st = R.stack(spec, w)
+    A = R.lib.ref_tensor_csr(n, ci.size, rp.ctypes.data, ci.ctypes.data, v.ctypes.data)
+    Xt = R.lib.ref_tensor_dense(n, 24, X.ctypes.data)
+    An = st.gcn_norm_tensor(A)
+    try:
+        got = st.forward_tensors(An, A, Xt, True, rows=n)
+    finally:
+        for t in (A, Xt, An):
+            R.lib.ref_tensor_free(t)
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
