@@ -74,6 +74,9 @@ def parse():
                     help="hub: time one long row through spmm (the heavy-row path) instead of the benchmark")
     ap.add_argument("--micro-entries", type=int, default=13_531)
     ap.add_argument("--micro-features", type=int, default=128)
+    ap.add_argument("--suite", action="store_true",
+                    help="one line per other benchmark configuration (Cora-shaped GCN, R-MAT spmm sweep, SAGE, "
+                         "GAT): GPU time beside the reference's CPU time; not the headline line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
@@ -586,8 +589,165 @@ def run_micro_hub(args):
     return 0
 
 
+# ── the other configurations (--suite) ──────────────────────────────────────
+def _gpu_ms(fn, reps: int = 20, warm: int = 3) -> float:
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def _ref_model_runner(spec, weights, n, rp, ci, v, X):
+    """The reference Model::forward + log_softmax on pre-built reference Tensors."""
+    import oracle
+    R = oracle.ref
+    m = R.model(spec, {k: np.asarray(t) for k, t in weights.items()})
+    rp_h = np.ascontiguousarray(rp.cpu().numpy(), dtype=np.int32)
+    ci_h = np.ascontiguousarray(ci.cpu().numpy(), dtype=np.int32)
+    v_h = np.ascontiguousarray(v.cpu().numpy(), dtype=np.float32)
+    X_h = np.ascontiguousarray(X.cpu().numpy(), dtype=np.float32)
+    A = R.lib.ref_tensor_csr(n, ci_h.size, rp_h.ctypes.data, ci_h.ctypes.data, v_h.ctypes.data)
+    Xt = R.lib.ref_tensor_dense(X_h.shape[0], X_h.shape[1], X_h.ctypes.data)
+
+    def run():
+        R._chk(R.lib.ref_model_forward_tensors(m.h, A, Xt, None, 1))
+
+    def free():
+        R.lib.ref_tensor_free(A)
+        R.lib.ref_tensor_free(Xt)
+
+    return run, free
+
+
+def run_suite(args):
+    """One JSON line per benchmark configuration other than the headline one:
+    the GPU time with inputs in HBM (CUDA events, warm; each call does what
+    Model::forward does -- gcn_norm or self-loops, the layers, log_softmax)
+    and the reference library's CPU time on the same inputs (median of up to
+    5 calls after a warm-up, all host threads).  Synthetic seeded inputs of
+    the configurations' shapes."""
+    import oracle
+    import tinygnn_b200 as tg
+    from tinygnn_b200 import synth
+    from tinygnn_b200.dist import Comm, Layer, ShardedModel
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    R = oracle.ref
+    peak, _ = measured_peaks()
+    h = lambda t: t.detach().cpu().numpy()  # noqa: E731
+
+    def emit(line, run=None, free=None):
+        if run is not None and R is not None:
+            dt, reps = time_reference(run, args.cpu_seconds)
+            free()
+            line["cpu_ms"] = dt * 1e3
+            line["cpu_cores"] = R.max_threads()
+            line["speedup"] = line["cpu_ms"] / line["gpu_ms"]
+        print(json.dumps(line), flush=True)
+
+    # 1. Cora-shaped GCN 1433 -> 16 -> 7
+    n, rp, ci, v, X = synth.cora_like(device=dev)
+    W0, W1 = synth.glorot(1433, 16, 2, 1, dev), synth.glorot(16, 7, 2, 2, dev)
+    b0, b1 = torch.zeros(16, device=dev), torch.zeros(7, device=dev)
+    A = tg.CSR(n, n, rp, ci, v)
+
+    def cora():
+        An = tg.gcn_norm(A)
+        tg.log_softmax_(tg.gcn_layer(An, tg.gcn_layer(An, X, W0, b0, "relu", mode="fast"), W1, b1, None,
+                                     mode="fast"))
+    ms = _gpu_ms(cora, reps=200, warm=10)
+    spec = [dict(type="gcn", **{"in": 1433, "out": 16}, act="relu"), dict(type="gcn", **{"in": 16, "out": 7})]
+    w = {"layer0.weight": h(W0), "layer0.bias": h(b0), "layer1.weight": h(W1), "layer1.bias": h(b1)}
+    emit({"suite": "gcn-cora-shape", "nodes": n, "nnz_norm": int(tg.gcn_norm(A).nnz), "gpu_ms": ms},
+         *(_ref_model_runner(spec, w, n, rp, ci, v, X) if R is not None else (None, None)))
+
+    # 2. spmm, R-MAT 2^20 / 2^24 draws, values U(0,1], F in {16, 64, 128, 256}
+    n, rp, ci, v = synth.rmat_csr(20, 1 << 24, 3, device=dev, values_seed=3)
+    A = tg.CSR(n, n, rp, ci, v).with_degree_order()
+    nnz = int(ci.numel())
+    for F in (16, 64, 128, 256):
+        B = synth.normal_rows(0, n, F, 4, 0, dev)
+        out = torch.empty((n, F), device=dev)
+        ms = _gpu_ms(lambda: tg.spmm(A, B, out=out))
+        alg = nnz * (8 + 4 * F) + n * (4 + 4 * F)
+        line = {"suite": "spmm-rmat-2^20", "F": F, "nnz": nnz, "gpu_ms": ms, "edges_per_s": nnz / (ms * 1e-3),
+                "alg_GBps": alg / (ms * 1e-3) / 1e9, "hbm_frac_of_measured": alg / (ms * 1e-3) / 1e9 / peak}
+        run = free = None
+        if R is not None:
+            At = R.lib.ref_tensor_csr(n, nnz, h(rp).ctypes.data, h(ci).ctypes.data, h(v).ctypes.data)
+            Bh = np.ascontiguousarray(h(B))
+            Bt = R.lib.ref_tensor_dense(n, F, Bh.ctypes.data)
+
+            def run(At=At, Bt=Bt):
+                R._chk(R.lib.ref_spmm_tensors(At, Bt, None))
+
+            def free(At=At, Bt=Bt):
+                R.lib.ref_tensor_free(At)
+                R.lib.ref_tensor_free(Bt)
+        emit(line, run, free)
+        del B, out
+
+    # 3. SAGE-mean 128 -> 128 -> 40 on a symmetrised R-MAT 2^18
+    n, rp, ci, v = synth.rmat_csr(18, 5_242_880, 5, device=dev, symmetric=True, no_self=True)
+    X = synth.normal_rows(0, n, 128, 6, 0, dev)
+    Wn1, Ws1 = synth.glorot(128, 128, 6, 1, dev), synth.glorot(128, 128, 6, 2, dev)
+    Wn2, Ws2 = synth.glorot(128, 40, 6, 3, dev), synth.glorot(128, 40, 6, 4, dev)
+    b1, b2 = torch.zeros(128, device=dev), torch.zeros(40, device=dev)
+    model = ShardedModel([Layer("sage", Wn1, b1, "relu", Ws1), Layer("sage", Wn2, b2, None, Ws2)], n,
+                         Comm(1, 0), dev, mode="fast")
+    A = tg.CSR(n, n, rp, ci, v).with_degree_order()
+    ms = _gpu_ms(lambda: model.forward(None, A, X))
+    spec = [dict(type="sage", **{"in": 128, "out": 128}, act="relu"), dict(type="sage", **{"in": 128, "out": 40})]
+    w = {"layer0.weight_neigh": h(Wn1), "layer0.weight_self": h(Ws1), "layer0.bias": h(b1),
+         "layer1.weight_neigh": h(Wn2), "layer1.weight_self": h(Ws2), "layer1.bias": h(b2)}
+    emit({"suite": "sage-rmat-2^18", "nodes": n, "nnz": int(ci.numel()), "gpu_ms": ms,
+          "edges_per_s": int(ci.numel()) / (ms * 1e-3)},
+         *(_ref_model_runner(spec, w, n, rp, ci, v, X) if R is not None else (None, None)))
+    del model
+
+    # 4. GAT 256 -> 8 heads x 8 (concat, ELU) -> 16 on an R-MAT 2^20 stored incoming, self-loops per call
+    n, rp, ci, v = synth.rmat_csr(20, 1 << 24, 7, device=dev, transpose=True)
+    X = synth.normal_rows(0, n, 256, 8, 0, dev)
+    heads, d = 8, 8
+    Wh = [synth.glorot(256, d, 8, 10 + k, dev) for k in range(heads)]
+    al = [synth.glorot(d, 1, 8, 30 + k, dev).flatten() for k in range(heads)]
+    ar = [synth.glorot(d, 1, 8, 50 + k, dev).flatten() for k in range(heads)]
+    W2 = synth.glorot(64, 16, 8, 70, dev)
+    al2, ar2 = synth.glorot(16, 1, 8, 71, dev).flatten(), synth.glorot(16, 1, 8, 72, dev).flatten()
+    W, AL, AR = torch.cat(Wh, 1), torch.stack(al), torch.stack(ar)
+    z1, z2 = torch.zeros((heads, d), device=dev), torch.zeros((1, 16), device=dev)
+    A = tg.CSR(n, n, rp, ci, v)
+
+    def gat():
+        Asl = tg.add_self_loops(A)
+        H = tg.gat_layer(Asl, X, W, AL, AR, heads, z1, 0.2, True, None, mode="fast")
+        tg.elu_(H)
+        tg.log_softmax_(tg.gat_layer(Asl, H, W2, al2.reshape(1, -1), ar2.reshape(1, -1), 1, z2, 0.2, True, None,
+                                     mode="fast"))
+    ms = _gpu_ms(gat, reps=10)
+    spec = [dict(type="gat", **{"in": 256, "out": d}, heads=heads, concat=True, post="elu"),
+            dict(type="gat", **{"in": 64, "out": 16}, heads=1)]
+    w = {}
+    for k in range(heads):
+        w[f"layer0.head{k}.weight"], w[f"layer0.head{k}.attn_left"] = h(Wh[k]), h(al[k])
+        w[f"layer0.head{k}.attn_right"], w[f"layer0.head{k}.bias"] = h(ar[k]), np.zeros(d, np.float32)
+    w.update({"layer1.head0.weight": h(W2), "layer1.head0.attn_left": h(al2), "layer1.head0.attn_right": h(ar2),
+              "layer1.head0.bias": np.zeros(16, np.float32)})
+    emit({"suite": "gat-rmat-2^20", "nodes": n, "nnz": int(ci.numel()), "gpu_ms": ms,
+          "edges_per_s": int(ci.numel()) / (ms * 1e-3)},
+         *(_ref_model_runner(spec, w, n, rp, ci, v, X) if R is not None else (None, None)))
+
+
 def main():
     args = parse()
+    if args.suite:
+        return run_suite(args)
     if args.micro == "hub":
         return run_micro_hub(args)
     if args.impl == "reference":
