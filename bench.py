@@ -680,9 +680,10 @@ def run_suite(args):
                 "alg_GBps": alg / (ms * 1e-3) / 1e9, "hbm_frac_of_measured": alg / (ms * 1e-3) / 1e9 / peak}
         run = free = None
         if R is not None:
-            At = R.lib.ref_tensor_csr(n, nnz, h(rp).ctypes.data, h(ci).ctypes.data, h(v).ctypes.data)
-            Bh = np.ascontiguousarray(h(B))
+            rp_h, ci_h, v_h, Bh = (np.ascontiguousarray(h(t)) for t in (rp, ci, v, B))  # alive across the calls
+            At = R.lib.ref_tensor_csr(n, nnz, rp_h.ctypes.data, ci_h.ctypes.data, v_h.ctypes.data)
             Bt = R.lib.ref_tensor_dense(n, F, Bh.ctypes.data)
+            del rp_h, ci_h, v_h, Bh  # the reference Tensors hold their own copies
 
             def run(At=At, Bt=Bt):
                 R._chk(R.lib.ref_spmm_tensors(At, Bt, None))
