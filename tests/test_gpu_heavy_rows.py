@@ -130,3 +130,36 @@ def test_gcn_layer_with_hub_rows_vs_oracle(tg):
                        torch.as_tensor(b).cuda(), "relu")
     assert_bits_equal(host(got), P.gcn_layer(*An, H, W, b, True), "gcn layer with hub rows")
     tg.ops.take_device_error()
+
+
+@pytest.mark.parametrize("heads,d,concat", [(8, 8, True), (1, 16, True), (4, 3, False), (2, 41, True)])
+def test_gat_hub_rows_vs_oracle(tg, heads, d, concat):
+    """GAT over hub rows: rows at and above the threshold are cut into
+    512-entry chunks whose online-softmax states merge in order (1022..9000
+    entries and one row over every column -- up to 40 chunks), the rest run
+    as whole rows; every head of every row within the fp32 tolerance of the
+    oracle's per-head GATLayer."""
+    from tests.helpers import assert_close
+    rng, rp, ci, v = hub_graph(7 + heads + d)
+    Asl_np = P.add_self_loops(rp, ci, v)
+    n = rp.size - 1
+    fi = 24
+    X = rng.standard_normal((n, fi)).astype(np.float32)
+    W = (rng.standard_normal((fi, heads * d)) * 0.3).astype(np.float32)
+    al = (rng.standard_normal((heads, d)) * 0.5).astype(np.float32)
+    ar = (rng.standard_normal((heads, d)) * 0.5).astype(np.float32)
+    b = (rng.standard_normal((heads, d)) * 0.1).astype(np.float32)
+    A = tg.CSR.from_numpy(*Asl_np)
+    dev = lambda a: torch.as_tensor(a).cuda()  # noqa: E731
+    got = host(tg.gat_layer(A, dev(X), dev(W), dev(al), dev(ar), heads, dev(b), 0.2, concat, None))
+    per_head = [P.gat_layer(*Asl_np, X, W[:, h * d:(h + 1) * d].copy(), al[h], ar[h], b[h], 0.2, False)
+                for h in range(heads)]
+    if concat:
+        ref = np.concatenate(per_head, axis=1)
+    else:
+        acc = np.zeros_like(per_head[0])
+        for t in per_head:
+            acc = (acc + t).astype(np.float32)
+        ref = (acc * np.float32(1.0 / heads)).astype(np.float32)
+    assert_close(got, ref, f"GAT hub rows h={heads} d={d} concat={concat}")
+    tg.ops.take_device_error()

@@ -22,7 +22,7 @@ void gemm(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const fl
 void gemm_dual_exact(int64_t M, int64_t N, int64_t K, const float* A1, int64_t lda1, const float* A2, int64_t lda2,
                      const float* B1, const float* B2, int64_t ldb, float* C, int64_t ldc, const float* bias, int act,
                      float alpha, cudaStream_t s);
-void gat_layer(int64_t N, const int32_t* rp, const int32_t* ci, const float* Hf, int64_t ldh, int64_t F_in, int H,
+void gat_layer(int64_t N, int64_t nnz, const int32_t* rp, const int32_t* ci, const float* Hf, int64_t ldh, int64_t F_in, int H,
                int d, const float* W_all, const float* al, const float* ar, const float* bias, float slope,
                bool concat, int act, int post, float* out, int64_t ldo, const int32_t* order, int mode,
                cudaStream_t s);
@@ -121,13 +121,13 @@ TG_API tg_status tg_gat_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
                                   const int32_t* row_order, int32_t mode, void* stream) {
     return guard([&] {
         require_device();
-        (void)nnz;
+        if (nnz < 0) invalid("GATLayer: negative nnz");
         if (F_in <= 0) invalid("GATLayer: in_features must be > 0.");
         if (F_out <= 0) invalid("GATLayer: out_features must be > 0.");
         if (heads <= 0) invalid("GATLayer: heads must be > 0.");
         check_ld("GATLayer::forward", "H", ldh, F_in);
         check_ld("GATLayer::forward", "out", ldo, concat ? heads * F_out : F_out);
-        gat_layer(N, row_ptr, col_ind, H, ldh, F_in, static_cast<int>(heads), static_cast<int>(F_out), W, a_left,
+        gat_layer(N, nnz, row_ptr, col_ind, H, ldh, F_in, static_cast<int>(heads), static_cast<int>(F_out), W, a_left,
                   a_right, bias, negative_slope, concat != 0, act, TG_ACT_NONE, out, ldo, row_order, mode,
                   as_stream(stream));
     });
