@@ -233,3 +233,9 @@ def test_dlpack_host_import_copies():
                                                          ("col_ind", None), ("values", None)]
     for name in ("__dlpack__", "__dlpack_device__", "row_ptr_dlpack", "col_ind_dlpack", "values_dlpack"):
         assert callable(getattr(tg.Tensor, name))
+    # CSR arrays are wrapped in place only: host arrays and other index types are refused
+    rp, ci, v = np.array([0, 1], np.int32), np.array([0], np.int32), np.array([1.0], np.float32)
+    with pytest.raises(ValueError, match="row_ptr must be on the current CUDA device"):
+        tg.Tensor.sparse_csr_from_dlpack(1, 1, rp, ci, v)
+    with pytest.raises(ValueError, match="row_ptr must be int32"):
+        tg.Tensor.sparse_csr_from_dlpack(1, 1, rp.astype(np.int64), ci, v)
