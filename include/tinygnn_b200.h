@@ -286,7 +286,9 @@ TG_API tg_status tg_gcn_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
  * library (TG_NOALLOC_SCRATCH_BYTES per GPU, held until the process exits),
  * so it allocates nothing: N * round_up(F_out, 4) * 4 bytes must fit, larger
  * layers return TG_ERR_INVALID_ARGUMENT.  Rows run in the caller's
- * row_order, or in natural order when it is NULL (no schedule is computed).
+ * row_order, or in natural order when it is NULL (no schedule is computed);
+ * every row, hub rows included, runs in the sub-warp gather kernel (the
+ * hub-row kernel's counter and side stream would allocate).
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress); make that first call before any stream capture.
  * All calls share the one array: calls whose work overlaps on the GPU (other

@@ -27,12 +27,20 @@ REF_SO = os.path.join(_HERE, "_ref", "libtinygnn_ref.so")
 _i64, _i32, _f32, _vp = C.c_int64, C.c_int, C.c_float, C.c_void_p
 
 
-def build(quiet: bool = True) -> None:
-    """Build the oracle libraries (the reference one only where its sources exist)."""
+def build(quiet: bool = True, target: str = "all") -> None:
+    """Build the oracle libraries (the reference one only where its sources
+    exist), serialised across processes by a lock file."""
+    import fcntl
     import subprocess
 
-    subprocess.run(["make", "-C", _HERE, "-j8", "all"], check=True,
-                   stdout=subprocess.DEVNULL if quiet else None)
+    os.makedirs(os.path.join(_HERE, "_build"), exist_ok=True)
+    with open(os.path.join(_HERE, "_build", ".build.lock"), "w") as lk:
+        fcntl.flock(lk, fcntl.LOCK_EX)
+        try:
+            subprocess.run(["make", "-C", _HERE, "-j8", target], check=True,
+                           stdout=subprocess.DEVNULL if quiet else None)
+        finally:
+            fcntl.flock(lk, fcntl.LOCK_UN)
 
 
 def _p(a: Optional[np.ndarray]):
@@ -81,6 +89,10 @@ class _Port:
         L.orc_gcn_layer.argtypes = [_i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _vp]
         L.orc_sage_layer.argtypes = [_i64, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp]
         L.orc_gat_layer.argtypes = [_i64, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _f32, _i32, _vp]
+        L.orc_max_threads.restype = _i32
+
+    def max_threads(self) -> int:
+        return self.lib.orc_max_threads()
 
     def matmul(self, A, B):
         A, B = _f(A), _f(B)
@@ -497,5 +509,7 @@ def _load(cls, path):
     return cls(path) if os.path.exists(path) else None
 
 
+if not os.path.exists(PORT_SO):  # a fresh checkout: the C restatement builds anywhere gcc is
+    build(target="oracle")
 port = _load(_Port, PORT_SO)
 ref = _load(_Ref, REF_SO)

@@ -27,6 +27,19 @@
 
 #define EXPORT __attribute__((visibility("default")))
 
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* Host threads the parallel loops below use (OpenMP's default team size). */
+EXPORT int orc_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
 /* ── matmul: src/ops.cpp:70-162 ───────────────────────────────────────────
  * (i, k, j) loop order; C starts at zero; every C[i][j] is one fused
  * multiply-add chain over k in increasing order (ops.cpp:121-159). */

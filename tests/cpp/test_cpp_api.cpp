@@ -51,7 +51,9 @@ static Tensor undirected(std::size_t n, std::vector<std::pair<int, int>> pairs) 
     return GraphLoader::edge_list_to_csr(e, n);
 }
 
-int main() {
+int main(int argc, char** argv) {
+    // scratch files go to the directory the caller gives (a per-test temp dir)
+    const std::string tmpdir = argc > 1 ? argv[1] : ".";
     // spmm 3x3 (test_spmm.cpp:198)
     {
         auto A = Tensor::sparse_csr(3, 3, {0, 2, 3, 5}, {0, 1, 1, 0, 2}, {1, 1, 1, 1, 1});
@@ -177,7 +179,8 @@ int main() {
     }
     // Model: weights from a TGNN file, multi-head GAT (concat + ELU) then GCN
     {
-        const char* path = "/tmp/tinygnn_b200_cpp_api_weights.bin";
+        const std::string path_s = tmpdir + "/tinygnn_b200_cpp_api_weights.bin";
+        const char* path = path_s.c_str();
         std::vector<std::pair<std::string, std::vector<float>>> ts;
         std::vector<std::pair<uint32_t, uint32_t>> shapes;
         auto add = [&](const std::string& n, uint32_t r, uint32_t c, float seed) {

@@ -50,11 +50,15 @@ def test_library_is_built_for_sm100a_only():
 
 
 def test_no_cpu_fallback_when_library_missing(tmp_path, monkeypatch):
-    """Importing the package without the built library fails loudly."""
+    """Importing the package without the built library, where nvcc is not
+    there to build it, fails loudly."""
     import importlib
+    import shutil
     import sys
-    from tinygnn_b200 import _lib
-    monkeypatch.setattr(os.path, "exists", lambda p, _e=os.path.exists: False if p == _lib.LIB_PATH else _e(p))
+    from tinygnn_b200 import _lib, build
+    hidden = {_lib.LIB_PATH, build.NVCC}
+    monkeypatch.setattr(os.path, "exists", lambda p, _e=os.path.exists: False if p in hidden else _e(p))
+    monkeypatch.setattr(shutil, "which", lambda *a, **k: None)
     saved = {k: sys.modules.pop(k) for k in list(sys.modules) if k.startswith("tinygnn_b200")}
     try:
         with pytest.raises(ImportError):

@@ -30,6 +30,6 @@ def test_cpp_api_known_answers_on_device():
     with tempfile.TemporaryDirectory() as d:
         exe = os.path.join(d, "t")
         _build(exe)
-        r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+        r = subprocess.run([exe, d], capture_output=True, text=True, timeout=300)
         assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
         assert "0 failed" in r.stdout

@@ -1,21 +1,18 @@
 """ctypes binding of the C ABI declared in include/tinygnn_b200.h.
 
 The shared library lives in-tree at tinygnn_b200/lib/libtinygnn_b200.so and
-is built by ``tinygnn_b200.build.build()`` (nvcc, sm_100a).  Importing this
-module without it raises immediately: the package has no CPU path.
+is built by ``python tinygnn_b200/build.py`` (nvcc, sm_100a).  When it is
+missing, importing this module builds it (``build.ensure_built``); where it
+is missing and cannot be built (no nvcc), the import raises: the package
+has no CPU path.
 """
 from __future__ import annotations
 
 import ctypes as C
-import os
 
-_HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "lib", "libtinygnn_b200.so")
+from . import build as _build
 
-if not os.path.exists(LIB_PATH):
-    raise ImportError(
-        f"tinygnn_b200: {LIB_PATH} is missing; build it with "
-        "`python -c 'import tinygnn_b200.build as b; b.build()'` (there is no CPU fallback)")
+LIB_PATH = _build.ensure_built()
 
 lib = C.CDLL(LIB_PATH)
 

@@ -42,6 +42,10 @@ struct GatherArgs {
     // Without `order`, large launches compute a longest-rows-first schedule
     // in pool memory; false keeps the natural row order and allocates nothing.
     bool allow_auto_order = true;
+    // Rows of the schedule long enough for the heavy-row kernel go there
+    // (it needs a pool-allocated counter and a side stream); false keeps
+    // every row in the sub-warp kernel -- the same arithmetic, bit for bit.
+    bool allow_heavy = true;
     // Column-block pass: only entries [seg_lo[i], seg_hi[i]) of row i; the
     // accumulator starts from C (carry) and the epilogue (1/deg with the full
     // row length, self, bias, activation) runs only on the last pass, so the

@@ -73,13 +73,15 @@ TG_API tg_status tg_gcn_layer_noalloc_f32(int64_t N, int64_t nnz, const int32_t*
         if (N < 0) invalid("GCNLayer::forward: negative node count");
         check_ld("GCNLayer::forward", "H", ldh, F_in);
         check_ld("GCNLayer::forward", "out", ldo, F_out);
-        const int64_t ldw = (F_out + 3) / 4 * 4;
-        const int64_t need = N * ldw * static_cast<int64_t>(sizeof(float));
-        if (need > static_cast<int64_t>(TG_NOALLOC_SCRATCH_BYTES))
+        // Limits are checked by division first, so that no product below can
+        // overflow: F_out and N are each bounded by the array's size.
+        constexpr int64_t cap_floats = static_cast<int64_t>(TG_NOALLOC_SCRATCH_BYTES / sizeof(float));
+        const int64_t ldw = F_out <= cap_floats ? (F_out + 3) / 4 * 4 : cap_floats + 1;
+        if (ldw > cap_floats || N > cap_floats / ldw)
             invalid("gcn_layer (no-alloc): N x F_out = " + std::to_string(N) + " x " + std::to_string(F_out) +
-                    " needs " + std::to_string(need) + " bytes of scratch; the fixed scratch holds " +
-                    std::to_string(static_cast<long long>(TG_NOALLOC_SCRATCH_BYTES)) +
-                    " (use tg_gcn_layer_f32, which allocates)");
+                    " needs more than the " + std::to_string(static_cast<long long>(TG_NOALLOC_SCRATCH_BYTES)) +
+                    " bytes the fixed scratch holds (N * round_up(F_out, 4) * 4 bytes; use tg_gcn_layer_f32, "
+                    "which allocates)");
         if (N == 0) return;
         const cudaStream_t s = as_stream(stream);
         float* HW = scratch_address();
@@ -91,6 +93,7 @@ TG_API tg_status tg_gcn_layer_noalloc_f32(int64_t N, int64_t nnz, const int32_t*
         a.B = HW; a.ldb = ldw; a.b_padded = true; a.F = F_out;
         a.C = out; a.ldc = ldo; a.bias = bias; a.act = act; a.op = GATHER_SUM;
         a.allow_auto_order = false;  // a schedule would need pool memory
+        a.allow_heavy = false;       // so would the hub-row kernel's counter and side stream
         gather_rows(a, s);
     });
 }

@@ -163,7 +163,7 @@ void gather_rows(const GatherArgs& args, cudaStream_t s) {
     // Long rows go to the heavy-row kernel on the side stream, launched
     // first so its CTAs are placed before the sub-warp kernel's.
     const int32_t minlen = heavy_min_len();
-    const bool heavy = a.order && minlen >= -1 && a.ldb % 4 == 0 && aligned(a.B, 16);
+    const bool heavy = a.allow_heavy && a.order && minlen >= -1 && a.ldb % 4 == 0 && aligned(a.B, 16);
     SideStream* side = nullptr;
     std::unique_ptr<Scratch<int32_t>> count;
     if (heavy) {

@@ -18,9 +18,14 @@ import::
 Every op runs on the current CUDA device (sm_100a kernels); tensors stay in
 device memory between calls and are copied to the host only by
 ``to_numpy`` / ``*_numpy`` / ``at``.  Importing this package loads
-libtinygnn_b200.so; a missing build is an ImportError, never a CPU path.
+libtinygnn_b200.so and the module over it, building both when they are
+missing; where they cannot be built the import raises, never a CPU path.
 """
 from __future__ import annotations
+
+from .. import build as _build
+
+_build.ensure_built(pymodule=True)
 
 try:
     from ._core import (
