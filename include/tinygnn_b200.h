@@ -174,8 +174,9 @@ TG_API tg_status tg_sage_mean_combine_segment_f32(int64_t M, int64_t K, const in
                                                   int32_t carry, int32_t last, int32_t mode,
                                                   void* stream);
 
-/* Rows sorted by decreasing stored length (ties by row id) into
- * order_out[M]: a schedule that starts the longest rows first. */
+/* A schedule that starts the longest rows first, into order_out[M]: rows
+ * in classes of decreasing stored length -- four classes per power of two
+ * of (length + 1) -- and by row id within a class (a stable bucket sort). */
 TG_API tg_status tg_csr_degree_order(int64_t M, const int32_t* row_ptr, int32_t* order_out,
                                      void* stream);
 

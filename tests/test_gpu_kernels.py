@@ -247,8 +247,13 @@ def test_degree_order_is_a_descending_bucket_permutation(tg):
     order = host(tg.degree_order(csr(tg, rp, ci, v)))
     assert np.array_equal(np.sort(order), np.arange(20000))
     lens = (rp[1:] - rp[:-1])[order]
-    buckets = np.floor(np.log2(lens + 1))
+    # length classes: x = len + 1 in [2^k, 2^(k+1)), split in quarters
+    x = (lens + 1).astype(np.int64)
+    k = np.floor(np.log2(x)).astype(np.int64)
+    quarter = ((x - (1 << k)) * 4) >> k
+    buckets = 4 * k + quarter
     assert np.all(np.diff(buckets) <= 0)
+    assert len(np.unique(buckets)) > len(np.unique(k))  # finer than powers of two
     for b in np.unique(buckets):  # stable: rows ascending inside a bucket
         assert np.all(np.diff(order[buckets == b]) > 0)
 

@@ -36,8 +36,9 @@ template <int VEC, int LPR, int SPL, bool CVEC>
 void launch_gather(const GatherArgs& a, cudaStream_t s) {
     constexpr int RPB = (256 / 32) * (32 / LPR);  // rows per block
     // Gathered rows in flight per batch (sweep on the Reddit-shaped graph,
-    // degree-ordered: 4 for 32-lane rows, 8 for narrower ones).
-    constexpr int U = (SPL >= 4) ? 2 : (SPL == 2 ? 4 : (LPR == 32 ? 4 : 8));
+    // degree-ordered: 4 for 32-lane rows, 8 for narrower ones); with 2-3
+    // vectors per lane 4 (a divisor of the 4- and 8-entry windows).
+    constexpr int U = (SPL >= 4) ? 2 : (SPL >= 2 ? 4 : (LPR == 32 ? 4 : 8));
     const int64_t per_pass = static_cast<int64_t>(LPR) * SPL * VEC;
     const int64_t passes = ceil_div(a.F, per_pass);
     dim3 grid(static_cast<unsigned>(ceil_div(a.M, RPB)), static_cast<unsigned>(passes));
@@ -49,11 +50,19 @@ void launch_gather(const GatherArgs& a, cudaStream_t s) {
                s, a);
 }
 
+// Lanes per row (LPR) x vectors per lane (SPL) for a row of S vector slots:
+// the shape whose LPR * SPL slots leave the fewest lanes idle.  A 41-float
+// row (11 float4 slots, the GCN output layer) takes 4 lanes x 3 vectors --
+// 11 of 12 slots busy, 8 rows per warp -- where 16 lanes x 1 left 5 of 16
+// idle; it also needs a quarter of the index shuffles per gathered row.
 template <int VEC, bool CVEC>
 void dispatch_lpr(const GatherArgs& a, cudaStream_t s) {
     const int64_t S = ceil_div(a.F, VEC);  // vector slots per row
-    if (S <= 8) launch_gather<VEC, 8, 1, CVEC>(a, s);
+    if (S <= 4) launch_gather<VEC, 4, 1, CVEC>(a, s);
+    else if (S <= 8) launch_gather<VEC, 8, 1, CVEC>(a, s);
+    else if (S <= 12) launch_gather<VEC, 4, 3, CVEC>(a, s);
     else if (S <= 16) launch_gather<VEC, 16, 1, CVEC>(a, s);
+    else if (S <= 24) launch_gather<VEC, 8, 3, CVEC>(a, s);
     else if (S <= 32) launch_gather<VEC, 32, 1, CVEC>(a, s);
     else if (S <= 64) launch_gather<VEC, 32, 2, CVEC>(a, s);
     else launch_gather<VEC, 32, 4, CVEC>(a, s);  // feature passes of 128 vectors beyond
@@ -120,13 +129,13 @@ void launch_heavy(const GatherArgs& a, cudaStream_t s) {
 void dispatch_light(const GatherArgs& a, cudaStream_t s) {
     // Load width: the widest vector dividing B's leading dimension with B
     // aligned, and dividing F unless B's rows are padded; narrower when it
-    // would leave fewer than 8 vectors per row.
+    // would leave fewer than 4 vectors per row (the narrowest sub-warp).
     auto ok = [&](int v) {
         if (a.F % v && !a.b_padded) return false;
         return a.ldb % v == 0 && aligned(a.B, 4 * v);
     };
     int vec = 4;
-    while (vec > 1 && (!ok(vec) || ceil_div(a.F, vec) < 8)) vec /= 2;
+    while (vec > 1 && (!ok(vec) || ceil_div(a.F, vec) < 4)) vec /= 2;
     if (vec == 4) dispatch_cvec<4>(a, s);
     else if (vec == 2) dispatch_cvec<2>(a, s);
     else dispatch_cvec<1>(a, s);
@@ -182,17 +191,23 @@ void gather_rows(const GatherArgs& args, cudaStream_t s) {
 }
 
 // ── Degree order: a stable bucket sort of rows by decreasing length ─────────
-// Bucket b(i) = clz(len_i + 1) (longest rows in the lowest bucket).  Three
-// passes: per-block bucket counts, one exclusive scan over (bucket, block),
-// then a stable scatter (ranks from warp match/popc and per-warp prefix
-// counts in shared memory).
+// Length classes, longest first: four per power of two -- x = len + 1 falls
+// in [2^k, 2^(k+1)), and the two bits below its leading one split that range
+// into quarters.  Rows that share a warp (up to 8 in the narrow gathers) then
+// differ in length by at most ~25 % within a class.  Every class boundary
+// 2^k - 1 stays a boundary, so the rows of at least 2^k - 1 entries lead the
+// schedule (the hub-row prefix relies on it).  Three passes: per-block class
+// counts, one exclusive scan over (class, block), then a stable scatter
+// (ranks from warp match/popc and per-warp prefix counts in shared memory).
 namespace {
 constexpr int ORDER_BLOCK = 1024;
-constexpr int NBUCKET = 32;
+constexpr int NBUCKET = 128;
 
 __device__ __forceinline__ int row_bucket(const int32_t* rp, int64_t i) {
-    const int32_t len = __ldg(rp + i + 1) - __ldg(rp + i);
-    return __clz(len + 1);  // len+1 >= 1: 0 for the longest, 31 for empty rows
+    const uint32_t x = static_cast<uint32_t>(__ldg(rp + i + 1) - __ldg(rp + i)) + 1u;  // >= 1
+    const int lz = __clz(x);                     // 0 for the longest rows, 31 for empty ones
+    const uint32_t q = (x << lz) >> 29 & 3u;     // the two bits below the leading one
+    return lz * 4 + 3 - static_cast<int>(q);     // 0 .. 127
 }
 
 __global__ void order_count_kernel(int64_t M, const int32_t* rp, int32_t* counts /*[NBUCKET][nblocks]*/) {
