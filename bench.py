@@ -454,7 +454,7 @@ def run_ours(args):
 
     import tinygnn_b200 as tg
     from tinygnn_b200 import synth
-    from tinygnn_b200.dist import Comm, ShardedModel, gcn_norm_rows, row_block, slice_rows
+    from tinygnn_b200.dist import Comm, ShardedModel, gcn_norm_rows, gcn_norm_rows_scheduled, row_block, slice_rows
     from tinygnn_b200.ops import CSR
 
     comm = Comm(world, rank, group)
@@ -507,8 +507,7 @@ def run_ours(args):
         # layers and log_softmax run.  Nothing derived from the graph is kept
         # between steps.
         if args.workload == "gcn":
-            An = gcn_norm_rows(A_raw, r0, R, comm, dis_buf)
-            An.with_degree_order()
+            An = gcn_norm_rows_scheduled(A_raw, r0, R, comm, dis_buf)  # keeps the raw rows' schedule
             model.forward(An, None, X)
         else:
             Ar = CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind, A_raw.values)

@@ -262,6 +262,33 @@ TG_API tg_status tg_csr_scale_sym_f32(int64_t rows, const int32_t* row_ptr, cons
                                       float* values, const float* dis_row, const float* dis_col,
                                       void* stream);
 
+/* The same row-block gcn_norm in two passes over the raw rows instead of
+ * five (src/layers.cpp:71-208 for these rows):
+ *   tg_gcn_norm_rows_degrees_f32  -> row_ptr_out[rows+1] of the self-looped
+ *       block, insert_out[rows] (where each row's diagonal is inserted, -1
+ *       when the row holds one) and dis_out[rows] = 1/sqrtf(degree of the
+ *       self-looped row, summed in stored order);
+ *   (all-gather dis over the blocks into dis_all)
+ *   tg_gcn_norm_rows_fill_f32     -> col_ind_out / values_out: the self-looped
+ *       rows with values (v * dis_row[i]) * dis_col[j].
+ * Bit-identical to the three-call form.  col_ind_out / values_out need
+ * row_ptr_out[rows] entries (at most nnz + rows); both calls are
+ * asynchronous (read row_ptr_out[rows] for the count).  row_order
+ * (nullable; e.g. tg_csr_degree_order of the raw rows) schedules the rows,
+ * longest first, so that a hub row does not end the launch alone; it
+ * changes speed only. */
+TG_API tg_status tg_gcn_norm_rows_degrees_f32(int64_t rows, int64_t row_offset, int64_t nnz,
+                                              const int32_t* row_ptr, const int32_t* col_ind,
+                                              const float* values, const int32_t* row_order,
+                                              int32_t* row_ptr_out, int32_t* insert_out,
+                                              float* dis_out, void* stream);
+TG_API tg_status tg_gcn_norm_rows_fill_f32(int64_t rows, int64_t row_offset, const int32_t* row_ptr,
+                                           const int32_t* col_ind, const float* values,
+                                           const int32_t* row_order, const int32_t* row_ptr_out,
+                                           const int32_t* insert, const float* dis_row,
+                                           const float* dis_col, int32_t* col_ind_out,
+                                           float* values_out, void* stream);
+
 /* Tensor::sparse_csr validation (src/tensor.cpp:46-86) on device arrays:
  * row_ptr[rows] == nnz, row_ptr non-decreasing, 0 <= col_ind < cols.
  * Synchronises `stream`; errors carry the reference's message. */

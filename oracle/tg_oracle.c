@@ -192,11 +192,15 @@ EXPORT int64_t orc_gcn_norm(int64_t N, const int32_t* rp, const int32_t* ci,
                             float* v_out) {
     const int64_t nnz = orc_add_self_loops(N, rp, ci, v, rp_out, ci_out, v_out);
     float* dis = (float*)malloc((size_t)(N > 0 ? N : 1) * sizeof(float));
+    /* rows are independent: parallel over rows as the reference's
+     * OpenMP loops are (layers.cpp:170, 190), each row's sum sequential */
+#pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < N; ++i) {
         float d = 0.0f;
         for (int32_t nz = rp_out[i]; nz < rp_out[i + 1]; ++nz) d += v_out[nz];
         dis[i] = d > 0.0f ? 1.0f / sqrtf(d) : 0.0f;
     }
+#pragma omp parallel for schedule(dynamic, 64)
     for (int64_t i = 0; i < N; ++i) {
         const float di = dis[i];
         for (int32_t nz = rp_out[i]; nz < rp_out[i + 1]; ++nz)

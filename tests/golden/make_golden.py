@@ -221,6 +221,27 @@ def ref_cases():
     m = R.model(spec, w)
     y = R.activation("log_softmax", m.forward(rp, ci, v, X))
     put("model_gat", rp=rp, ci=ci, v=v, X=X, out=y, **{k.replace(".", "_"): a for k, a in w.items()})
+    # Rows in stored (unsorted) column order, some holding their diagonal
+    # twice, values integer or fractional: add_self_loops inserts before the
+    # first column > i in stored order and adds 1 to every diagonal entry.
+    rng2 = np.random.default_rng(20261202)
+    n = 300
+    lens = rng2.integers(0, 14, n)
+    rp = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    ci = rng2.integers(0, n, rp[-1]).astype(np.int32)
+    for i in rng2.choice(n, n // 3, replace=False):
+        a, b = rp[i], rp[i + 1]
+        if b > a:
+            ci[rng2.integers(a, b)] = i
+            if b - a > 3:
+                ci[rng2.integers(a, b)] = i
+    for tag, v in (("unsorted_int", rng2.integers(1, 4, ci.size)),
+                   ("unsorted_frac", rng2.random(ci.size) + 0.1)):
+        v = v.astype(np.float32)
+        a = R.add_self_loops(rp, ci, v)
+        g = R.gcn_norm(rp, ci, v)
+        put(f"asl_{tag}", rp=rp, ci=ci, v=v, out_rp=a[0], out_ci=a[1], out_v=a[2])
+        put(f"gcnnorm_{tag}", rp=rp, ci=ci, v=v, out_rp=g[0], out_ci=g[1], out_v=g[2])
     return out
 
 

@@ -67,6 +67,35 @@ def test_row_block_gcn_norm_matches_global(tg, world):
         assert_bits_equal(asl.values.cpu().numpy(), G[2][a:b], "values")
 
 
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_two_pass_row_block_gcn_norm_matches_global(tg, world):
+    """tg_gcn_norm_rows_degrees_f32 / _fill_f32 per row block, with an
+    emulated all-gather of 1/sqrt(deg) between them, equal the rows of the
+    global gcn_norm bit for bit (weighted rows too: the sequential degree)."""
+    from tinygnn_b200.dist import row_block, slice_rows
+    rng, rp, ci, v, X = _graph()
+    n = rp.size - 1
+    for weighted, ordered in ((False, False), (True, False), (False, True), (True, True)):
+        vv = (rng.random(ci.size) + 0.25).astype(np.float32) if weighted else v
+        A = tg.CSR.from_numpy(rp, ci, vv)
+        G = P.gcn_norm(rp, ci, vv)
+        R = (n + world - 1) // world
+        dis_all = torch.zeros(R * world, device="cuda")
+        firsts = []
+        for r in range(world):
+            _, r0, r1 = row_block(n, world, r)
+            Ar = slice_rows(A.row_ptr, A.col_ind, A.values, r0, r1, n)
+            if ordered:  # the longest-first schedule only orders the work
+                Ar.order = tg.degree_order(Ar)
+            firsts.append((r0, r1, Ar) + tg.ops.gcn_norm_rows_degrees(Ar, r0, dis_all[r * R:r * R + (r1 - r0)]))
+        for r, (r0, r1, Ar, rpo, ins) in enumerate(firsts):
+            B = tg.ops.gcn_norm_rows_fill(Ar, r0, rpo, ins, dis_all[r * R:r * R + (r1 - r0)], dis_all)
+            a, b = G[0][r0], G[0][r1]
+            assert_bits_equal(B.row_ptr.cpu().numpy(), (G[0][r0:r1 + 1] - a).astype(np.int32), "row_ptr")
+            assert_bits_equal(B.col_ind.cpu().numpy(), G[1][a:b], "col_ind")
+            assert_bits_equal(B.values.cpu().numpy(), G[2][a:b], f"values weighted={weighted} ordered={ordered}")
+
+
 @pytest.mark.parametrize("workload,bpr", [("gcn", 2), ("gcn", 3), ("sage", 4)])
 def test_single_gpu_column_passes_are_bit_identical(tg, workload, bpr):
     from tinygnn_b200.dist import Comm, Layer, ShardedModel, gcn_norm_rows

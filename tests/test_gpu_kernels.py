@@ -317,11 +317,38 @@ def test_edge_list_to_csr_errors(tg):
     assert host(r.row_ptr).tolist() == [0]
 
 
-@pytest.mark.parametrize("kind", ["plain", "with_diag", "weighted_empty_rows", "powerlaw"])
+def _unsorted_dup_diag(rng, n=3000, deg=20):
+    """Rows in random column order, some holding their diagonal twice, with
+    integer and fractional values mixed per row."""
+    lens = rng.integers(0, 2 * deg, n)
+    rp = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    ci = rng.integers(0, n, rp[-1]).astype(np.int32)
+    for i in rng.choice(n, n // 4, replace=False):  # one or two diagonal entries
+        a, b = rp[i], rp[i + 1]
+        if b > a:
+            ci[rng.integers(a, b)] = i
+            if b - a > 3 and rng.random() < 0.5:
+                ci[rng.integers(a, b)] = i
+    v = np.where(rng.random(ci.size) < 0.5, rng.integers(1, 4, ci.size), rng.random(ci.size) + 0.1)
+    return rp, ci, v.astype(np.float32)
+
+
+@pytest.mark.parametrize("kind", ["plain", "with_diag", "weighted_empty_rows", "powerlaw", "integral_weights",
+                                  "large_integral", "unsorted_dup_diag", "negative_integral"])
 def test_self_loops_and_gcn_norm_vs_oracle(tg, kind):
+    """Both degree paths: rows of integer values within the exactness bound
+    (summed as a tree) and every other row (the sequential chain)."""
     rng = np.random.default_rng(len(kind))
     if kind == "powerlaw":
         rp, ci, v = powerlaw_csr(rng, 20000, 30, weighted=False, diag=False)
+    elif kind in ("integral_weights", "large_integral", "negative_integral"):
+        rp, ci, v = powerlaw_csr(rng, 20000, 30, weighted=False, diag=True)
+        hi = {"integral_weights": 5, "large_integral": 1 << 20, "negative_integral": 3}[kind]
+        v = rng.integers(1, hi, ci.size).astype(np.float32)
+        if kind == "negative_integral":
+            v *= np.where(rng.random(ci.size) < 0.3, -1, 1).astype(np.float32)
+    elif kind == "unsorted_dup_diag":
+        rp, ci, v = _unsorted_dup_diag(rng)
     else:
         rp, ci, v = rand_csr(rng, 8000, 8000, 12, weighted=kind.startswith("weighted"),
                              diag=kind == "with_diag" or kind.startswith("weighted"),

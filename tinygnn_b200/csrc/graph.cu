@@ -221,69 +221,175 @@ __global__ void row_expand_kernel(int64_t N, const int32_t* hist_scan, int32_t* 
 }
 
 // ── add_self_loops / gcn_norm ───────────────────────────────────────────────
-// Pass 1: new row lengths (len + 1 when the row has no diagonal) into out_rp[i+1].
-// The diagonal of local row i is column i + off (a block of rows of a square matrix).
-__global__ void self_loop_count_kernel(int64_t N, int64_t off, const int32_t* rp, const int32_t* ci, int32_t* out_rp) {
-    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    if (row >= N) return;
+// Two row passes (one warp per row) over a block of rows of a square matrix
+// whose local row i is global row i + off (the whole matrix: off = 0).
+//
+// Pass 1 (self_loop_rows_kernel): whether the row holds its diagonal, where
+// add_self_loops inserts it otherwise -- before the first column > i in
+// stored order, else at the end (src/layers.cpp:104-133) -- as insert[i]
+// (-1: the row has one), the new length into out_rp[i+1], and for gcn_norm
+// 1/sqrt(deg) of the self-looped row (src/layers.cpp:168-187).
+//
+// The degree is the reference's sequential float sum of the row's values in
+// stored order, with every diagonal entry as v + 1 and an inserted one as 1.
+// When every value is an integer and len * (max|v| + 1) + 1 < 2^24, every
+// partial sum of any subset is an integer below 2^24 -- exact in fp32 -- so
+// any summation order gives the sequential result bit for bit, and the warp
+// adds its lanes' partial sums as a tree (always the case for unweighted
+// graphs).  Otherwise the row is summed again as one sequential chain.
+//
+// Pass 2 (self_loop_fill_kernel): the self-looped row -- columns copied with
+// the diagonal inserted, diagonal values v + 1 -- and for gcn_norm each value
+// scaled (v * dis_row[i]) * dis_col[j], two roundings in that order
+// (src/layers.cpp:192-198).  dis_col is indexed by global column.
+// Each warp keeps CH chunks of 32 entries in flight (one load per lane per
+// array per chunk, all issued before any is used).
+constexpr int kSlChunks = 4;
+
+template <bool DEG>
+__global__ void self_loop_rows_kernel(int64_t N, int64_t off, const int32_t* rp, const int32_t* ci, const float* v,
+                                      const int32_t* order, int32_t* out_rp, int32_t* insert, float* dis) {
+    const int64_t slot = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (slot >= N) return;
+    const int64_t row = order ? static_cast<int64_t>(order[slot]) : slot;
     const int lane = threadIdx.x & 31;
     const int32_t s = rp[row], e = rp[row + 1];
+    const int32_t i32 = static_cast<int32_t>(row + off);
     bool has = false;
-    for (int32_t b = s; b < e && !has; b += 32) {
-        const bool d = (b + lane < e) && ci[b + lane] == static_cast<int32_t>(row + off);
-        has = __any_sync(0xffffffffu, d);
+    int32_t ins = -1;                 // offset of the first column > i, -1 = none seen
+    float part = 0.0f;                // this lane's partial degree (integer rows)
+    bool integral = true;
+    uint32_t max_bits = 0;            // max |v| as bits (order-preserving for |v|)
+    for (int32_t b = s; b < e; b += 32 * kSlChunks) {
+        int32_t c[kSlChunks];
+        float x[kSlChunks];
+#pragma unroll
+        for (int u = 0; u < kSlChunks; ++u) {
+            const int32_t t = b + 32 * u + lane;
+            c[u] = t < e ? ci[t] : INT32_MIN;
+            if (DEG) x[u] = t < e ? v[t] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kSlChunks; ++u) {
+            const bool diag = c[u] == i32;
+            const unsigned gt = __ballot_sync(0xffffffffu, c[u] > i32);
+            if (ins < 0 && gt) ins = (b + 32 * u - s) + __ffs(gt) - 1;
+            has = has || __any_sync(0xffffffffu, diag);
+            if (DEG) {
+                part = __fadd_rn(part, diag ? __fadd_rn(x[u], 1.0f) : x[u]);
+                integral = integral && (x[u] == truncf(x[u]));
+                max_bits = max(max_bits, __float_as_uint(x[u]) & 0x7fffffffu);
+            }
+        }
+        if (!DEG && has) break;  // add_self_loops alone only needs to know that it is there
     }
-    if (lane == 0) out_rp[row + 1] = (e - s) + (has ? 0 : 1);
-    if (row == 0 && lane == 0) out_rp[0] = 0;
+    const int32_t len = e - s;
+    const int32_t pos = has ? -1 : (ins >= 0 ? ins : len);
+    if (DEG) {
+        integral = __all_sync(0xffffffffu, integral);
+        max_bits = __reduce_max_sync(0xffffffffu, max_bits);
+        float deg;
+        if (integral && static_cast<double>(len) * (static_cast<double>(__uint_as_float(max_bits)) + 1.0) + 1.0 <
+                            16777216.0) {
+            for (int d = 16; d > 0; d >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, d));
+            deg = has ? part : __fadd_rn(part, 1.0f);
+        } else {
+            // the reference's chain: d = 0; d += v in stored order
+            deg = 0.0f;
+            for (int32_t b = s; b < e; b += 32) {
+                const int32_t t = b + lane;
+                float x = t < e ? v[t] : 0.0f;
+                if (t < e && ci[t] == i32) x = __fadd_rn(x, 1.0f);
+                const int n = min(32, e - b);
+                for (int k = 0; k < n; ++k) {
+                    if (b - s + k == pos) deg = __fadd_rn(deg, 1.0f);
+                    deg = __fadd_rn(deg, __shfl_sync(0xffffffffu, x, k));
+                }
+            }
+            if (pos == len) deg = __fadd_rn(deg, 1.0f);
+        }
+        if (lane == 0) dis[row] = deg > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(deg)) : 0.0f;
+    }
+    if (lane == 0) {
+        out_rp[row + 1] = len + (has ? 0 : 1);
+        insert[row] = pos;
+        if (row == 0) out_rp[0] = 0;
+    }
 }
 
-// Pass 2: copy with the diagonal inserted before the first column > i (or
-// appended), an existing diagonal becoming v + 1.  NORM also applies
-// gcn_norm's scale (pass 3 of the norm, after the degrees are known).
+template <bool NORM>
 __global__ void self_loop_fill_kernel(int64_t N, int64_t off, const int32_t* rp, const int32_t* ci, const float* v,
-                                      const int32_t* out_rp, int32_t* out_ci, float* out_v) {
-    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    if (row >= N) return;
+                                      const int32_t* order, const int32_t* out_rp, const int32_t* insert,
+                                      const float* dis_row, const float* dis_col, int32_t* out_ci, float* out_v) {
+    const int64_t slot = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (slot >= N) return;
+    const int64_t row = order ? static_cast<int64_t>(order[slot]) : slot;
     const int lane = threadIdx.x & 31;
     const int32_t s = rp[row], e = rp[row + 1];
     const int32_t o = out_rp[row];
-    const bool insert = (out_rp[row + 1] - o) != (e - s);
+    const int32_t ins = insert[row];
     const int32_t i32 = static_cast<int32_t>(row + off);
-    int32_t ins = e - s;  // insertion offset within the row (append by default)
-    if (insert) {
-        for (int32_t b = s; b < e; b += 32) {
-            const bool gt = (b + lane < e) && ci[b + lane] > i32;
-            const unsigned m = __ballot_sync(0xffffffffu, gt);
-            if (m) { ins = (b - s) + __ffs(m) - 1; break; }
+    const float di = NORM ? dis_row[row] : 1.0f;
+    for (int32_t b = s; b < e; b += 32 * kSlChunks) {
+        int32_t c[kSlChunks];
+        float x[kSlChunks], dj[kSlChunks];
+#pragma unroll
+        for (int u = 0; u < kSlChunks; ++u) {
+            const int32_t t = b + 32 * u + lane;
+            c[u] = t < e ? ci[t] : 0;
+            x[u] = t < e ? v[t] : 0.0f;
+        }
+        if (NORM) {
+#pragma unroll
+            for (int u = 0; u < kSlChunks; ++u) dj[u] = (b + 32 * u + lane < e) ? dis_col[c[u]] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kSlChunks; ++u) {
+            const int32_t t = b + 32 * u + lane;
+            if (t < e) {
+                const int32_t rel = t - s;
+                const int32_t p = o + rel + ((ins >= 0 && rel >= ins) ? 1 : 0);
+                const float xs = (c[u] == i32) ? __fadd_rn(x[u], 1.0f) : x[u];
+                out_ci[p] = c[u];
+                out_v[p] = NORM ? __fmul_rn(__fmul_rn(xs, di), dj[u]) : xs;
+            }
         }
     }
-    for (int32_t b = s; b < e; b += 32) {
-        const int32_t t = b + lane;
-        if (t < e) {
-            const int32_t c = ci[t];
-            const int32_t rel = t - s;
-            const int32_t pos = o + rel + ((insert && rel >= ins) ? 1 : 0);
-            out_ci[pos] = c;
-            out_v[pos] = (c == i32) ? __fadd_rn(v[t], 1.0f) : v[t];
-        }
-    }
-    if (insert && lane == 0) {
+    if (ins >= 0 && lane == 0) {
         out_ci[o + ins] = i32;
-        out_v[o + ins] = 1.0f;
+        out_v[o + ins] = NORM ? __fmul_rn(__fmul_rn(1.0f, di), dis_col[i32]) : 1.0f;
     }
 }
 
-// Degree (sequential float sum of the self-looped row) and 1/sqrt(deg).
+// Degree (sequential float sum of a self-looped row) and 1/sqrt(deg): the
+// standalone form for rows that already hold their self-loops.
 __global__ void gcn_degree_kernel(int64_t N, const int32_t* rp, const float* v, float* dis) {
     const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     if (row >= N) return;
     const int lane = threadIdx.x & 31;
     const int32_t s = rp[row], e = rp[row + 1];
-    float d = 0.0f;
+    float part = 0.0f;
+    bool integral = true;
+    uint32_t max_bits = 0;
     for (int32_t b = s; b < e; b += 32) {
         const float x = (b + lane < e) ? v[b + lane] : 0.0f;
-        const int n = min(32, e - b);
-        for (int k = 0; k < n; ++k) d = __fadd_rn(d, __shfl_sync(0xffffffffu, x, k));
+        part = __fadd_rn(part, x);
+        integral = integral && (x == truncf(x));
+        max_bits = max(max_bits, __float_as_uint(x) & 0x7fffffffu);
+    }
+    integral = __all_sync(0xffffffffu, integral);
+    max_bits = __reduce_max_sync(0xffffffffu, max_bits);
+    float d;
+    if (integral && static_cast<double>(e - s) * static_cast<double>(__uint_as_float(max_bits)) < 16777216.0) {
+        for (int k = 16; k > 0; k >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, k));
+        d = part;  // exact: see self_loop_rows_kernel
+    } else {
+        d = 0.0f;
+        for (int32_t b = s; b < e; b += 32) {
+            const float x = (b + lane < e) ? v[b + lane] : 0.0f;
+            const int n = min(32, e - b);
+            for (int k = 0; k < n; ++k) d = __fadd_rn(d, __shfl_sync(0xffffffffu, x, k));
+        }
     }
     if (lane == 0) dis[row] = d > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(d)) : 0.0f;
 }
@@ -429,16 +535,44 @@ void edge_list_to_csr(int64_t N, int64_t E, const int32_t* src, const int32_t* d
     }
 }
 
+// Pass 1 of a row block: out_rp (scanned), insert[], and with DEG dis[].
+void self_loop_rows(int64_t N, int64_t off, const int32_t* rp, const int32_t* ci, const float* v,
+                    const int32_t* order, int32_t* orp, int32_t* insert, float* dis, cudaStream_t s) {
+    if (N == 0) {
+        TG_CUDA(cudaMemsetAsync(orp, 0, sizeof(int32_t), s));
+        return;
+    }
+    if (dis)
+        launch("self_loop_rows<deg>", self_loop_rows_kernel<true>, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, off,
+               rp, ci, v, order, orp, insert, dis);
+    else
+        launch("self_loop_rows", self_loop_rows_kernel<false>, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, off, rp,
+               ci, v, order, orp, insert, dis);
+    inclusive_scan_i32(orp + 1, N, s);
+}
+
+// Pass 2 of a row block; dis_row == nullptr: add_self_loops alone.
+void self_loop_fill(int64_t N, int64_t off, const int32_t* rp, const int32_t* ci, const float* v,
+                    const int32_t* order, const int32_t* orp, const int32_t* insert, const float* dis_row,
+                    const float* dis_col, int32_t* oci, float* ov, cudaStream_t s) {
+    if (N == 0) return;
+    if (dis_row)
+        launch("self_loop_fill<norm>", self_loop_fill_kernel<true>, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, off,
+               rp, ci, v, order, orp, insert, dis_row, dis_col, oci, ov);
+    else
+        launch("self_loop_fill", self_loop_fill_kernel<false>, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, off, rp,
+               ci, v, order, orp, insert, dis_row, dis_col, oci, ov);
+}
+
 int64_t add_self_loops(int64_t N, int64_t off, const int32_t* rp, const int32_t* ci, const float* v, int32_t* orp,
                        int32_t* oci, float* ov, cudaStream_t s) {
     if (N == 0) {
         TG_CUDA(cudaMemsetAsync(orp, 0, sizeof(int32_t), s));
         return 0;
     }
-    launch("self_loop_count", self_loop_count_kernel, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, off, rp, ci, orp);
-    inclusive_scan_i32(orp + 1, N, s);
-    launch("self_loop_fill", self_loop_fill_kernel, dim3(warp_rows_grid(N)), dim3(256), 0, s, N, off, rp, ci, v,
-           static_cast<const int32_t*>(orp), oci, ov);
+    Scratch<int32_t> insert(static_cast<size_t>(N), s);
+    self_loop_rows(N, off, rp, ci, v, nullptr, orp, insert.p, nullptr, s);
+    self_loop_fill(N, off, rp, ci, v, nullptr, orp, insert.p, nullptr, nullptr, oci, ov, s);
     return read_back(orp + N, s);
 }
 
@@ -453,12 +587,15 @@ void scale_sym(int64_t N, const int32_t* rp, const int32_t* ci, float* v, const 
 
 int64_t gcn_norm(int64_t N, const int32_t* rp, const int32_t* ci, const float* v, int32_t* orp, int32_t* oci,
                  float* ov, cudaStream_t s) {
-    const int64_t out = add_self_loops(N, 0, rp, ci, v, orp, oci, ov, s);
-    if (N == 0) return 0;
+    if (N == 0) {
+        TG_CUDA(cudaMemsetAsync(orp, 0, sizeof(int32_t), s));
+        return 0;
+    }
+    Scratch<int32_t> insert(static_cast<size_t>(N), s);
     Scratch<float> dis(static_cast<size_t>(N), s);
-    degree_inv_sqrt(N, orp, ov, dis.p, s);
-    scale_sym(N, orp, oci, ov, dis.p, dis.p, s);
-    return out;
+    self_loop_rows(N, 0, rp, ci, v, nullptr, orp, insert.p, dis.p, s);
+    self_loop_fill(N, 0, rp, ci, v, nullptr, orp, insert.p, dis.p, dis.p, oci, ov, s);
+    return read_back(orp + N, s);
 }
 
 }  // namespace tg
@@ -517,6 +654,40 @@ TG_API tg_status tg_add_self_loops_rows_f32(int64_t rows, int64_t row_offset, in
         const int64_t n = add_self_loops(rows, row_offset, row_ptr, col_ind, values, row_ptr_out, col_ind_out,
                                          values_out, as_stream(stream));
         if (nnz_out) *nnz_out = n;
+    });
+}
+
+TG_API tg_status tg_gcn_norm_rows_degrees_f32(int64_t rows, int64_t row_offset, int64_t nnz, const int32_t* row_ptr,
+                                              const int32_t* col_ind, const float* values, const int32_t* row_order,
+                                              int32_t* row_ptr_out, int32_t* insert_out, float* dis_out,
+                                              void* stream) {
+    return guard([&] {
+        require_device();
+        if (rows < 0 || row_offset < 0 || nnz < 0) invalid("gcn_norm: negative size");
+        if (nnz + rows > INT32_MAX) invalid("gcn_norm: result does not fit int32 row_ptr");
+        check_ptr("gcn_norm", "row_ptr_out", row_ptr_out, true);
+        check_ptr("gcn_norm", "row_ptr/insert_out/dis_out", row_ptr && insert_out && dis_out ? row_ptr : nullptr,
+                  rows > 0);
+        check_ptr("gcn_norm", "col_ind/values", col_ind && values ? col_ind : nullptr, nnz > 0);
+        self_loop_rows(rows, row_offset, row_ptr, col_ind, values, row_order, row_ptr_out, insert_out, dis_out,
+                       as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_gcn_norm_rows_fill_f32(int64_t rows, int64_t row_offset, const int32_t* row_ptr,
+                                           const int32_t* col_ind, const float* values, const int32_t* row_order,
+                                           const int32_t* row_ptr_out, const int32_t* insert, const float* dis_row,
+                                           const float* dis_col, int32_t* col_ind_out, float* values_out,
+                                           void* stream) {
+    return guard([&] {
+        require_device();
+        if (rows < 0 || row_offset < 0) invalid("gcn_norm: negative size");
+        check_ptr("gcn_norm", "row_ptr/row_ptr_out/insert/dis_row/dis_col/col_ind_out/values_out",
+                  row_ptr && row_ptr_out && insert && dis_row && dis_col && col_ind_out && values_out ? row_ptr
+                                                                                                      : nullptr,
+                  rows > 0);
+        self_loop_fill(rows, row_offset, row_ptr, col_ind, values, row_order, row_ptr_out, insert, dis_row, dis_col,
+                       col_ind_out, values_out, as_stream(stream));
     });
 }
 

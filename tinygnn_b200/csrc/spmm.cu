@@ -36,9 +36,8 @@ template <int VEC, int LPR, int SPL, bool CVEC>
 void launch_gather(const GatherArgs& a, cudaStream_t s) {
     constexpr int RPB = (256 / 32) * (32 / LPR);  // rows per block
     // Gathered rows in flight per batch (sweep on the Reddit-shaped graph,
-    // degree-ordered: 4 for 32-lane rows, 8 for narrower ones); with 2-3
-    // vectors per lane 4 (a divisor of the 4- and 8-entry windows).
-    constexpr int U = (SPL >= 4) ? 2 : (SPL >= 2 ? 4 : (LPR == 32 ? 4 : 8));
+    // degree-ordered: 4 for 32-lane rows, 8 for narrower ones).
+    constexpr int U = (SPL >= 4) ? 2 : (SPL == 2 ? 4 : (LPR == 32 ? 4 : 8));
     const int64_t per_pass = static_cast<int64_t>(LPR) * SPL * VEC;
     const int64_t passes = ceil_div(a.F, per_pass);
     dim3 grid(static_cast<unsigned>(ceil_div(a.M, RPB)), static_cast<unsigned>(passes));
@@ -50,19 +49,19 @@ void launch_gather(const GatherArgs& a, cudaStream_t s) {
                s, a);
 }
 
-// Lanes per row (LPR) x vectors per lane (SPL) for a row of S vector slots:
-// the shape whose LPR * SPL slots leave the fewest lanes idle.  A 41-float
-// row (11 float4 slots, the GCN output layer) takes 4 lanes x 3 vectors --
-// 11 of 12 slots busy, 8 rows per warp -- where 16 lanes x 1 left 5 of 16
-// idle; it also needs a quarter of the index shuffles per gathered row.
+// Lanes per row (LPR) x vectors per lane (SPL) for a row of S vector slots.
+// Each load instruction should cover few 128-byte lines: the L1TEX data
+// pipe's wavefronts, not the idle lanes, bound the narrow gathers.  Measured
+// on the Reddit-shaped layer-2 gather (41-float rows, 11 float4 slots): 16
+// lanes x 1 vector (two rows per instruction, 5 of 16 lanes idle) 1.75 ms;
+// 4 lanes x 3 vectors (eight rows per instruction, 11 of 12 slots busy)
+// 2.25 ms -- each instruction touched ~12 lines for 512 bytes.
 template <int VEC, bool CVEC>
 void dispatch_lpr(const GatherArgs& a, cudaStream_t s) {
     const int64_t S = ceil_div(a.F, VEC);  // vector slots per row
     if (S <= 4) launch_gather<VEC, 4, 1, CVEC>(a, s);
     else if (S <= 8) launch_gather<VEC, 8, 1, CVEC>(a, s);
-    else if (S <= 12) launch_gather<VEC, 4, 3, CVEC>(a, s);
     else if (S <= 16) launch_gather<VEC, 16, 1, CVEC>(a, s);
-    else if (S <= 24) launch_gather<VEC, 8, 3, CVEC>(a, s);
     else if (S <= 32) launch_gather<VEC, 32, 1, CVEC>(a, s);
     else if (S <= 64) launch_gather<VEC, 32, 2, CVEC>(a, s);
     else launch_gather<VEC, 32, 4, CVEC>(a, s);  // feature passes of 128 vectors beyond

@@ -177,14 +177,24 @@ class PeerExchange:
 
 def gcn_norm_rows(A: CSR, row0: int, R: int, comm: Comm, dis_all: Optional[torch.Tensor] = None) -> CSR:
     """gcn_norm of this rank's row block (global columns), bit-identical to the
-    rows of the single-GPU gcn_norm."""
-    asl = ops.add_self_loops_rows(A, row0)
+    rows of the single-GPU gcn_norm: one pass for the self-looped row lengths
+    and 1/sqrt(deg), the all-gather of 1/sqrt(deg), one pass writing the
+    scaled self-looped rows."""
     if dis_all is None:
         dis_all = torch.zeros(R * comm.world, dtype=torch.float32, device=A.row_ptr.device)
     mine = dis_all[comm.rank * R:comm.rank * R + A.n_rows]
-    ops.degree_inv_sqrt(asl, out=mine)
+    rp, ins = ops.gcn_norm_rows_degrees(A, row0, mine)
     comm.all_gather_rows(dis_all.view(-1, 1), R)
-    return ops.scale_sym_(asl, mine, dis_all)
+    return ops.gcn_norm_rows_fill(A, row0, rp, ins, mine, dis_all)
+
+
+def gcn_norm_rows_scheduled(A: CSR, row0: int, R: int, comm: Comm, dis_all: Optional[torch.Tensor] = None) -> CSR:
+    """gcn_norm_rows with the raw rows' longest-first schedule computed once:
+    both normalisation passes run in it, and the normalised block keeps it
+    for the gathers (same arithmetic; the order changes speed only)."""
+    if A.order is None:
+        A = CSR(A.n_rows, A.n_cols, A.row_ptr, A.col_ind, A.values, ops.degree_order(A))
+    return gcn_norm_rows(A, row0, R, comm, dis_all)
 
 
 @dataclass
@@ -467,14 +477,13 @@ class ShardedModel:
             d_v.fill_(1.0)
         cur.wait_event(csr_ready)
         A = CSR(self.rows, self.n, d_rp, d_ci, d_v)
-        A_gcn = (gcn_norm_rows(A, self.row0, self.R, self.comm, bufs["dis"])
+        A_gcn = (gcn_norm_rows_scheduled(A, self.row0, self.R, self.comm, bufs["dis"])
                  if any(L.kind == "gcn" for L in self.layers) else None)
         if single and nb > 1:
             # Layer 1 per feature block: GEMM of block q's rows, then the gather
             # pass over the columns of block q (exact: passes in column order).
             L = self.layers[0]
             fo = L.W.shape[1]
-            A_gcn.order = ops.degree_order(A_gcn)
             sp = ops.column_splits(A_gcn, nb, width)
             B = self.full[0][:self.n, :fo]
             for q in range(nb):

@@ -365,6 +365,37 @@ def scale_sym_(A: CSR, dis_row: torch.Tensor, dis_col: torch.Tensor) -> CSR:
     return A
 
 
+def gcn_norm_rows_degrees(A: CSR, row_offset: int, dis_out: torch.Tensor, row_order=None):
+    """Pass 1 of gcn_norm on a row block: (row_ptr of the self-looped block,
+    per-row insertion offsets); 1/sqrt(deg) into ``dis_out`` (float32[n_rows]).
+    ``row_order`` (or A's own schedule) only orders the work."""
+    N = A.n_rows
+    dev = A.row_ptr.device
+    rp = torch.empty(N + 1, dtype=torch.int32, device=dev)
+    ins = torch.empty(max(N, 1), dtype=torch.int32, device=dev)
+    check(lib.tg_gcn_norm_rows_degrees_f32(N, row_offset, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values),
+                                           _p(_ord(A, row_order)), _p(rp), _p(ins), _p(dis_out), _stream()))
+    return rp, ins
+
+
+def gcn_norm_rows_fill(A: CSR, row_offset: int, rp_out: torch.Tensor, insert: torch.Tensor, dis_row: torch.Tensor,
+                       dis_col: torch.Tensor, row_order=None) -> CSR:
+    """Pass 2 of gcn_norm on a row block: the self-looped rows, values scaled
+    (v * dis_row[i]) * dis_col[j] (global columns).  The result keeps A's row
+    schedule: its rows have the same lengths, plus one where a diagonal was
+    inserted."""
+    N = A.n_rows
+    cap = A.nnz + N
+    dev = A.row_ptr.device
+    order = _ord(A, row_order)
+    ci = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+    v = torch.empty(max(cap, 1), dtype=torch.float32, device=dev)
+    check(lib.tg_gcn_norm_rows_fill_f32(N, row_offset, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(order),
+                                        _p(rp_out), _p(insert), _p(dis_row), _p(dis_col), _p(ci), _p(v), _stream()))
+    nnz = int(rp_out[N].item()) if N else 0  # after both passes are queued
+    return CSR(N, A.n_cols, rp_out, ci[:nnz], v[:nnz], order)
+
+
 def csr_validate(A: CSR) -> None:
     """Tensor::sparse_csr's checks (src/tensor.cpp:46-86) on device arrays."""
     check(lib.tg_csr_validate(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _stream()))
