@@ -476,7 +476,7 @@ def run_ours(args):
     # A normalised graph kept from one call to the next, with its
     # longest-rows-first schedule: only the layers-only figure uses it.
     A_cached = A_gcn if A_gcn is not None else CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind,
-                                                   A_raw.values)
+                                                   A_raw.values, validated=A_raw.validated)
     A_cached.with_degree_order()
     nnz_local = A_gcn.nnz if A_gcn is not None else A_raw.nnz
     nnz_total = nnz_local
@@ -510,7 +510,8 @@ def run_ours(args):
             An = gcn_norm_rows_scheduled(A_raw, r0, R, comm, dis_buf)  # keeps the raw rows' schedule
             model.forward(An, None, X)
         else:
-            Ar = CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind, A_raw.values)
+            Ar = CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind, A_raw.values,
+                     validated=A_raw.validated)
             Ar.with_degree_order()
             model.forward(None, Ar, X)
 

@@ -84,12 +84,24 @@ typedef enum tg_mode { TG_MODE_EXACT = 0, TG_MODE_FAST = 1 } tg_mode;
 /* ── library ─────────────────────────────────────────────────────────────── */
 TG_API const char* tg_last_error_message(void); /* thread-local */
 TG_API const char* tg_version(void);
-TG_API int32_t tg_abi_version(void);
+TG_API int32_t tg_abi_version(void); /* 2 */
 /* Number of CUDA devices; 0 means every compute call returns TG_ERR_NO_DEVICE. */
 TG_API int32_t tg_device_count(void);
 /* How many kernels this library has launched in this process (all devices);
  * used by benchmarks to count their own launches. */
 TG_API uint64_t tg_kernel_launch_count(void);
+
+/* Input CSR checks.  Every entry point that reads a caller's CSR first
+ * checks it on the device -- Tensor::sparse_csr's checks (src/tensor.cpp:
+ * 46-86): row_ptr non-decreasing, row_ptr[rows] == nnz, every column in
+ * [0, cols) -- plus row_ptr[0] >= 0 and every row_order entry in [0, rows),
+ * and returns TG_ERR_INVALID_ARGUMENT with the reference's message before
+ * any kernel reads through the arrays.  The check reads row_ptr and col_ind
+ * once and synchronises the stream.  A caller whose CSRs were checked
+ * already (built by this library, or by tg_csr_validate) turns it off for
+ * the calling thread with tg_set_csr_checks(0); returns the previous
+ * setting (1 = on, the default). */
+TG_API int32_t tg_set_csr_checks(int32_t enabled);
 
 /* ── dense ops (level 1) ─────────────────────────────────────────────────── */
 
@@ -282,8 +294,9 @@ TG_API tg_status tg_gcn_norm_rows_degrees_f32(int64_t rows, int64_t row_offset, 
                                               const float* values, const int32_t* row_order,
                                               int32_t* row_ptr_out, int32_t* insert_out,
                                               float* dis_out, void* stream);
-TG_API tg_status tg_gcn_norm_rows_fill_f32(int64_t rows, int64_t row_offset, const int32_t* row_ptr,
-                                           const int32_t* col_ind, const float* values,
+TG_API tg_status tg_gcn_norm_rows_fill_f32(int64_t rows, int64_t row_offset, int64_t n_cols,
+                                           const int32_t* row_ptr, const int32_t* col_ind,
+                                           const float* values,
                                            const int32_t* row_order, const int32_t* row_ptr_out,
                                            const int32_t* insert, const float* dis_row,
                                            const float* dis_col, int32_t* col_ind_out,

@@ -37,7 +37,7 @@ def test_python_binding_covers_every_declared_symbol():
 
 def test_library_metadata_calls():
     from tinygnn_b200 import _lib
-    assert _lib.lib.tg_abi_version() == 1
+    assert _lib.lib.tg_abi_version() == 2
     assert b"sm_100a" in _lib.lib.tg_version()
     assert _lib.lib.tg_device_count() >= 0
 

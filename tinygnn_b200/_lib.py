@@ -59,7 +59,8 @@ SIGNATURES = {
     "tg_csr_degree_inv_sqrt_f32": (i32, [i64, vp, vp, vp, vp]),
     "tg_csr_scale_sym_f32": (i32, [i64, vp, vp, vp, vp, vp, vp]),
     "tg_gcn_norm_rows_degrees_f32": (i32, [i64, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp]),
-    "tg_gcn_norm_rows_fill_f32": (i32, [i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "tg_gcn_norm_rows_fill_f32": (i32, [i64, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "tg_set_csr_checks": (i32, [i32]),
     "tg_gcn_layer_f32": (i32, [i64, i64, vp, vp, vp, vp, i64, i64, i64, vp, vp, i32, vp, i64, vp, i32, vp]),
     "tg_sage_layer_f32": (i32, [i64, i64, vp, vp, vp, i64, i64, i64, vp, vp, vp, i32, i32, vp, i64, vp, i32, vp]),
     "tg_gat_layer_f32": (i32, [i64, i64, vp, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp, f32, i32, i32, vp, i64,

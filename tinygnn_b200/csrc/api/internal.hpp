@@ -33,6 +33,17 @@ inline void cuda(cudaError_t e, const char* what) {
 
 inline int mode() { return fast_math() ? TG_MODE_FAST : TG_MODE_EXACT; }
 
+// The API's CSR Tensors are validated where they are built
+// (Tensor::sparse_csr) or come from the library itself, so the C-ABI calls
+// made for them skip the ABI's own input checks (restored on scope exit).
+struct TrustedCsr {
+    int32_t prev;
+    TrustedCsr() : prev(tg_set_csr_checks(0)) {}
+    ~TrustedCsr() { tg_set_csr_checks(prev); }
+    TrustedCsr(const TrustedCsr&) = delete;
+    TrustedCsr& operator=(const TrustedCsr&) = delete;
+};
+
 inline std::size_t pad4(std::size_t n) { return (n + 3) / 4 * 4; }
 
 inline std::string shape_str(std::size_t r, std::size_t c) {

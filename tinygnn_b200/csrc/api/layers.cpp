@@ -35,6 +35,7 @@ Tensor expand_csr(const Tensor& A, bool norm) {
     int32_t* ci = dalloc<int32_t>(cap);
     float* v = dalloc<float>(cap);
     int64_t out_nnz = 0;
+    const detail::TrustedCsr trusted_csr;
     const auto fn = norm ? tg_gcn_norm_f32 : tg_add_self_loops_f32;
     const tg_status st = fn(static_cast<int64_t>(N), static_cast<int64_t>(nnz), A.device_row_ptr(),
                             A.device_col_ind(), A.device_data(), rp, ci, v, &out_nnz, stream());
@@ -103,6 +104,7 @@ Tensor sage_max_aggregate(const Tensor& A, const Tensor& H) {
                                     std::to_string(H.rows()) + ").");
     Tensor out = Tensor::dense_device(A.rows(), H.cols());
     if (A.rows() == 0 || H.cols() == 0) return out;
+    const detail::TrustedCsr trusted_csr;
     check(tg_sage_max_aggregate_f32(static_cast<int64_t>(A.rows()), static_cast<int64_t>(A.cols()),
                                     static_cast<int64_t>(A.nnz()), A.device_row_ptr(), A.device_col_ind(),
                                     H.device_data(), static_cast<int64_t>(H.cols()),
@@ -128,6 +130,7 @@ Tensor edge_softmax(const Tensor& A) {
         detail::cuda(cudaMemsetAsync(v, 0, nnz * sizeof(float), detail::cstream()), "edge_softmax");
     }
     Tensor t = TensorAccess::csr_from_device(N, A.cols(), rp, ci, v, nnz);
+    const detail::TrustedCsr trusted_csr;
     if (N) check(tg_edge_softmax_f32(static_cast<int64_t>(N), static_cast<int64_t>(nnz), t.device_row_ptr(),
                                      A.device_data(), t.mutable_device_data(), stream()));
     return t;
@@ -178,6 +181,7 @@ Tensor GCNLayer::forward(const Tensor& A_norm, const Tensor& H) const {
                       H.device_data(), static_cast<int64_t>(H.device_ld()), weight_.device_data(),
                       static_cast<int64_t>(weight_.device_ld()), HW.mutable_device_data(),
                       static_cast<int64_t>(HW.device_ld()), nullptr, TG_ACT_NONE, 0.0f, detail::mode(), stream()));
+    const detail::TrustedCsr trusted_csr;
     check(tg_spmm_f32(static_cast<int64_t>(N), static_cast<int64_t>(N), static_cast<int64_t>(A_norm.nnz()),
                       A_norm.device_row_ptr(), A_norm.device_col_ind(), A_norm.device_data(), HW.device_data(),
                       static_cast<int64_t>(out_features_), static_cast<int64_t>(HW.device_ld()),
@@ -239,6 +243,7 @@ Tensor SAGELayer::forward(const Tensor& A, const Tensor& H) const {
                               static_cast<int64_t>(pr->device_ld()), nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST,
                               stream()));
         }
+        const detail::TrustedCsr trusted_csr;
         check(tg_sage_mean_combine_f32(static_cast<int64_t>(N), static_cast<int64_t>(A.cols()),
                                        static_cast<int64_t>(A.nnz()), A.device_row_ptr(), A.device_col_ind(),
                                        Tn.device_data(), static_cast<int64_t>(Fo), static_cast<int64_t>(Tn.device_ld()),
@@ -250,6 +255,7 @@ Tensor SAGELayer::forward(const Tensor& A, const Tensor& H) const {
     }
     // Aggregate first, then the interleaved dual product (bit-identical).
     Tensor agg = Tensor::dense_device(N, Fi);
+    const detail::TrustedCsr trusted_csr;
     check(tg_sage_aggregate_f32(static_cast<int64_t>(N), static_cast<int64_t>(A.cols()), static_cast<int64_t>(A.nnz()),
                                 A.device_row_ptr(), A.device_col_ind(), H.device_data(), static_cast<int64_t>(Fi),
                                 static_cast<int64_t>(H.device_ld()), agg.mutable_device_data(),
@@ -314,6 +320,7 @@ Tensor GATLayer::forward(const Tensor& A, const Tensor& H) const {
     Tensor out = Tensor::dense_device(N, out_features_);
     if (N == 0) return out;
     const Contig W(weight_);
+    const detail::TrustedCsr trusted_csr;
     check(tg_gat_layer_f32(static_cast<int64_t>(N), static_cast<int64_t>(A.nnz()), A.device_row_ptr(),
                            A.device_col_ind(), H.device_data(), static_cast<int64_t>(H.device_ld()),
                            static_cast<int64_t>(in_features_), 1, static_cast<int64_t>(out_features_), W.ptr,

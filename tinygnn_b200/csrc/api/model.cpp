@@ -219,6 +219,7 @@ Tensor Model::forward(const Tensor& adjacency, const Tensor& features) const {
                 }
                 const std::size_t ocols = e.gat_concat ? heads * d : d;
                 out = Tensor::dense_device(in->rows(), ocols);
+                const detail::TrustedCsr trusted_csr;
                 check(tg_gat_layer_f32(static_cast<int64_t>(in->rows()), static_cast<int64_t>(A_sl.nnz()),
                                        A_sl.device_row_ptr(), A_sl.device_col_ind(), in->device_data(),
                                        static_cast<int64_t>(in->device_ld()), static_cast<int64_t>(fi),

@@ -65,6 +65,7 @@ Tensor spmm(const Tensor& A, const Tensor& B) {
                                     std::to_string(K) + " vs " + std::to_string(K2) + ").");
     Tensor C = Tensor::dense_device(M, N);
     if (M == 0 || N == 0 || A.nnz() == 0) return C;  // zeros (ops.cpp:234)
+    const detail::TrustedCsr trusted_csr;
     check(tg_spmm_f32(static_cast<int64_t>(M), static_cast<int64_t>(K), static_cast<int64_t>(A.nnz()),
                       A.device_row_ptr(), A.device_col_ind(), A.device_data(), B.device_data(),
                       static_cast<int64_t>(N), static_cast<int64_t>(B.device_ld()), C.mutable_device_data(),

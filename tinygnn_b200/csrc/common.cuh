@@ -65,6 +65,29 @@ tg_status guard(F&& f) noexcept {
 
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
+// ── Input CSR checks ─────────────────────────────────────────────────────
+// Tensor::sparse_csr's checks (src/tensor.cpp:46-86) on device arrays --
+// row_ptr non-decreasing, row_ptr[rows] == nnz, every column in [0, cols) --
+// plus row_ptr[0] >= 0 (with the others, every row lies inside col_ind) and,
+// when given, every row_order entry in [0, rows).  cols < 0: the columns are
+// only compared, never used as addresses (no range check); nnz < 0: nnz is
+// row_ptr[rows].  Throws invalid_argument with the reference's message.
+// `words` (nullable) is device memory for the result (sizeof 32 bytes);
+// without it the result goes to pool scratch.  Synchronises `s`.
+void csr_validate(int64_t rows, int64_t cols, int64_t nnz, const int32_t* rp, const int32_t* ci, cudaStream_t s,
+                  const int32_t* order = nullptr, void* words = nullptr);
+constexpr size_t kCsrCheckWordsBytes = 32;
+
+// The calling thread's tg_set_csr_checks setting (on unless turned off).
+bool csr_checks_enabled();
+
+// What every entry point that reads a caller's CSR runs first: the checks
+// above, unless the caller turned them off for this thread.
+inline void check_csr_input(int64_t rows, int64_t cols, int64_t nnz, const int32_t* rp, const int32_t* ci,
+                            cudaStream_t s, const int32_t* order = nullptr, void* words = nullptr) {
+    if (csr_checks_enabled() && (rows > 0 || nnz > 0)) csr_validate(rows, cols, nnz, rp, ci, s, order, words);
+}
+
 // Number of SMs of the current device (cached per device).
 int num_sms();
 

@@ -244,7 +244,9 @@ TG_API tg_status tg_edge_softmax_f32(int64_t M, int64_t nnz, const int32_t* row_
                                      float* values_out, void* stream) {
     return guard([&] {
         require_device();
-        (void)nnz;
+        if (M < 0 || nnz < 0) invalid("edge_softmax: negative size");
+        if (M == 0) return;
+        check_csr_input(M, -1, nnz, row_ptr, nullptr, as_stream(stream));  // reads values by row only
         const dim3 grid(static_cast<unsigned>(ceil_div(M, 128)));
         launch("edge_softmax", edge_softmax_kernel, grid, dim3(128), 0, as_stream(stream), M, row_ptr,
                values, values_out);

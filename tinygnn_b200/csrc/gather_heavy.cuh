@@ -164,8 +164,8 @@ __global__ void __launch_bounds__(kHeavyThreads) gather_heavy_kernel(const Gathe
         if (tid < nrows) {
             const int32_t row = ld_i32(a.order + tb + static_cast<int64_t>(tid) * groups, stream);
             const int32_t rb = ld_i32(a.rp + row, stream), re = ld_i32(a.rp + row + 1, stream);
-            const int32_t s = a.seg_lo ? ld_i32(a.seg_lo + row, stream) : rb;
-            const int32_t e = a.seg_hi ? ld_i32(a.seg_hi + row, stream) : re;
+            const int32_t s = a.seg_lo ? max(rb, ld_i32(a.seg_lo + row, stream)) : rb;  // inside the row
+            const int32_t e = a.seg_hi ? min(re, ld_i32(a.seg_hi + row, stream)) : re;
             S.table[tid] = HeavyRow{row, s, e - s, re - rb, e > s ? (e - s + kHeavyG - 1) / kHeavyG : 1};
         }
         __syncthreads();

@@ -201,8 +201,9 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const GatherArgs a) {
 
     const int32_t row_begin = ld_i32(a.rp + row, stream);
     const int32_t row_end = ld_i32(a.rp + row + 1, stream);
-    const int32_t start = a.seg_lo ? ld_i32(a.seg_lo + row, stream) : row_begin;
-    const int32_t end = a.seg_hi ? ld_i32(a.seg_hi + row, stream) : row_end;
+    // a segment never reaches outside its row
+    const int32_t start = a.seg_lo ? max(row_begin, ld_i32(a.seg_lo + row, stream)) : row_begin;
+    const int32_t end = a.seg_hi ? min(row_end, ld_i32(a.seg_hi + row, stream)) : row_end;
 
     // Window of LPR entries: one (col, val) per lane; the next one is loaded
     // before the current one is consumed.

@@ -20,6 +20,7 @@
 // ============================================================================
 #include <algorithm>
 #include <climits>
+#include <memory>
 #include <vector>
 
 #include "launch.cuh"
@@ -106,19 +107,34 @@ __global__ void scan_add_kernel(int32_t* x, int64_t n, const int32_t* sums) {
 
 // ── CSR validation (Tensor::sparse_csr) ──────────────────────────────────────
 struct CheckWords {
-    unsigned long long first_bad_col;  // index of the first out-of-range col_ind
-    unsigned long long first_bad_rp;   // first i with row_ptr[i] < row_ptr[i-1]
+    unsigned long long first_bad_col;    // index of the first out-of-range col_ind
+    unsigned long long first_bad_rp;     // first i with row_ptr[i] < row_ptr[i-1]
+    unsigned long long first_bad_order;  // first i with row_order[i] outside [0, rows)
+    int32_t rp_first, rp_last;           // row_ptr[0], row_ptr[rows]
 };
+static_assert(sizeof(CheckWords) == kCsrCheckWordsBytes, "CheckWords size");
 
 __global__ void csr_check_kernel(int64_t rows, int64_t cols, int64_t nnz, const int32_t* rp, const int32_t* ci,
-                                 CheckWords* w) {
+                                 const int32_t* order, CheckWords* w) {
     const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < nnz; t += stride) {
-        const int32_t c = ci[t];
-        if (c < 0 || c >= cols) atomicMin(&w->first_bad_col, static_cast<unsigned long long>(t));
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (tid == 0 && rp) {
+        w->rp_first = rp[0];
+        w->rp_last = rp[rows];
     }
-    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x + 1; t <= rows; t += stride)
+    if (cols >= 0) {
+        // nnz < 0: the column array holds row_ptr[rows] entries
+        const int64_t n = nnz >= 0 ? nnz : (rp ? max(0, rp[rows]) : 0);
+        for (int64_t t = tid; t < n; t += stride) {
+            const int32_t c = ci[t];
+            if (c < 0 || c >= cols) atomicMin(&w->first_bad_col, static_cast<unsigned long long>(t));
+        }
+    }
+    for (int64_t t = tid + 1; t <= rows; t += stride)
         if (rp[t] < rp[t - 1]) atomicMin(&w->first_bad_rp, static_cast<unsigned long long>(t));
+    if (order)
+        for (int64_t t = tid; t < rows; t += stride)
+            if (order[t] < 0 || order[t] >= rows) atomicMin(&w->first_bad_order, static_cast<unsigned long long>(t));
 }
 
 // ── edge_list_to_csr ────────────────────────────────────────────────────────
@@ -434,19 +450,28 @@ void inclusive_scan_i32(int32_t* x, int64_t n, cudaStream_t s) {
     }
 }
 
-void csr_validate(int64_t rows, int64_t cols, int64_t nnz, const int32_t* rp, const int32_t* ci, cudaStream_t s) {
-    if (rows < 0 || cols < 0 || nnz < 0) invalid("Tensor::sparse_csr: negative size");
-    if (rows > 0 || nnz > 0) {
-        const int32_t last = rp ? read_back(rp + rows, s) : 0;
-        if (static_cast<int64_t>(last) != nnz)
-            invalid("Tensor::sparse_csr: row_ptr.back() (" + std::to_string(last) +
-                    ") must equal values.size() (" + std::to_string(nnz) + ")");
+void csr_validate(int64_t rows, int64_t cols, int64_t nnz, const int32_t* rp, const int32_t* ci, cudaStream_t s,
+                  const int32_t* order, void* words) {
+    if (rows < 0) invalid("Tensor::sparse_csr: negative size");
+    if (rows > 0 && !rp) invalid("Tensor::sparse_csr: row_ptr is NULL");
+    if (nnz > 0 && !ci && cols >= 0) invalid("Tensor::sparse_csr: col_ind is NULL");
+    if (rows == 0 && nnz <= 0 && !rp) return;
+    std::unique_ptr<Scratch<CheckWords>> own;
+    CheckWords* w = static_cast<CheckWords*>(words);
+    if (!w) {
+        own.reset(new Scratch<CheckWords>(1, s));
+        w = own->p;
     }
-    Scratch<CheckWords> w(1, s);
-    TG_CUDA(cudaMemsetAsync(w.p, 0xff, sizeof(CheckWords), s));
-    launch("csr_check", csr_check_kernel, dim3(stride_grid(std::max(nnz, rows), 256)), dim3(256), 0, s, rows, cols,
-           nnz, rp, ci, w.p);
-    const CheckWords h = read_back(w.p, s);
+    TG_CUDA(cudaMemsetAsync(w, 0xff, sizeof(CheckWords), s));
+    const int64_t span = std::max<int64_t>(std::max<int64_t>(nnz, rows), 1);
+    launch("csr_check", csr_check_kernel, dim3(stride_grid(span, 256)), dim3(256), 0, s, rows, cols, nnz, rp, ci, order,
+           w);
+    const CheckWords h = read_back(w, s);
+    if (rp && h.rp_first < 0)
+        invalid("Tensor::sparse_csr: row_ptr[0] (" + std::to_string(h.rp_first) + ") must be >= 0");
+    if (nnz >= 0 && rp && static_cast<int64_t>(h.rp_last) != nnz)
+        invalid("Tensor::sparse_csr: row_ptr.back() (" + std::to_string(h.rp_last) +
+                ") must equal values.size() (" + std::to_string(nnz) + ")");
     if (h.first_bad_col != ~0ull) {
         const int32_t c = read_back(ci + h.first_bad_col, s);
         invalid("Tensor::sparse_csr: col_ind[" + std::to_string(h.first_bad_col) + "] = " + std::to_string(c) +
@@ -457,6 +482,11 @@ void csr_validate(int64_t rows, int64_t cols, int64_t nnz, const int32_t* rp, co
         invalid("Tensor::sparse_csr: row_ptr must be non-decreasing; row_ptr[" + std::to_string(h.first_bad_rp) +
                 "] = " + std::to_string(a) + " < row_ptr[" + std::to_string(h.first_bad_rp - 1) +
                 "] = " + std::to_string(b));
+    }
+    if (h.first_bad_order != ~0ull) {
+        const int32_t o = read_back(order + h.first_bad_order, s);
+        invalid("row_order[" + std::to_string(h.first_bad_order) + "] = " + std::to_string(o) +
+                " is out of range [0, " + std::to_string(rows) + ")");
     }
 }
 
@@ -624,6 +654,7 @@ TG_API tg_status tg_add_self_loops_f32(int64_t N, int64_t nnz, const int32_t* ro
         require_device();
         if (N < 0 || nnz < 0) invalid("add_self_loops: negative size");
         if (nnz + N > INT32_MAX) invalid("add_self_loops: result does not fit int32 row_ptr");
+        check_csr_input(N, N, nnz, row_ptr, col_ind, as_stream(stream));
         const int64_t n = add_self_loops(N, 0, row_ptr, col_ind, values, row_ptr_out, col_ind_out, values_out,
                                          as_stream(stream));
         if (nnz_out) *nnz_out = n;
@@ -637,6 +668,7 @@ TG_API tg_status tg_gcn_norm_f32(int64_t N, int64_t nnz, const int32_t* row_ptr,
         require_device();
         if (N < 0 || nnz < 0) invalid("gcn_norm: negative size");
         if (nnz + N > INT32_MAX) invalid("gcn_norm: result does not fit int32 row_ptr");
+        check_csr_input(N, N, nnz, row_ptr, col_ind, as_stream(stream));
         const int64_t n = gcn_norm(N, row_ptr, col_ind, values, row_ptr_out, col_ind_out, values_out,
                                    as_stream(stream));
         if (nnz_out) *nnz_out = n;
@@ -651,6 +683,7 @@ TG_API tg_status tg_add_self_loops_rows_f32(int64_t rows, int64_t row_offset, in
         require_device();
         if (rows < 0 || row_offset < 0 || nnz < 0) invalid("add_self_loops: negative size");
         if (nnz + rows > INT32_MAX) invalid("add_self_loops: result does not fit int32 row_ptr");
+        check_csr_input(rows, -1, nnz, row_ptr, col_ind, as_stream(stream));  // columns only compared
         const int64_t n = add_self_loops(rows, row_offset, row_ptr, col_ind, values, row_ptr_out, col_ind_out,
                                          values_out, as_stream(stream));
         if (nnz_out) *nnz_out = n;
@@ -669,19 +702,22 @@ TG_API tg_status tg_gcn_norm_rows_degrees_f32(int64_t rows, int64_t row_offset, 
         check_ptr("gcn_norm", "row_ptr/insert_out/dis_out", row_ptr && insert_out && dis_out ? row_ptr : nullptr,
                   rows > 0);
         check_ptr("gcn_norm", "col_ind/values", col_ind && values ? col_ind : nullptr, nnz > 0);
+        check_csr_input(rows, -1, nnz, row_ptr, col_ind, as_stream(stream), row_order);  // columns only compared
         self_loop_rows(rows, row_offset, row_ptr, col_ind, values, row_order, row_ptr_out, insert_out, dis_out,
                        as_stream(stream));
     });
 }
 
-TG_API tg_status tg_gcn_norm_rows_fill_f32(int64_t rows, int64_t row_offset, const int32_t* row_ptr,
+TG_API tg_status tg_gcn_norm_rows_fill_f32(int64_t rows, int64_t row_offset, int64_t n_cols, const int32_t* row_ptr,
                                            const int32_t* col_ind, const float* values, const int32_t* row_order,
                                            const int32_t* row_ptr_out, const int32_t* insert, const float* dis_row,
                                            const float* dis_col, int32_t* col_ind_out, float* values_out,
                                            void* stream) {
     return guard([&] {
         require_device();
-        if (rows < 0 || row_offset < 0) invalid("gcn_norm: negative size");
+        if (rows < 0 || row_offset < 0 || n_cols < 0) invalid("gcn_norm: negative size");
+        if (row_offset + rows > n_cols) invalid("gcn_norm: rows [row_offset, row_offset + rows) exceed n_cols");
+        check_csr_input(rows, n_cols, -1, row_ptr, col_ind, as_stream(stream), row_order);
         check_ptr("gcn_norm", "row_ptr/row_ptr_out/insert/dis_row/dis_col/col_ind_out/values_out",
                   row_ptr && row_ptr_out && insert && dis_row && dis_col && col_ind_out && values_out ? row_ptr
                                                                                                       : nullptr,
@@ -696,6 +732,7 @@ TG_API tg_status tg_csr_degree_inv_sqrt_f32(int64_t rows, const int32_t* row_ptr
     return guard([&] {
         require_device();
         if (rows < 0) invalid("gcn_norm: negative size");
+        check_csr_input(rows, -1, -1, row_ptr, nullptr, as_stream(stream));
         if (rows) degree_inv_sqrt(rows, row_ptr, values, dis_out, as_stream(stream));
     });
 }
@@ -705,6 +742,7 @@ TG_API tg_status tg_csr_scale_sym_f32(int64_t rows, const int32_t* row_ptr, cons
     return guard([&] {
         require_device();
         if (rows < 0) invalid("gcn_norm: negative size");
+        check_csr_input(rows, -1, -1, row_ptr, col_ind, as_stream(stream));  // col_ind must index dis_col
         if (rows) scale_sym(rows, row_ptr, col_ind, values, dis_row, dis_col, as_stream(stream));
     });
 }
@@ -713,6 +751,7 @@ TG_API tg_status tg_csr_validate(int64_t rows, int64_t cols, int64_t nnz, const 
                                  const int32_t* col_ind, void* stream) {
     return guard([&] {
         require_device();
+        if (rows < 0 || cols < 0 || nnz < 0) invalid("Tensor::sparse_csr: negative size");
         csr_validate(rows, cols, nnz, row_ptr, col_ind, as_stream(stream));
     });
 }

@@ -88,11 +88,12 @@ TG_API tg_status tg_gcn_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
                                   const int32_t* row_order, int32_t mode, void* stream) {
     return guard([&] {
         require_device();
-        (void)nnz;
+        if (N < 0 || nnz < 0) invalid("GCNLayer::forward: negative size");
         if (F_in <= 0) invalid("GCNLayer: in_features must be > 0.");
         if (F_out <= 0) invalid("GCNLayer: out_features must be > 0.");
         check_ld("GCNLayer::forward", "H", ldh, F_in);
         check_ld("GCNLayer::forward", "out", ldo, F_out);
+        check_csr_input(N, N, nnz, row_ptr, col_ind, as_stream(stream), row_order);
         gcn_layer(N, row_ptr, col_ind, values, H, ldh, F_in, F_out, W, bias, act, out, ldo, row_order, mode,
                   as_stream(stream));
     });
@@ -104,11 +105,12 @@ TG_API tg_status tg_sage_layer_f32(int64_t N, int64_t nnz, const int32_t* row_pt
                                    float* out, int64_t ldo, const int32_t* row_order, int32_t mode, void* stream) {
     return guard([&] {
         require_device();
-        (void)nnz;
+        if (N < 0 || nnz < 0) invalid("SAGELayer::forward: negative size");
         if (F_in <= 0) invalid("SAGELayer: in_features must be > 0.");
         if (F_out <= 0) invalid("SAGELayer: out_features must be > 0.");
         check_ld("SAGELayer::forward", "H", ldh, F_in);
         check_ld("SAGELayer::forward", "out", ldo, F_out);
+        check_csr_input(N, N, nnz, row_ptr, col_ind, as_stream(stream), row_order);
         sage_layer(N, row_ptr, col_ind, H, ldh, F_in, F_out, W_neigh, W_self, bias, aggregator, act, out, ldo,
                    row_order, mode, as_stream(stream));
     });
@@ -127,6 +129,8 @@ TG_API tg_status tg_gat_layer_f32(int64_t N, int64_t nnz, const int32_t* row_ptr
         if (heads <= 0) invalid("GATLayer: heads must be > 0.");
         check_ld("GATLayer::forward", "H", ldh, F_in);
         check_ld("GATLayer::forward", "out", ldo, concat ? heads * F_out : F_out);
+        if (N < 0) invalid("GATLayer::forward: negative size");
+        check_csr_input(N, N, nnz, row_ptr, col_ind, as_stream(stream), row_order);
         gat_layer(N, nnz, row_ptr, col_ind, H, ldh, F_in, static_cast<int>(heads), static_cast<int>(F_out), W, a_left,
                   a_right, bias, negative_slope, concat != 0, act, TG_ACT_NONE, out, ldo, row_order, mode,
                   as_stream(stream));

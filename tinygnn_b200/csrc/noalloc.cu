@@ -30,25 +30,38 @@ void gemm_exact(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
 namespace {
 
 static __device__ __align__(256) float g_noalloc_scratch[TG_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+// The input CSR check's result words (the allocating entry points take them
+// from the pool).
+static __device__ __align__(256) unsigned long long g_noalloc_check[kCsrCheckWordsBytes / 8];
 
+struct Addresses {
+    float* scratch = nullptr;
+    void* check = nullptr;
+};
 std::mutex g_mu;
-std::vector<float*> g_addr;  // per device; nullptr = not looked up yet
+std::vector<Addresses> g_addr;  // per device; nullptr = not looked up yet
 
-// The scratch array's device address on the current device.
-float* scratch_address() {
+void* symbol_address(const void* sym) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, sym);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(TG_ERR_CUDA, std::string("gcn_layer (no-alloc): cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+    }
+    return p;
+}
+
+// The fixed arrays' device addresses on the current device.
+Addresses addresses() {
     int dev = 0;
     TG_CUDA(cudaGetDevice(&dev));
     std::lock_guard<std::mutex> lk(g_mu);
-    if (static_cast<int>(g_addr.size()) <= dev) g_addr.resize(dev + 1, nullptr);
-    if (!g_addr[dev]) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            fail(TG_ERR_CUDA, std::string("gcn_layer (no-alloc): cudaGetSymbolAddress failed: ") +
-                                  cudaGetErrorString(e));
-        }
-        g_addr[dev] = static_cast<float*>(p);
+    if (static_cast<int>(g_addr.size()) <= dev) g_addr.resize(dev + 1);
+    if (!g_addr[dev].scratch) {
+        Addresses a;
+        a.scratch = static_cast<float*>(symbol_address(g_noalloc_scratch));
+        a.check = symbol_address(g_noalloc_check);
+        g_addr[dev] = a;
     }
     return g_addr[dev];
 }
@@ -67,7 +80,7 @@ TG_API tg_status tg_gcn_layer_noalloc_f32(int64_t N, int64_t nnz, const int32_t*
                                           int64_t ldo, const int32_t* row_order, void* stream) {
     return guard([&] {
         require_device();
-        (void)nnz;
+        if (nnz < 0) invalid("GCNLayer::forward: negative nnz");
         if (F_in <= 0) invalid("GCNLayer: in_features must be > 0.");
         if (F_out <= 0) invalid("GCNLayer: out_features must be > 0.");
         if (N < 0) invalid("GCNLayer::forward: negative node count");
@@ -84,7 +97,9 @@ TG_API tg_status tg_gcn_layer_noalloc_f32(int64_t N, int64_t nnz, const int32_t*
                     "which allocates)");
         if (N == 0) return;
         const cudaStream_t s = as_stream(stream);
-        float* HW = scratch_address();
+        const Addresses fixed = addresses();
+        check_csr_input(N, N, nnz, row_ptr, col_ind, s, row_order, fixed.check);
+        float* HW = fixed.scratch;
         // Every element the gather reads is written by this GEMM first, so
         // nothing carried over from an earlier call needs clearing.
         gemm_exact(N, F_out, F_in, H, ldh, W, F_out, HW, ldw, nullptr, TG_ACT_NONE, 0.0f, s);

@@ -14,6 +14,7 @@ namespace tg {
 
 namespace {
 thread_local std::string g_last_error;
+thread_local bool g_csr_checks = true;
 std::atomic<uint64_t> g_launches{0};
 std::mutex g_dev_mu;
 std::vector<int> g_sms;           // per device, 0 = not queried yet
@@ -21,6 +22,8 @@ std::vector<char> g_pool_ready;   // per device
 }  // namespace
 
 void set_last_error(const std::string& m) { g_last_error = m; }
+
+bool csr_checks_enabled() { return g_csr_checks; }
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
@@ -104,7 +107,7 @@ TG_API const char* tg_last_error_message(void) { return tg::g_last_error.c_str()
 
 TG_API const char* tg_version(void) { return "tinygnn_b200 0.1.0 (sm_100a)"; }
 
-TG_API int32_t tg_abi_version(void) { return 1; }
+TG_API int32_t tg_abi_version(void) { return 2; }
 
 TG_API int32_t tg_device_count(void) {
     int n = 0;
@@ -117,6 +120,12 @@ TG_API int32_t tg_device_count(void) {
 
 TG_API uint64_t tg_kernel_launch_count(void) {
     return tg::g_launches.load(std::memory_order_relaxed);
+}
+
+TG_API int32_t tg_set_csr_checks(int32_t enabled) {
+    const int32_t prev = tg::g_csr_checks ? 1 : 0;
+    tg::g_csr_checks = enabled != 0;
+    return prev;
 }
 
 }  // extern "C"

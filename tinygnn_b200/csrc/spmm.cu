@@ -334,6 +334,7 @@ TG_API tg_status tg_spmm_f32(int64_t M, int64_t K, int64_t nnz, const int32_t* r
         check_ptr("spmm", "col_ind/values", col_ind && values ? col_ind : nullptr, nnz > 0);
         check_ptr("spmm", "B", B, nnz > 0 && F > 0);
         check_ptr("spmm", "C", C, M > 0 && F > 0);
+        check_csr_input(M, K, nnz, row_ptr, col_ind, as_stream(stream), row_order);
         GatherArgs a;
         a.M = M; a.rp = row_ptr; a.ci = col_ind; a.val = values; a.order = row_order;
         a.B = B; a.ldb = ldb; a.F = F; a.C = C; a.ldc = ldc;
@@ -349,11 +350,11 @@ TG_API tg_status tg_sage_mean_combine_f32(int64_t M, int64_t K, int64_t nnz, con
                                           int64_t ldo, const int32_t* row_order, int32_t mode, void* stream) {
     return guard([&] {
         require_device();
-        (void)K; (void)nnz;
         if (M < 0 || F < 0) invalid("sage_mean_combine: negative size");
         check_ld("sage_mean_combine", "Tn", ldn, F);
         check_ld("sage_mean_combine", "Ts", lds, F);
         check_ld("sage_mean_combine", "out", ldo, F);
+        check_csr_input(M, K, nnz, row_ptr, col_ind, as_stream(stream), row_order);
         GatherArgs a;
         a.M = M; a.rp = row_ptr; a.ci = col_ind; a.order = row_order;
         a.B = Tn; a.ldb = ldn; a.F = F; a.self = Ts; a.lds = lds;
@@ -370,6 +371,7 @@ TG_API tg_status tg_csr_column_splits(int64_t M, const int32_t* row_ptr, const i
         if (M < 0 || nblocks < 1 || width < 1) invalid("csr_column_splits: need M >= 0, nblocks >= 1, width >= 1");
         const int64_t total = M * (nblocks + 1);
         if (total == 0) return;
+        check_csr_input(M, -1, -1, row_ptr, col_ind, as_stream(stream));  // columns only compared
         launch("column_splits", column_splits_kernel, dim3(static_cast<unsigned>(ceil_div(total, 256))), dim3(256), 0,
                as_stream(stream), M, row_ptr, col_ind, static_cast<int>(nblocks), width, splits_out);
     });
@@ -382,11 +384,11 @@ TG_API tg_status tg_spmm_segment_f32(int64_t M, int64_t K, const int32_t* row_pt
                                      int32_t mode, void* stream) {
     return guard([&] {
         require_device();
-        (void)K;
         if (M < 0 || F < 0) invalid("spmm_segment: negative size");
         check_ld("spmm_segment", "B", ldb, F);
         check_ld("spmm_segment", "C", ldc, F);
         check_ptr("spmm_segment", "seg_begin/seg_end", seg_begin && seg_end ? seg_begin : nullptr, M > 0);
+        check_csr_input(M, K, -1, row_ptr, col_ind, as_stream(stream), row_order);
         GatherArgs a;
         a.M = M; a.rp = row_ptr; a.ci = col_ind; a.val = values; a.order = row_order;
         a.B = B; a.ldb = ldb; a.F = F; a.C = C; a.ldc = ldc;
@@ -405,11 +407,11 @@ TG_API tg_status tg_sage_mean_combine_segment_f32(int64_t M, int64_t K, const in
                                                   int32_t last, int32_t mode, void* stream) {
     return guard([&] {
         require_device();
-        (void)K;
         if (M < 0 || F < 0) invalid("sage_mean_combine_segment: negative size");
         check_ld("sage_mean_combine_segment", "Tn", ldn, F);
         check_ld("sage_mean_combine_segment", "Ts", lds, F);
         check_ld("sage_mean_combine_segment", "out", ldo, F);
+        check_csr_input(M, K, -1, row_ptr, col_ind, as_stream(stream), row_order);
         GatherArgs a;
         a.M = M; a.rp = row_ptr; a.ci = col_ind; a.order = row_order;
         a.B = Tn; a.ldb = ldn; a.F = F; a.self = Ts; a.lds = lds;
@@ -436,9 +438,10 @@ TG_API tg_status tg_sage_aggregate_f32(int64_t M, int64_t K, int64_t nnz,
                                        int64_t ldo, int32_t aggregator, void* stream) {
     return guard([&] {
         require_device();
-        (void)K; (void)nnz;
+        if (M < 0 || F < 0) invalid("sage_aggregate: negative size");
         check_ld("sage_aggregate", "H", ldh, F);
         check_ld("sage_aggregate", "out", ldo, F);
+        check_csr_input(M, K, nnz, row_ptr, col_ind, as_stream(stream));
         GatherArgs a;
         a.M = M; a.rp = row_ptr; a.ci = col_ind; a.B = H; a.ldb = ldh; a.F = F;
         a.C = out; a.ldc = ldo;
@@ -459,9 +462,10 @@ TG_API tg_status tg_sage_max_aggregate_f32(int64_t M, int64_t K, int64_t nnz,
                                            int64_t ldo, void* stream) {
     return guard([&] {
         require_device();
-        (void)K; (void)nnz;
+        if (M < 0 || F < 0) invalid("sage_max_aggregate: negative size");
         check_ld("sage_max_aggregate", "H", ldh, F);
         check_ld("sage_max_aggregate", "out", ldo, F);
+        check_csr_input(M, K, nnz, row_ptr, col_ind, as_stream(stream));
         GatherArgs a;
         a.M = M; a.rp = row_ptr; a.ci = col_ind; a.B = H; a.ldb = ldh; a.F = F;
         a.C = out; a.ldc = ldo; a.op = GATHER_MAX;

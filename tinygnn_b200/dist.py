@@ -193,7 +193,7 @@ def gcn_norm_rows_scheduled(A: CSR, row0: int, R: int, comm: Comm, dis_all: Opti
     both normalisation passes run in it, and the normalised block keeps it
     for the gathers (same arithmetic; the order changes speed only)."""
     if A.order is None:
-        A = CSR(A.n_rows, A.n_cols, A.row_ptr, A.col_ind, A.values, ops.degree_order(A))
+        A = CSR(A.n_rows, A.n_cols, A.row_ptr, A.col_ind, A.values, ops.degree_order(A), A.validated)
     return gcn_norm_rows(A, row0, R, comm, dis_all)
 
 
@@ -538,7 +538,8 @@ class ShardedModel:
         step = max(1, -(-self.rows // chunks))  # a rank may own no rows
         for a in range(0, self.rows, step):
             b = min(self.rows, a + step)
-            Ak = CSR(b - a, A.n_cols, A.row_ptr[a:b + 1], A.col_ind, A.values)
+            # rows [a, b) of a checked CSR (its row_ptr slice indexes the same arrays)
+            Ak = CSR(b - a, A.n_cols, A.row_ptr[a:b + 1], A.col_ind, A.values, validated=A.validated)
             Ak.order = ops.degree_order(Ak)
             out = self.outs[li][a:b]
             if L.kind == "gcn":

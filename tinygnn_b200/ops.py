@@ -68,6 +68,10 @@ class CSR:
     # Optional row schedule (int32 permutation, longest rows first) reused by
     # every gather over this matrix; without it large gathers compute one.
     order: Optional[torch.Tensor] = None
+    # The library checks every CSR it is given (Tensor::sparse_csr's checks,
+    # on the device) before reading through it; a CSR that passed once, or
+    # that the library built, is marked and not checked again.
+    validated: bool = False
 
     @property
     def nnz(self) -> int:
@@ -91,6 +95,23 @@ class CSR:
 
     def numpy(self):
         return (self.row_ptr.cpu().numpy(), self.col_ind.cpu().numpy(), self.values.cpu().numpy())
+
+
+def _csr_call(csrs, fn, *args) -> None:
+    """Call a C-ABI entry point that reads the CSRs ``csrs``.  The library
+    checks a caller's CSR on every call unless the thread turns the checks
+    off (tg_set_csr_checks); here they run once per CSR object: calls on CSRs
+    already checked (or built by the library) turn them off around the call."""
+    trusted = all(c.validated for c in csrs)
+    prev = lib.tg_set_csr_checks(0) if trusted else None
+    try:
+        check(fn(*args))
+    finally:
+        if prev is not None:
+            lib.tg_set_csr_checks(prev)
+    if not trusted:
+        for c in csrs:
+            c.validated = True
 
 
 # ── dense ops ────────────────────────────────────────────────────────────────
@@ -207,16 +228,16 @@ def spmm(A: CSR, B: torch.Tensor, bias=None, act=None, alpha: float = 0.0, row_o
         out = torch.empty((A.n_rows, F), dtype=torch.float32, device=B.device)
     b = _vec(bias)
     flags = MODE[mode] | (FLAG_B_ROWS_PADDED if _padded(B) else 0)
-    check(lib.tg_spmm_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(B), F,
+    _csr_call((A,), lib.tg_spmm_f32, A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(B), F,
                           _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha, _p(_ord(A, row_order)), flags,
-                          _stream()))
+                          _stream())
     return out
 
 
 def column_splits(A: CSR, nblocks: int, width: int) -> torch.Tensor:
     """(nblocks+1) x n_rows split points of sorted rows at column multiples of `width`."""
     out = torch.empty((nblocks + 1, A.n_rows), dtype=torch.int32, device=A.row_ptr.device)
-    check(lib.tg_csr_column_splits(A.n_rows, _p(A.row_ptr), _p(A.col_ind), nblocks, width, _p(out), _stream()))
+    _csr_call((A,), lib.tg_csr_column_splits, A.n_rows, _p(A.row_ptr), _p(A.col_ind), nblocks, width, _p(out), _stream())
     return out
 
 
@@ -226,9 +247,9 @@ def spmm_segment(A: CSR, B: torch.Tensor, seg_begin: torch.Tensor, seg_end: torc
     B = _dense(B, "B")
     b = _vec(bias)
     flags = FLAG_B_ROWS_PADDED if _padded(B) else 0
-    check(lib.tg_spmm_segment_f32(A.n_rows, A.n_cols, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(seg_begin),
+    _csr_call((A,), lib.tg_spmm_segment_f32, A.n_rows, A.n_cols, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(seg_begin),
                                   _p(seg_end), _p(B), B.shape[1], _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha,
-                                  _p(_ord(A, row_order)), int(carry), int(last), flags, _stream()))
+                                  _p(_ord(A, row_order)), int(carry), int(last), flags, _stream())
     return out
 
 
@@ -238,10 +259,10 @@ def sage_mean_combine_segment(A: CSR, Tn: torch.Tensor, Ts: torch.Tensor, seg_be
     Tn, Ts = _dense(Tn, "Tn"), _dense(Ts, "Ts")
     b = _vec(bias)
     flags = FLAG_B_ROWS_PADDED if _padded(Tn) else 0
-    check(lib.tg_sage_mean_combine_segment_f32(A.n_rows, A.n_cols, _p(A.row_ptr), _p(A.col_ind), _p(seg_begin),
+    _csr_call((A,), lib.tg_sage_mean_combine_segment_f32, A.n_rows, A.n_cols, _p(A.row_ptr), _p(A.col_ind), _p(seg_begin),
                                                _p(seg_end), _p(Tn), Tn.shape[1], _ld(Tn), _p(Ts), _ld(Ts), _p(b),
                                                ACT[act], _p(out), _ld(out), _p(_ord(A, row_order)), int(carry),
-                                               int(last), flags, _stream()))
+                                               int(last), flags, _stream())
     return out
 
 
@@ -254,9 +275,9 @@ def sage_mean_combine(A: CSR, Tn: torch.Tensor, Ts: torch.Tensor, bias=None, act
         out = torch.empty((A.n_rows, F), dtype=torch.float32, device=Tn.device)
     b = _vec(bias)
     flags = FLAG_B_ROWS_PADDED if _padded(Tn) else 0
-    check(lib.tg_sage_mean_combine_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(Tn), F,
+    _csr_call((A,), lib.tg_sage_mean_combine_f32, A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(Tn), F,
                                        _ld(Tn), _p(Ts), _ld(Ts), _p(b), ACT[act], _p(out), _ld(out),
-                                       _p(_ord(A, row_order)), flags, _stream()))
+                                       _p(_ord(A, row_order)), flags, _stream())
     return out
 
 
@@ -270,9 +291,9 @@ def degree_order(A: CSR) -> torch.Tensor:
 def sage_aggregate(A: CSR, H: torch.Tensor, aggregator: str = "mean") -> torch.Tensor:
     H = _dense(H, "H")
     out = torch.empty((A.n_rows, H.shape[1]), dtype=torch.float32, device=H.device)
-    check(lib.tg_sage_aggregate_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(H), H.shape[1],
+    _csr_call((A,), lib.tg_sage_aggregate_f32, A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(H), H.shape[1],
                                     _ld(H), _p(out), _ld(out), _lib.AGG_MAX if aggregator == "max" else
-                                    _lib.AGG_MEAN, _stream()))
+                                    _lib.AGG_MEAN, _stream())
     return out
 
 
@@ -283,16 +304,16 @@ def sage_max_aggregate(A: CSR, H: torch.Tensor) -> torch.Tensor:
         raise _lib.InvalidArgument(_lib.INVALID_ARGUMENT,
                                    f"sage_max_aggregate: A.cols() ({A.n_cols}) != H.rows() ({H.shape[0]}).")
     out = torch.empty((A.n_rows, H.shape[1]), dtype=torch.float32, device=H.device)
-    check(lib.tg_sage_max_aggregate_f32(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(H),
-                                        H.shape[1], _ld(H), _p(out), _ld(out), _stream()))
+    _csr_call((A,), lib.tg_sage_max_aggregate_f32, A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(H),
+                                        H.shape[1], _ld(H), _p(out), _ld(out), _stream())
     return out
 
 
 def edge_softmax(A: CSR) -> CSR:
     """edge_softmax (src/layers.cpp:768): same structure, row-softmaxed values."""
     v = torch.zeros_like(A.values)
-    check(lib.tg_edge_softmax_f32(A.n_rows, A.nnz, _p(A.row_ptr), _p(A.values), _p(v), _stream()))
-    return CSR(A.n_rows, A.n_cols, A.row_ptr.clone(), A.col_ind.clone(), v)
+    _csr_call((A,), lib.tg_edge_softmax_f32, A.n_rows, A.nnz, _p(A.row_ptr), _p(A.values), _p(v), _stream())
+    return CSR(A.n_rows, A.n_cols, A.row_ptr.clone(), A.col_ind.clone(), v, validated=True)
 
 
 # ── graph construction ───────────────────────────────────────────────────────
@@ -306,7 +327,7 @@ def edge_list_to_csr(src: torch.Tensor, dst: torch.Tensor, num_nodes: int) -> CS
     ci = torch.empty(max(E, 1), dtype=torch.int32, device=dev)
     v = torch.empty(max(E, 1), dtype=torch.float32, device=dev)
     check(lib.tg_edge_list_to_csr(num_nodes, E, _p(src), _p(dst), _p(rp), _p(ci), _p(v), _stream()))
-    return CSR(num_nodes, num_nodes, rp, ci[:E], v[:E])
+    return CSR(num_nodes, num_nodes, rp, ci[:E], v[:E], validated=True)
 
 
 def _csr_expand(fn, A: CSR) -> CSR:
@@ -321,9 +342,9 @@ def _csr_expand(fn, A: CSR) -> CSR:
     ci = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
     v = torch.empty(max(cap, 1), dtype=torch.float32, device=dev)
     nnz = C.c_int64(0)
-    check(fn(N, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(rp), _p(ci), _p(v), C.byref(nnz),
-             _stream()))
-    return CSR(N, N, rp, ci[:nnz.value], v[:nnz.value])
+    _csr_call((A,), fn, N, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(rp), _p(ci), _p(v), C.byref(nnz),
+              _stream())
+    return CSR(N, N, rp, ci[:nnz.value], v[:nnz.value], validated=True)
 
 
 def add_self_loops(A: CSR) -> CSR:
@@ -345,23 +366,23 @@ def add_self_loops_rows(A: CSR, row_offset: int) -> CSR:
     ci = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
     v = torch.empty(max(cap, 1), dtype=torch.float32, device=dev)
     nnz = C.c_int64(0)
-    check(lib.tg_add_self_loops_rows_f32(N, row_offset, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(rp),
-                                         _p(ci), _p(v), C.byref(nnz), _stream()))
-    return CSR(N, A.n_cols, rp, ci[:nnz.value], v[:nnz.value])
+    _csr_call((A,), lib.tg_add_self_loops_rows_f32, N, row_offset, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(rp),
+                                         _p(ci), _p(v), C.byref(nnz), _stream())
+    return CSR(N, A.n_cols, rp, ci[:nnz.value], v[:nnz.value], validated=True)
 
 
 def degree_inv_sqrt(A: CSR, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """dis[i] = 1/sqrtf(sum of row i's values) (0 for non-positive sums)."""
     if out is None:
         out = torch.empty(A.n_rows, dtype=torch.float32, device=A.row_ptr.device)
-    check(lib.tg_csr_degree_inv_sqrt_f32(A.n_rows, _p(A.row_ptr), _p(A.values), _p(out), _stream()))
+    _csr_call((A,), lib.tg_csr_degree_inv_sqrt_f32, A.n_rows, _p(A.row_ptr), _p(A.values), _p(out), _stream())
     return out
 
 
 def scale_sym_(A: CSR, dis_row: torch.Tensor, dis_col: torch.Tensor) -> CSR:
     """values = (values * dis_row[i]) * dis_col[j], in place."""
-    check(lib.tg_csr_scale_sym_f32(A.n_rows, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(dis_row),
-                                   _p(dis_col), _stream()))
+    _csr_call((A,), lib.tg_csr_scale_sym_f32, A.n_rows, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(dis_row),
+                                   _p(dis_col), _stream())
     return A
 
 
@@ -373,8 +394,8 @@ def gcn_norm_rows_degrees(A: CSR, row_offset: int, dis_out: torch.Tensor, row_or
     dev = A.row_ptr.device
     rp = torch.empty(N + 1, dtype=torch.int32, device=dev)
     ins = torch.empty(max(N, 1), dtype=torch.int32, device=dev)
-    check(lib.tg_gcn_norm_rows_degrees_f32(N, row_offset, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values),
-                                           _p(_ord(A, row_order)), _p(rp), _p(ins), _p(dis_out), _stream()))
+    _csr_call((A,), lib.tg_gcn_norm_rows_degrees_f32, N, row_offset, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values),
+                                           _p(_ord(A, row_order)), _p(rp), _p(ins), _p(dis_out), _stream())
     return rp, ins
 
 
@@ -390,10 +411,10 @@ def gcn_norm_rows_fill(A: CSR, row_offset: int, rp_out: torch.Tensor, insert: to
     order = _ord(A, row_order)
     ci = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
     v = torch.empty(max(cap, 1), dtype=torch.float32, device=dev)
-    check(lib.tg_gcn_norm_rows_fill_f32(N, row_offset, _p(A.row_ptr), _p(A.col_ind), _p(A.values), _p(order),
-                                        _p(rp_out), _p(insert), _p(dis_row), _p(dis_col), _p(ci), _p(v), _stream()))
+    _csr_call((A,), lib.tg_gcn_norm_rows_fill_f32, N, row_offset, dis_col.numel(), _p(A.row_ptr), _p(A.col_ind),
+              _p(A.values), _p(order), _p(rp_out), _p(insert), _p(dis_row), _p(dis_col), _p(ci), _p(v), _stream())
     nnz = int(rp_out[N].item()) if N else 0  # after both passes are queued
-    return CSR(N, A.n_cols, rp_out, ci[:nnz], v[:nnz], order)
+    return CSR(N, A.n_cols, rp_out, ci[:nnz], v[:nnz], order, validated=True)
 
 
 def csr_validate(A: CSR) -> None:
@@ -410,9 +431,9 @@ def gcn_layer(A_norm: CSR, H: torch.Tensor, W: torch.Tensor, bias=None, act="rel
     if out is None:
         out = torch.empty((N, F_out), dtype=torch.float32, device=H.device)
     b = _vec(bias)
-    check(lib.tg_gcn_layer_f32(N, A_norm.nnz, _p(A_norm.row_ptr), _p(A_norm.col_ind), _p(A_norm.values), _p(H),
+    _csr_call((A_norm,), lib.tg_gcn_layer_f32, N, A_norm.nnz, _p(A_norm.row_ptr), _p(A_norm.col_ind), _p(A_norm.values), _p(H),
                                _ld(H), W.shape[0], F_out, _p(W), _p(b), ACT[act], _p(out), _ld(out),
-                               _p(_ord(A_norm, row_order)), MODE[mode], _stream()))
+                               _p(_ord(A_norm, row_order)), MODE[mode], _stream())
     return out
 
 
@@ -425,9 +446,9 @@ def sage_layer(A: CSR, H: torch.Tensor, W_neigh: torch.Tensor, W_self: torch.Ten
     if out is None:
         out = torch.empty((N, F_out), dtype=torch.float32, device=H.device)
     b = _vec(bias)
-    check(lib.tg_sage_layer_f32(N, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(H), _ld(H), Wn.shape[0], F_out,
+    _csr_call((A,), lib.tg_sage_layer_f32, N, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(H), _ld(H), Wn.shape[0], F_out,
                                 _p(Wn), _p(Ws), _p(b), _lib.AGG_MAX if aggregator == "max" else _lib.AGG_MEAN,
-                                ACT[act], _p(out), _ld(out), _p(_ord(A, row_order)), MODE[mode], _stream()))
+                                ACT[act], _p(out), _ld(out), _p(_ord(A, row_order)), MODE[mode], _stream())
     return out
 
 
@@ -445,9 +466,9 @@ def gat_layer(A_sl: CSR, H: torch.Tensor, W: torch.Tensor, a_left: torch.Tensor,
     N = A_sl.n_rows
     if out is None:
         out = torch.empty((N, heads * F_out if concat else F_out), dtype=torch.float32, device=H.device)
-    check(lib.tg_gat_layer_f32(N, A_sl.nnz, _p(A_sl.row_ptr), _p(A_sl.col_ind), _p(H), _ld(H), W.shape[0], heads,
+    _csr_call((A_sl,), lib.tg_gat_layer_f32, N, A_sl.nnz, _p(A_sl.row_ptr), _p(A_sl.col_ind), _p(H), _ld(H), W.shape[0], heads,
                                F_out, _p(W), _p(al), _p(ar), _p(b), negative_slope, int(concat), ACT[act],
-                               _p(out), _ld(out), _p(_ord(A_sl, row_order)), MODE[mode], _stream()))
+                               _p(out), _ld(out), _p(_ord(A_sl, row_order)), MODE[mode], _stream())
     return out
 
 
