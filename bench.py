@@ -454,7 +454,7 @@ def run_ours(args):
 
     import tinygnn_b200 as tg
     from tinygnn_b200 import synth
-    from tinygnn_b200.dist import Comm, ShardedModel, gcn_norm_rows, gcn_norm_rows_scheduled, row_block, slice_rows
+    from tinygnn_b200.dist import Comm, ShardedModel, row_block, slice_rows
     from tinygnn_b200.ops import CSR
 
     comm = Comm(world, rank, group)
@@ -472,13 +472,15 @@ def run_ours(args):
     Xp = torch.zeros((rows, (FEATS + 3) // 4 * 4), dtype=torch.float32, device=dev)
     Xp[:, :FEATS] = synth.normal_rows(r0, rows, FEATS, FEAT_SEED, 0, dev)
     X = Xp[:, :FEATS]
-    A_gcn = gcn_norm_rows(A_raw, r0, R, comm) if args.workload == "gcn" else None
-    # A normalised graph kept from one call to the next, with its
-    # longest-rows-first schedule: only the layers-only figure uses it.
-    A_cached = A_gcn if A_gcn is not None else CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind,
-                                                   A_raw.values, validated=A_raw.validated)
-    A_cached.with_degree_order()
-    nnz_local = A_gcn.nnz if A_gcn is not None else A_raw.nnz
+    # edges of the normalised adjacency (GCN: A + I) this rank aggregates
+    nnz_local = A_raw.nnz
+    if args.workload == "gcn":
+        lens = (A_raw.row_ptr[1:] - A_raw.row_ptr[:-1]).long()
+        rows_of = torch.repeat_interleave(torch.arange(rows, device=dev), lens)
+        has_diag = torch.zeros(rows, dtype=torch.bool, device=dev)
+        has_diag[rows_of[A_raw.col_ind.long() == rows_of + r0]] = True
+        nnz_local += int(rows - int(has_diag.sum()))
+        del lens, rows_of, has_diag
     nnz_total = nnz_local
     if world > 1:
         import torch.distributed as dist
@@ -503,21 +505,19 @@ def run_ours(args):
 
     def step():
         # What Model::forward does every call (src/model.cpp:359-439): the raw
-        # adjacency is normalised (gcn_norm) and scheduled afresh, then the
-        # layers and log_softmax run.  Nothing derived from the graph is kept
-        # between steps.
-        if args.workload == "gcn":
-            An = gcn_norm_rows_scheduled(A_raw, r0, R, comm, dis_buf)  # keeps the raw rows' schedule
-            model.forward(An, None, X)
-        else:
-            Ar = CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind, A_raw.values,
-                     validated=A_raw.validated)
-            Ar.with_degree_order()
-            model.forward(None, Ar, X)
+        # adjacency is normalised (gcn_norm; in FAST mode as per-row scale
+        # factors folded into the GEMM and gather epilogues) and scheduled
+        # afresh, then the layers and log_softmax run.  Nothing derived from
+        # the graph is kept between steps.
+        Ar = CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind, A_raw.values, validated=A_raw.validated)
+        model.forward_model(Ar, X, dis_all=dis_buf)
+
+    prepared = model.prepare(CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind, A_raw.values,
+                                 validated=A_raw.validated), dis_buf)
 
     def layers_step():
         # the layers alone on a graph normalised and scheduled once
-        model.forward(A_gcn, A_cached if A_gcn is None else None, X)
+        model.forward_prepared(prepared, X)
 
     sampler = ClockSampler(local)
     sampler.start()
@@ -563,7 +563,7 @@ def run_ours(args):
     d2h = h_out.numel() * 4
 
     # parity spot check of the e2e logits against the device-resident run
-    ref_out = model.forward(A_gcn, A_cached if A_gcn is None else None, X)
+    ref_out = model.forward_prepared(prepared, X)
     torch.cuda.synchronize()
     e2e_matches = None if args.no_e2e else bool(torch.equal(ref_out.cpu(), h_out))
 

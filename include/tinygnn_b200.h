@@ -117,6 +117,15 @@ TG_API tg_status tg_gemm_f32(int64_t M, int64_t N, int64_t K, const float* A, in
                              const float* bias, int32_t act, float alpha, int32_t mode,
                              void* stream);
 
+/* C = act(diag(row_scale) . (A . B) + bias): tg_gemm_f32 with row i of the
+ * product multiplied by row_scale[i] (one rounding) before the bias.  No
+ * counterpart in the reference; it carries gcn_norm's column scaling in the
+ * FAST GCN forward (tg_gcn_aggregate_f32). */
+TG_API tg_status tg_gemm_rowscale_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+                                      const float* B, int64_t ldb, float* C, int64_t ldc,
+                                      const float* row_scale, const float* bias, int32_t act,
+                                      float alpha, int32_t mode, void* stream);
+
 /* C = A1 . B1 and A2 . B2 interleaved per k (the fused dual GEMV of
  * SAGELayer::forward, src/layers.cpp:639-669): for k = 0..K-1,
  * acc = fma(A1[i][k], B1[k][j], acc); acc = fma(A2[i][k], B2[k][j], acc).
@@ -308,6 +317,37 @@ TG_API tg_status tg_gcn_norm_rows_fill_f32(int64_t rows, int64_t row_offset, int
 TG_API tg_status tg_csr_validate(int64_t rows, int64_t cols, int64_t nnz,
                                  const int32_t* row_ptr, const int32_t* col_ind, void* stream);
 
+/* The FAST GCN forward without a normalised copy of A.  gcn_norm's
+ * D^-1/2 (A + I) D^-1/2 (src/layers.cpp:158-208) applied to HW factors as
+ *   out_i = dis_i * (sum_j a_ij Hs_j + Hs_i),   Hs = diag(dis) . HW,
+ * with d_i = (sum of row i's values) + 1 -- A + I's row sum whether or not
+ * row i holds its diagonal (that entry becomes a_ii + 1) -- and dis_i =
+ * 1/sqrtf(d_i) (0 when d_i <= 0).  Equal to the normalised path in exact
+ * arithmetic; the roundings differ, within the fp32 tolerance
+ * |d| <= 1e-5 + 1e-4 |ref| (degrees of integer-valued rows are exact).
+ * The scale of a row needs only its own row, so row-partitioned callers
+ * exchange Hs and need no exchange of dis.  No counterpart in the reference.
+ *
+ * tg_gcn_norm_scale_f32: dis_out[rows] for a block of raw rows (values read
+ *   in any order; nnz = row_ptr[rows] - row_ptr[0] entries).
+ * tg_gcn_aggregate_f32: out_i = act(dis[i] * (sum_j a_ij Hs[j] + Hs_self[i])
+ *   + bias) for the M rows of a block (global columns < K; Hs K x F, ld
+ *   ldh; Hs_self / dis this block's rows), the sum one fused multiply-add
+ *   chain in stored order.  seg_begin / seg_end (nullable) restrict each row
+ *   to entries [seg_begin[i], seg_end[i]) for column-block passes as in
+ *   tg_spmm_segment_f32: the chain is carried through `out` (carry != 0)
+ *   and the epilogue runs on the pass with last != 0.  mode: the
+ *   TG_FLAG_B_ROWS_PADDED bit. */
+TG_API tg_status tg_gcn_norm_scale_f32(int64_t rows, int64_t nnz, const int32_t* row_ptr,
+                                       const float* values, float* dis_out, void* stream);
+TG_API tg_status tg_gcn_aggregate_f32(int64_t M, int64_t K, int64_t nnz, const int32_t* row_ptr,
+                                      const int32_t* col_ind, const float* values, const float* Hs,
+                                      int64_t F, int64_t ldh, const float* Hs_self, int64_t lds,
+                                      const float* dis, const float* bias, int32_t act, float* out,
+                                      int64_t ldo, const int32_t* row_order, const int32_t* seg_begin,
+                                      const int32_t* seg_end, int32_t carry, int32_t last,
+                                      int32_t mode, void* stream);
+
 /* ── layers ──────────────────────────────────────────────────────────────── */
 
 /* GCNLayer::forward (src/layers.cpp:286-339): out = act(A_norm . (H . W) + b)
@@ -382,7 +422,8 @@ TG_API tg_status tg_ipc_get_handle(const void* ptr, void* handle_out, int64_t* o
 TG_API tg_status tg_ipc_open_handle(const void* handle, void** base_out);
 TG_API tg_status tg_ipc_close_handle(void* base);
 
-/* C = act(A . B + bias) on the tensor cores (FAST mode arithmetic), with
+/* C = act(A . B + bias) on the tensor cores (FAST mode arithmetic; rows
+ * scaled by row_scale[i] before the bias when it is not NULL), with
  * every stored row also written at the same offset of peer_C[p] (another
  * GPU's copy of C's buffer, same ldc), for p < npeers (<= TG_MAX_PEERS); once
  * a 128-row tile has landed in every copy, *peer_flags[p] += 1 (a 64-bit
@@ -394,7 +435,8 @@ TG_API tg_status tg_ipc_close_handle(void* base);
 #define TG_FLAG_C_COLS_PADDED 0x200
 TG_API tg_status tg_gemm_peers_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                                    const float* B, int64_t ldb, float* C, int64_t ldc,
-                                   const float* bias, int32_t act, float alpha, int32_t npeers,
+                                   const float* bias, int32_t act, float alpha,
+                                   const float* row_scale, int32_t npeers,
                                    float* const* peer_C, uint64_t* const* peer_flags, int32_t flags,
                                    void* stream);
 

@@ -145,8 +145,8 @@ def test_forward_from_host_equals_resident_forward(tg, workload, mode, blocks, u
     A = tg.CSR.from_numpy(rp, ci, v)
     Xd = torch.zeros((n, (fin + 3) // 4 * 4), device="cuda")[:, :fin]
     Xd[:] = torch.as_tensor(X[:, :fin]).cuda()
-    An = gcn_norm_rows(A, 0, n, Comm(1, 0)) if not sage else None
-    ref = model.forward(An, A, Xd).cpu().numpy().copy()
+    # the resident Model::forward (EXACT: normalised copy; FAST: factored)
+    ref = model.forward_model(A, Xd).cpu().numpy().copy()
     pin = lambda t: t.cpu().pin_memory()  # noqa: E731
     h_out = torch.empty((n, 11)).pin_memory()
     bufs = {}
@@ -220,3 +220,75 @@ def test_sharded_forward_equals_unpartitioned(tg, workload, world):
     w = {k: t.cpu().numpy() for k, t in w.items()}
     oref = P.activation("log_softmax", oracle.model_forward(P, spec, w, rp, ci, v, X))
     assert_close(ref.cpu().numpy(), oref, f"{kind} vs oracle")
+
+
+@pytest.mark.parametrize("world,weighted", [(1, False), (1, True), (2, False), (3, True), (8, False)])
+def test_fast_factored_gcn_forward(tg, world, weighted):
+    """FAST GCN without a normalised copy of A (per-row 1/sqrt(deg) folded
+    into the GEMM and gather epilogues): emulated ranks equal one rank bit
+    for bit (every factor is rank-local), and the logits are within the fp32
+    tolerance of the oracle's Model::forward (gcn_norm, layers, log_softmax)."""
+    from tinygnn_b200.dist import Layer, ShardedModel, row_block, slice_rows
+    rng, rp, ci, v, X = _graph(seed=20 + world)
+    if weighted:
+        v = (rng.random(ci.size) + 0.25).astype(np.float32)
+    n = rp.size - 1
+    W0 = torch.as_tensor((rng.standard_normal((40, 32)) * 0.2).astype(np.float32)).cuda()
+    W1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
+    b0 = torch.as_tensor((rng.standard_normal(32) * 0.1).astype(np.float32)).cuda()
+    b1 = torch.as_tensor((rng.standard_normal(11) * 0.1).astype(np.float32)).cuda()
+    layers = [Layer("gcn", W0, b0, "relu"), Layer("gcn", W1, b1, None)]
+    A = tg.CSR.from_numpy(rp, ci, v)
+    Xd = torch.as_tensor(X).cuda()
+    one = ShardedModel(layers, n, LocalComm(1, 0), "cuda", mode="fast")
+    ref = one.forward_model(A, Xd).clone()
+
+    R = (n + world - 1) // world
+    shards, preps, H = [], [], []
+    for r in range(world):
+        _, r0, r1 = row_block(n, world, r)
+        sh = ShardedModel(layers, n, LocalComm(world, r), "cuda", mode="fast")
+        shards.append(sh)
+        preps.append(sh.prepare(slice_rows(A.row_ptr, A.col_ind, A.values, r0, r1, n)))
+        H.append(Xd[r0:r1])
+    for li in range(2):
+        for r, sh in enumerate(shards):
+            sh.scale = preps[r][2]
+            sh.transform(li, H[r])
+        for r, sh in enumerate(shards):  # emulated all-gather
+            for q, src in enumerate(shards):
+                if q != r:
+                    sh.full[li][q * R:(q + 1) * R] = src.full[li][q * R:(q + 1) * R]
+        H = []
+        for r, sh in enumerate(shards):
+            sh.scale = preps[r][2]
+            H.append(sh.aggregate(li, preps[r][0], preps[r][1]))
+            sh.scale = None
+    got = torch.cat([tg.log_softmax_(h) for h in H], 0)
+    torch.cuda.synchronize()
+    assert_bits_equal(got.cpu().numpy(), ref.cpu().numpy(), f"fast gcn x{world} vs one rank")
+    spec = [dict(type="gcn", **{"in": 40, "out": 32}, act="relu"), dict(type="gcn", **{"in": 32, "out": 11})]
+    w = {"layer0.weight": W0, "layer0.bias": b0, "layer1.weight": W1, "layer1.bias": b1}
+    w = {k: t.cpu().numpy() for k, t in w.items()}
+    oref = P.activation("log_softmax", oracle.model_forward(P, spec, w, rp, ci, v, X))
+    assert_close(ref.cpu().numpy(), oref, f"fast factored gcn weighted={weighted} vs oracle")
+
+
+def test_gcn_norm_scale_matches_gcn_norm_degrees(tg):
+    """1/sqrt(row sum + 1) of the raw rows is gcn_norm's 1/sqrt(deg) of A + I:
+    bit for bit on integer-valued rows (with and without diagonals), within
+    the tolerance on fractional ones."""
+    rng = np.random.default_rng(5)
+    n = 30000
+    rp, ci, v = powerlaw_csr(rng, n, 14, weighted=False, diag=True)  # some rows hold their diagonal
+    for kind in ("unit", "integer", "fractional"):
+        vv = {"unit": np.ones_like(v), "integer": rng.integers(1, 5, v.size).astype(np.float32),
+              "fractional": (rng.random(v.size) + 0.1).astype(np.float32)}[kind]
+        A = tg.CSR.from_numpy(rp, ci, vv)
+        exact = torch.empty(n, device="cuda")
+        tg.ops.gcn_norm_rows_degrees(A, 0, exact)
+        fast = tg.ops.gcn_norm_scale(A)
+        if kind == "fractional":
+            assert_close(fast.cpu().numpy(), exact.cpu().numpy(), kind)
+        else:
+            assert_bits_equal(fast.cpu().numpy(), exact.cpu().numpy(), kind)

@@ -34,6 +34,10 @@ SIGNATURES = {
     "tg_device_count": (i32, []),
     "tg_kernel_launch_count": (u64, []),
     "tg_gemm_f32": (i32, [i64, i64, i64, vp, i64, vp, i64, vp, i64, vp, i32, f32, i32, vp]),
+    "tg_gemm_rowscale_f32": (i32, [i64, i64, i64, vp, i64, vp, i64, vp, i64, vp, vp, i32, f32, i32, vp]),
+    "tg_gcn_norm_scale_f32": (i32, [i64, i64, vp, vp, vp, vp]),
+    "tg_gcn_aggregate_f32": (i32, [i64, i64, i64, vp, vp, vp, vp, i64, i64, vp, i64, vp, vp, i32, vp, i64, vp, vp, vp,
+                                   i32, i32, i32, vp]),
     "tg_gemm_dual_f32": (i32, [i64, i64, i64, vp, i64, vp, i64, vp, vp, i64, vp, i64, vp, i32, f32, vp]),
     "tg_activation_f32": (i32, [i32, f32, vp, i64, i64, i64, vp]),
     "tg_softmax_rows_f32": (i32, [vp, i64, i64, i64, vp]),
@@ -69,7 +73,7 @@ SIGNATURES = {
     "tg_ipc_get_handle": (i32, [vp, vp, P64]),
     "tg_ipc_open_handle": (i32, [vp, C.POINTER(vp)]),
     "tg_ipc_close_handle": (i32, [vp]),
-    "tg_gemm_peers_f32": (i32, [i64, i64, i64, vp, i64, vp, i64, vp, i64, vp, i32, f32, i32, C.POINTER(vp),
+    "tg_gemm_peers_f32": (i32, [i64, i64, i64, vp, i64, vp, i64, vp, i64, vp, i32, f32, vp, i32, C.POINTER(vp),
                                 C.POINTER(vp), i32, vp]),
     "tg_wait_flags": (i32, [vp, C.POINTER(u64), i32, i64, vp]),
     "tg_gcn_layer_noalloc_f32": (i32, [i64, i64, vp, vp, vp, vp, i64, i64, i64, vp, vp, i32, vp, i64, vp, vp]),

@@ -30,6 +30,7 @@ struct GatherArgs {
     int64_t ldc = 0;
     const float* self = nullptr;      // optional additive term (row i), ld lds
     int64_t lds = 0;
+    const float* row_scale = nullptr; // optional per-row factor (after the self term, before the bias)
     const float* bias = nullptr;      // optional bias[F]
     int act = TG_ACT_NONE;
     float alpha = 0.0f;

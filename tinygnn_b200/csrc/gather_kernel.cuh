@@ -11,8 +11,9 @@
 //   * L2 policy: the CSR arrays are streamed (evict_first), the gathered
 //     operand is kept (evict_last) -- it is re-read ~nnz/K times, the CSR once;
 //     neither is allocated in L1 (no reuse there).
-//  Epilogue: (1/deg) -> (+ self row) -> (+ bias) -> activation, one rounding
-//  each, then vector or element stores depending on C's alignment.
+//  Epilogue: (1/deg) -> (+ self row) -> (x row scale) -> (+ bias) ->
+//  activation, one rounding each, then vector or element stores depending on
+//  C's alignment.
 // ============================================================================
 #pragma once
 
@@ -114,8 +115,8 @@ __device__ __forceinline__ void start_acc(const GatherArgs& a, int64_t row, int6
 }
 
 // Stores features [fo, fo+VEC) of `row`: the raw accumulator on an
-// intermediate pass, else (1/deg) -> (+ self row) -> (+ bias) -> activation,
-// one rounding each.
+// intermediate pass, else (1/deg) -> (+ self row) -> (x row scale) ->
+// (+ bias) -> activation, one rounding each.
 template <int OP, int VEC, bool CVEC>
 __device__ __forceinline__ void finish_acc(const GatherArgs& a, int64_t row, int64_t fo, bool full, int32_t deg,
                                            const float (&acc)[VEC]) {
@@ -130,6 +131,7 @@ __device__ __forceinline__ void finish_acc(const GatherArgs& a, int64_t row, int
         return;
     }
     const float inv_deg = (OP == GATHER_SUM && a.mean && deg > 0) ? __fdiv_rn(1.0f, static_cast<float>(deg)) : 1.0f;
+    const float rs = a.row_scale ? a.row_scale[row] : 1.0f;
     const bool vec_io = CVEC && full;
     float x[VEC], sv[VEC], bv[VEC];
     if (vec_io) {
@@ -149,6 +151,7 @@ __device__ __forceinline__ void finish_acc(const GatherArgs& a, int64_t row, int
         if (OP == GATHER_MAX && deg == 0) v = 0.0f;
         if (OP == GATHER_SUM && a.mean && deg > 0) v = __fmul_rn(v, inv_deg);
         if (a.self) v = __fadd_rn(v, sv[k]);
+        if (a.row_scale) v = __fmul_rn(v, rs);
         if (a.bias) v = __fadd_rn(v, bv[k]);
         x[k] = apply_act(a.act, v, a.alpha);
     }

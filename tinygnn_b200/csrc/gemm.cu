@@ -13,6 +13,7 @@
 //  The DUAL form interleaves two products per k (SAGE's fused dual GEMV,
 //  src/layers.cpp:639-669).
 // ============================================================================
+#include <algorithm>
 #include "launch.cuh"
 
 namespace tg {
@@ -188,7 +189,7 @@ int gather_take_error(cudaStream_t s);
 int peer_take_error(cudaStream_t s);
 void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
              int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s, const PeerOut& peers = PeerOut{},
-             bool c_cols_padded = false);
+             bool c_cols_padded = false, const float* row_scale = nullptr);
 
 // FAST: tensor cores (3xTF32) when the operands allow TMA; otherwise, and in
 // EXACT mode, the k-sequential FMA kernel.
@@ -198,6 +199,36 @@ void gemm(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const fl
         gemm_tc(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, s);
     else
         gemm_exact(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, s);
+}
+
+namespace {
+// C = act(rs[i] * C + bias), in place (the scaled GEMM without tensor cores).
+__global__ void scale_rows_kernel(int64_t M, int64_t N, float* C, int64_t ldc, const float* rs, const float* bias,
+                                  int act, float alpha) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < M * N; t += stride) {
+        const int64_t i = t / N, j = t % N;
+        float v = __fmul_rn(C[i * ldc + j], rs[i]);
+        if (bias) v = __fadd_rn(v, bias[j]);
+        C[i * ldc + j] = apply_act(act, v, alpha);
+    }
+}
+}  // namespace
+
+// C = act(diag(rs) . (A . B) + bias): the tensor-core epilogue scales each
+// row before the bias; without tensor cores, the exact product then a pass.
+void gemm_rowscale(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
+                   float* C, int64_t ldc, const float* rs, const float* bias, int act, float alpha, int mode,
+                   cudaStream_t s) {
+    if (M == 0 || N == 0) return;
+    if ((mode & 0xff) == TG_MODE_FAST && gemm_tc_supported(N, K, A, lda)) {
+        gemm_tc(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, s, PeerOut{}, false, rs);
+        return;
+    }
+    gemm_exact(M, N, K, A, lda, B, ldb, C, ldc, nullptr, TG_ACT_NONE, 0.0f, s);
+    const int64_t total = M * N;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(total, 256), 8 * num_sms()));
+    launch("scale_rows", scale_rows_kernel, dim3(grid), dim3(256), 0, s, M, N, C, ldc, rs, bias, act, alpha);
 }
 
 void gemm_dual_exact(int64_t M, int64_t N, int64_t K, const float* A1, int64_t lda1,
@@ -229,6 +260,24 @@ TG_API tg_status tg_gemm_f32(int64_t M, int64_t N, int64_t K, const float* A, in
         check_ptr("matmul", "B", B, K > 0 && N > 0);
         check_ptr("matmul", "C", C, M > 0 && N > 0);
         gemm(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, mode, as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_gemm_rowscale_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+                                      const float* B, int64_t ldb, float* C, int64_t ldc,
+                                      const float* row_scale, const float* bias, int32_t act, float alpha,
+                                      int32_t mode, void* stream) {
+    return guard([&] {
+        require_device();
+        if (M < 0 || N < 0 || K < 0) invalid("matmul: negative size");
+        check_ld("matmul", "A", lda, K);
+        check_ld("matmul", "B", ldb, N);
+        check_ld("matmul", "C", ldc, N);
+        check_ptr("matmul", "A", A, M > 0 && K > 0);
+        check_ptr("matmul", "B", B, K > 0 && N > 0);
+        check_ptr("matmul", "C", C, M > 0 && N > 0);
+        check_ptr("matmul", "row_scale", row_scale, M > 0 && N > 0);
+        gemm_rowscale(M, N, K, A, lda, B, ldb, C, ldc, row_scale, bias, act, alpha, mode, as_stream(stream));
     });
 }
 

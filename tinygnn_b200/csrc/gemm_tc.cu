@@ -116,6 +116,7 @@ struct TcArgs {
     float alpha;
     int64_t ncols;  // columns stored: N, or round_up(N, 4) when the rows are padded (vec)
     int vec;        // 16-byte stores (peer copies; ldc % 4 == 0, outputs 16-byte aligned, ncols % 4 == 0)
+    const float* rs;  // nullable: row i of the product scaled by rs[i] before the bias (one rounding)
 };
 
 // PEERS: the epilogue also stores to peer copies (and may use 16-byte
@@ -274,11 +275,18 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 #pragma unroll 8
                 for (int rr = 0; rr < rows; ++rr) {  // 8 rows' loads in flight
                     const int64_t off = (m0 + q * 32 + rr) * g.ldc;
+                    const float sc = g.rs ? __ldg(g.rs + m0 + q * 32 + rr) : 1.0f;
 #pragma unroll
                     for (int k = 0; k < V4; ++k) {
                         const int col = (lane + 32 * k) * 4;
                         if (col < g.ncols) {
                             float4 v = *reinterpret_cast<const float4*>(tile + rr * SB + col);
+                            if (g.rs) {
+                                v.x = __fmul_rn(v.x, sc);
+                                v.y = __fmul_rn(v.y, sc);
+                                v.z = __fmul_rn(v.z, sc);
+                                v.w = __fmul_rn(v.w, sc);
+                            }
                             if (g.bias) {
                                 v.x = __fadd_rn(v.x, bv[k][0]);
                                 v.y = __fadd_rn(v.y, bv[k][1]);
@@ -308,11 +316,13 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 #pragma unroll 4
                 for (int rr = 0; rr < rows; ++rr) {
                     const int64_t off = (m0 + q * 32 + rr) * g.ldc;
+                    const float sc = g.rs ? __ldg(g.rs + m0 + q * 32 + rr) : 1.0f;
 #pragma unroll
                     for (int k = 0; k < CPL; ++k) {
                         const int col = lane + 32 * k;
                         if (col < g.N) {
                             float v = tile[rr * SB + col];
+                            if (g.rs) v = __fmul_rn(v, sc);
                             if (g.bias) v = __fadd_rn(v, bv[k]);
                             v = apply_act(g.act, v, g.alpha);
                             g.C[off + col] = v;
@@ -560,6 +570,7 @@ __global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant_
                 for (int rr = 0; rr < rows; ++rr) {
                     if (col < g.ncols) {
                         float v = buf[rr * 33 + lane];
+                        if (g.rs) v = __fmul_rn(v, __ldg(g.rs + r0 + rr));
                         if (g.bias) v = __fadd_rn(v, bv);
                         v = apply_act(g.act, v, g.alpha);
                         const int64_t off = (r0 + rr) * g.ldc + col;
@@ -692,7 +703,7 @@ bool gemm_tc_supported(int64_t N, int64_t K, const float* A, int64_t lda) {
 
 void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
              int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s, const PeerOut& peers,
-             bool c_cols_padded) {
+             bool c_cols_padded, const float* row_scale) {
     if (M == 0 || N == 0) return;
     const int BN = N <= 16 ? 16 : N <= 32 ? 32 : N <= 48 ? 48 : N <= 64 ? 64 : N <= 128 ? 128 : 256;
     const int64_t Kp = (K + 3) / 4 * 4;
@@ -709,7 +720,7 @@ void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const
     bool vec = peers.n > 0 && ldc % 4 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
                (N % 4 == 0 || (c_cols_padded && ldc >= n4));
     for (int p = 0; p < peers.n; ++p) vec = vec && reinterpret_cast<uintptr_t>(peers.c[p]) % 16 == 0;
-    const TcArgs g{C, ldc, M, N, K, bias, act, alpha, vec ? n4 : N, vec ? 1 : 0};
+    const TcArgs g{C, ldc, M, N, K, bias, act, alpha, vec ? n4 : N, vec ? 1 : 0, row_scale};
     if (use_persistent(peers.n > 0)) {
         switch (BN) {
             case 16: launch_tcp<16>(ma, mh, ml, g, peers, s); break;

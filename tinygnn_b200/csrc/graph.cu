@@ -346,18 +346,30 @@ __global__ void self_loop_fill_kernel(int64_t N, int64_t off, const int32_t* rp,
     const int32_t ins = insert[row];
     const int32_t i32 = static_cast<int32_t>(row + off);
     const float di = NORM ? dis_row[row] : 1.0f;
-    for (int32_t b = s; b < e; b += 32 * kSlChunks) {
-        int32_t c[kSlChunks];
-        float x[kSlChunks], dj[kSlChunks];
+    // Software-pipelined: the next group's (col, value) loads are issued
+    // before this group's dis_col gathers are consumed and its stores made.
+    int32_t c[kSlChunks];
+    float x[kSlChunks];
 #pragma unroll
-        for (int u = 0; u < kSlChunks; ++u) {
-            const int32_t t = b + 32 * u + lane;
-            c[u] = t < e ? ci[t] : 0;
-            x[u] = t < e ? v[t] : 0.0f;
-        }
+    for (int u = 0; u < kSlChunks; ++u) {
+        const int32_t t = s + 32 * u + lane;
+        c[u] = t < e ? ci[t] : 0;
+        x[u] = t < e ? v[t] : 0.0f;
+    }
+    for (int32_t b = s; b < e; b += 32 * kSlChunks) {
+        float dj[kSlChunks];
         if (NORM) {
 #pragma unroll
             for (int u = 0; u < kSlChunks; ++u) dj[u] = (b + 32 * u + lane < e) ? dis_col[c[u]] : 0.0f;
+        }
+        int32_t cn[kSlChunks];
+        float xn[kSlChunks];
+        const int32_t bn = b + 32 * kSlChunks;
+#pragma unroll
+        for (int u = 0; u < kSlChunks; ++u) {
+            const int32_t t = bn + 32 * u + lane;
+            cn[u] = t < e ? ci[t] : 0;
+            xn[u] = t < e ? v[t] : 0.0f;
         }
 #pragma unroll
         for (int u = 0; u < kSlChunks; ++u) {
@@ -370,11 +382,36 @@ __global__ void self_loop_fill_kernel(int64_t N, int64_t off, const int32_t* rp,
                 out_v[p] = NORM ? __fmul_rn(__fmul_rn(xs, di), dj[u]) : xs;
             }
         }
+#pragma unroll
+        for (int u = 0; u < kSlChunks; ++u) {
+            c[u] = cn[u];
+            x[u] = xn[u];
+        }
     }
     if (ins >= 0 && lane == 0) {
         out_ci[o + ins] = i32;
         out_v[o + ins] = NORM ? __fmul_rn(__fmul_rn(1.0f, di), dis_col[i32]) : 1.0f;
     }
+}
+
+// FAST gcn_norm scale: dis[i] = 1/sqrt(sum of row i's values + 1), the sum in
+// any order (a warp tree; exact for integer rows within 2^24).
+__global__ void gcn_scale_rows_kernel(int64_t N, const int32_t* rp, const float* v, float* dis) {
+    const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (row >= N) return;
+    const int lane = threadIdx.x & 31;
+    const int32_t s = rp[row], e = rp[row + 1];
+    float part = 0.0f;
+    for (int32_t b = s; b < e; b += 32 * kSlChunks) {
+        float x[kSlChunks];
+#pragma unroll
+        for (int u = 0; u < kSlChunks; ++u) x[u] = (b + 32 * u + lane < e) ? v[b + 32 * u + lane] : 0.0f;
+#pragma unroll
+        for (int u = 0; u < kSlChunks; ++u) part = __fadd_rn(part, x[u]);
+    }
+    for (int k = 16; k > 0; k >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, k));
+    const float d = __fadd_rn(part, 1.0f);
+    if (lane == 0) dis[row] = d > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(d)) : 0.0f;
 }
 
 // Degree (sequential float sum of a self-looped row) and 1/sqrt(deg): the
@@ -724,6 +761,20 @@ TG_API tg_status tg_gcn_norm_rows_fill_f32(int64_t rows, int64_t row_offset, int
                   rows > 0);
         self_loop_fill(rows, row_offset, row_ptr, col_ind, values, row_order, row_ptr_out, insert, dis_row, dis_col,
                        col_ind_out, values_out, as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_gcn_norm_scale_f32(int64_t rows, int64_t nnz, const int32_t* row_ptr, const float* values,
+                                       float* dis_out, void* stream) {
+    return guard([&] {
+        require_device();
+        if (rows < 0 || nnz < 0) invalid("gcn_norm: negative size");
+        if (rows == 0) return;
+        check_ptr("gcn_norm", "row_ptr/dis_out", row_ptr && dis_out ? row_ptr : nullptr, true);
+        check_ptr("gcn_norm", "values", values, nnz > 0);
+        check_csr_input(rows, -1, -1, row_ptr, nullptr, as_stream(stream));  // values read by row only
+        launch("gcn_scale_rows", gcn_scale_rows_kernel, dim3(warp_rows_grid(rows)), dim3(256), 0, as_stream(stream),
+               rows, row_ptr, values, dis_out);
     });
 }
 

@@ -32,7 +32,7 @@ namespace tg {
 
 void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
              int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s, const PeerOut& peers,
-             bool c_cols_padded);
+             bool c_cols_padded, const float* row_scale);
 bool gemm_tc_supported(int64_t N, int64_t K, const float* A, int64_t lda);
 
 namespace {
@@ -151,8 +151,8 @@ TG_API tg_status tg_ipc_close_handle(void* base) {
 
 TG_API tg_status tg_gemm_peers_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B,
                                    int64_t ldb, float* C, int64_t ldc, const float* bias, int32_t act, float alpha,
-                                   int32_t npeers, float* const* peer_C, uint64_t* const* peer_flags,
-                                   int32_t flags, void* stream) {
+                                   const float* row_scale, int32_t npeers, float* const* peer_C,
+                                   uint64_t* const* peer_flags, int32_t flags, void* stream) {
     return guard([&] {
         require_device();
         if (M < 0 || N < 0 || K < 0) invalid("gemm_peers: negative size");
@@ -176,7 +176,7 @@ TG_API tg_status tg_gemm_peers_f32(int64_t M, int64_t N, int64_t K, const float*
             peers.flag[p] = reinterpret_cast<unsigned long long*>(peer_flags[p]);
         }
         gemm_tc(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, as_stream(stream), peers,
-                (flags & TG_FLAG_C_COLS_PADDED) != 0);
+                (flags & TG_FLAG_C_COLS_PADDED) != 0, row_scale);
     });
 }
 

@@ -422,6 +422,35 @@ TG_API tg_status tg_sage_mean_combine_segment_f32(int64_t M, int64_t K, const in
     });
 }
 
+TG_API tg_status tg_gcn_aggregate_f32(int64_t M, int64_t K, int64_t nnz, const int32_t* row_ptr,
+                                      const int32_t* col_ind, const float* values, const float* Hs, int64_t F,
+                                      int64_t ldh, const float* Hs_self, int64_t lds, const float* dis,
+                                      const float* bias, int32_t act, float* out, int64_t ldo,
+                                      const int32_t* row_order, const int32_t* seg_begin, const int32_t* seg_end,
+                                      int32_t carry, int32_t last, int32_t mode, void* stream) {
+    return guard([&] {
+        require_device();
+        if (M < 0 || K < 0 || F < 0 || nnz < 0) invalid("gcn_aggregate: negative size");
+        check_ld("gcn_aggregate", "Hs", ldh, F);
+        check_ld("gcn_aggregate", "Hs_self", lds, F);
+        check_ld("gcn_aggregate", "out", ldo, F);
+        check_ptr("gcn_aggregate", "row_ptr/Hs_self/dis/out", row_ptr && Hs_self && dis && out ? row_ptr : nullptr,
+                  M > 0 && F > 0);
+        check_ptr("gcn_aggregate", "col_ind/values/Hs", col_ind && values && Hs ? col_ind : nullptr, nnz > 0 && F > 0);
+        if ((seg_begin == nullptr) != (seg_end == nullptr)) invalid("gcn_aggregate: seg_begin and seg_end go together");
+        // with segments the CSR may be a row-offset view: its entry count is row_ptr[M]
+        check_csr_input(M, K, seg_begin ? -1 : nnz, row_ptr, col_ind, as_stream(stream), row_order);
+        GatherArgs a;
+        a.M = M; a.rp = row_ptr; a.ci = col_ind; a.val = values; a.order = row_order;
+        a.B = Hs; a.ldb = ldh; a.F = F; a.C = out; a.ldc = ldo;
+        a.self = Hs_self; a.lds = lds; a.row_scale = dis;
+        a.bias = bias; a.act = act; a.op = GATHER_SUM;
+        a.b_padded = (mode & TG_FLAG_B_ROWS_PADDED) != 0;
+        a.seg_lo = seg_begin; a.seg_hi = seg_end; a.carry = carry != 0; a.last = last != 0;
+        gather_rows(a, as_stream(stream));
+    });
+}
+
 TG_API tg_status tg_csr_degree_order(int64_t M, const int32_t* row_ptr, int32_t* order_out,
                                      void* stream) {
     return guard([&] {

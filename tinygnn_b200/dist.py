@@ -292,6 +292,20 @@ class ShardedModel:
             self.selfs.append(torch.empty((self.rows, _pad4(fo)), dtype=torch.float32, device=device)
                               if L.kind == "sage" else None)
         self.timing = None  # optional hook: (layer index, phase, "start"|"end") -> None
+        # FAST GCN without a normalised copy of A: this rank's 1/sqrt(deg)
+        # while a forward runs (set by forward_model / forward_from_host).
+        self.scale: Optional[torch.Tensor] = None
+        self.scale_buf = torch.empty(max(self.rows, 1), dtype=torch.float32, device=device)
+
+    def _scaled(self, li: int) -> bool:
+        """Layer li is a GCN layer run in the factored FAST form."""
+        return self.scale is not None and self.layers[li].kind == "gcn"
+
+    def _self_rows(self, li: int, a: int = 0, b: Optional[int] = None) -> torch.Tensor:
+        """This rank's rows [a, b) of layer li's gathered operand."""
+        fo = self.layers[li].W.shape[1]
+        r0 = self.comm.rank * self.R
+        return self.full[li][r0 + a:r0 + (self.rows if b is None else b), :fo]
 
     def _mark(self, li: int, what: str, edge: str) -> None:
         if self.timing is not None:
@@ -338,9 +352,11 @@ class ShardedModel:
                 self.hpad[li][:, :H.shape[1]] = H
                 H = self.hpad[li][:, :H.shape[1]]
             outs, flags = self.pex.peer_targets(li, r * self.R * buf.shape[1])
-            ops.gemm_peers(H, L.W, buf[r * self.R:r * self.R + self.rows, :fo], outs, flags, cols_padded=True)
+            ops.gemm_peers(H, L.W, buf[r * self.R:r * self.R + self.rows, :fo], outs, flags, cols_padded=True,
+                           row_scale=self.scale if self._scaled(li) else None)
         else:
-            ops.matmul(H, L.W, out=self.full[li][r * self.R:r * self.R + self.rows, :fo], mode=self.mode)
+            ops.matmul(H, L.W, out=self.full[li][r * self.R:r * self.R + self.rows, :fo], mode=self.mode,
+                       row_scale=self.scale if self._scaled(li) else None)
         if L.kind == "sage":
             ops.matmul(H, L.W_self, out=self.selfs[li][:, :fo], mode=self.mode)
         self._mark(li, "gemm", "end")
@@ -364,6 +380,9 @@ class ShardedModel:
         L = self.layers[li]
         fo = L.W.shape[1]
         B = self.full[li][:self.n, :fo]
+        if self._scaled(li):
+            return ops.gcn_aggregate(A, B, self._self_rows(li), self.scale, bias=L.b, act=L.act, out=self.outs[li],
+                                     seg_begin=lo, seg_end=hi, carry=carry, last=last)
         if L.kind == "gcn":
             if lo is None:
                 return ops.spmm(A, B, bias=L.b, act=L.act, out=self.outs[li])
@@ -477,8 +496,7 @@ class ShardedModel:
             d_v.fill_(1.0)
         cur.wait_event(csr_ready)
         A = CSR(self.rows, self.n, d_rp, d_ci, d_v)
-        A_gcn = (gcn_norm_rows_scheduled(A, self.row0, self.R, self.comm, bufs["dis"])
-                 if any(L.kind == "gcn" for L in self.layers) else None)
+        A_gcn = self._normalise(A, bufs["dis"])
         if single and nb > 1:
             # Layer 1 per feature block: GEMM of block q's rows, then the gather
             # pass over the columns of block q (exact: passes in column order).
@@ -492,9 +510,15 @@ class ShardedModel:
                 if a < b:
                     if landing is not None:
                         d_X[a:b].copy_(landing[a:b])
-                    ops.matmul(d_X[a:b], L.W, out=self.full[0][a:b, :fo], mode=self.mode)
-                ops.spmm_segment(A_gcn, B, sp[q], sp[q + 1], self.outs[0], q > 0, q == nb - 1, bias=L.b,
-                                 act=L.act)
+                    ops.matmul(d_X[a:b], L.W, out=self.full[0][a:b, :fo], mode=self.mode,
+                               row_scale=self.scale[a:b] if self._scaled(0) else None)
+                if self._scaled(0):
+                    ops.gcn_aggregate(A_gcn, B, self._self_rows(0), self.scale, bias=L.b, act=L.act,
+                                      out=self.outs[0], seg_begin=sp[q], seg_end=sp[q + 1], carry=q > 0,
+                                      last=q == nb - 1)
+                else:
+                    ops.spmm_segment(A_gcn, B, sp[q], sp[q + 1], self.outs[0], q > 0, q == nb - 1, bias=L.b,
+                                     act=L.act)
             H = self.outs[0]
             first = 1
         else:
@@ -521,7 +545,57 @@ class ShardedModel:
             self.exchange(last)
             self._chunked_last_layer(A_gcn, A, h_out, cp, out_chunks)
         cur.synchronize()
+        self.scale = None
         return h_out
+
+    def _normalise(self, A: CSR, dis_all: torch.Tensor) -> Optional[CSR]:
+        """What Model::forward does to the raw adjacency rows before the GCN
+        layers (src/model.cpp:365-381), with a longest-first row schedule:
+        EXACT -- the normalised copy, bit for bit; FAST -- the raw rows plus
+        this rank's 1/sqrt(deg) (self.scale), for the factored layers.
+        None when no layer is a GCN layer."""
+        if not any(L.kind == "gcn" for L in self.layers):
+            self.scale = None
+            return None
+        if self.mode == "fast":
+            As = CSR(A.n_rows, A.n_cols, A.row_ptr, A.col_ind, A.values, A.order, A.validated)
+            if As.order is None:
+                As.order = ops.degree_order(As)
+            self.scale = ops.gcn_norm_scale(As, out=self.scale_buf[:A.n_rows])
+            return As
+        self.scale = None
+        return gcn_norm_rows_scheduled(A, self.row0, self.R, self.comm, dis_all)
+
+    def prepare(self, A_raw: CSR, dis_all: Optional[torch.Tensor] = None):
+        """The per-graph part of Model::forward for this rank's raw adjacency
+        rows: (A for the GCN layers, A for the SAGE layers, this rank's GCN
+        scale or None) -- see _normalise."""
+        if dis_all is None and self.mode != "fast":
+            dis_all = torch.zeros(self.R * self.comm.world, dtype=torch.float32, device=self.device)
+        A_gcn = self._normalise(A_raw, dis_all)
+        scale, self.scale = self.scale, None
+        A_sage = A_raw
+        if A_gcn is not None and self.mode == "fast":
+            A_sage = A_gcn  # the same raw rows, scheduled
+        elif A_raw.order is None and any(L.kind == "sage" for L in self.layers):
+            A_sage = CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind, A_raw.values,
+                         ops.degree_order(A_raw), A_raw.validated)
+        return A_gcn, A_sage, scale
+
+    def forward_prepared(self, prepared, X: torch.Tensor, log_softmax: bool = True) -> torch.Tensor:
+        """The layers (and log_softmax) on a graph prepared by prepare()."""
+        A_gcn, A_sage, scale = prepared
+        self.scale = scale
+        try:
+            return self.forward(A_gcn, A_sage, X, log_softmax)
+        finally:
+            self.scale = None
+
+    def forward_model(self, A_raw: CSR, X: torch.Tensor, log_softmax: bool = True,
+                      dis_all: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Model::forward on this rank's raw adjacency rows (no self-loops) and
+        feature rows in HBM: normalisation, the layers, log_softmax."""
+        return self.forward_prepared(self.prepare(A_raw, dis_all), X, log_softmax)
 
     def _chunked_last_layer(self, A_gcn: Optional[CSR], A_raw: CSR, h_out: torch.Tensor,
                             cp: torch.cuda.Stream, chunks: int) -> None:
@@ -542,7 +616,9 @@ class ShardedModel:
             Ak = CSR(b - a, A.n_cols, A.row_ptr[a:b + 1], A.col_ind, A.values, validated=A.validated)
             Ak.order = ops.degree_order(Ak)
             out = self.outs[li][a:b]
-            if L.kind == "gcn":
+            if self._scaled(li):
+                ops.gcn_aggregate(Ak, B, self._self_rows(li, a, b), self.scale[a:b], bias=L.b, act=L.act, out=out)
+            elif L.kind == "gcn":
                 ops.spmm(Ak, B, bias=L.b, act=L.act, out=out)
             else:
                 ops.sage_mean_combine(Ak, B, self.selfs[li][a:b, :fo], bias=L.b, act=L.act, out=out)

@@ -116,8 +116,10 @@ def _csr_call(csrs, fn, *args) -> None:
 
 # ── dense ops ────────────────────────────────────────────────────────────────
 def matmul(A: torch.Tensor, B: torch.Tensor, bias=None, act=None, alpha: float = 0.0,
-           out: Optional[torch.Tensor] = None, mode: str = "exact") -> torch.Tensor:
-    """C = act(A . B + bias)  (TinyGNN matmul, src/ops.cpp:70)."""
+           out: Optional[torch.Tensor] = None, mode: str = "exact",
+           row_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """C = act(A . B + bias)  (TinyGNN matmul, src/ops.cpp:70); with
+    ``row_scale``, C = act(diag(row_scale) . (A . B) + bias)."""
     A, B = _dense(A, "A"), _dense(B, "B")
     if A.shape[1] != B.shape[0]:
         raise _lib.InvalidArgument(
@@ -129,6 +131,10 @@ def matmul(A: torch.Tensor, B: torch.Tensor, bias=None, act=None, alpha: float =
     if out is None:
         out = torch.empty((M, N), dtype=torch.float32, device=A.device)
     b = _vec(bias)
+    if row_scale is not None:
+        check(lib.tg_gemm_rowscale_f32(M, N, K, _p(A), _ld(A), _p(B), _ld(B), _p(out), _ld(out), _p(row_scale),
+                                       _p(b), ACT[act], alpha, MODE[mode], _stream()))
+        return out
     check(lib.tg_gemm_f32(M, N, K, _p(A), _ld(A), _p(B), _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha,
                           MODE[mode], _stream()))
     return out
@@ -417,6 +423,33 @@ def gcn_norm_rows_fill(A: CSR, row_offset: int, rp_out: torch.Tensor, insert: to
     return CSR(N, A.n_cols, rp_out, ci[:nnz], v[:nnz], order, validated=True)
 
 
+def gcn_norm_scale(A: CSR, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """FAST gcn_norm as per-row factors: dis[i] = 1/sqrt(sum of row i's values + 1)."""
+    if out is None:
+        out = torch.empty(A.n_rows, dtype=torch.float32, device=A.row_ptr.device)
+    nnz = A.nnz
+    _csr_call((A,), lib.tg_gcn_norm_scale_f32, A.n_rows, nnz, _p(A.row_ptr), _p(A.values), _p(out), _stream())
+    return out
+
+
+def gcn_aggregate(A: CSR, Hs: torch.Tensor, Hs_self: torch.Tensor, dis: torch.Tensor, bias=None, act=None,
+                  out: Optional[torch.Tensor] = None, seg_begin=None, seg_end=None, carry: bool = False,
+                  last: bool = True, row_order=None) -> torch.Tensor:
+    """out_i = act(dis[i] * (sum_j a_ij Hs[j] + Hs_self[i]) + bias): the GCN
+    aggregation of D^-1/2 (A + I) D^-1/2 without a normalised copy of A
+    (Hs = diag(dis) . HW over all nodes).  Optional column-block pass."""
+    Hs, Hs_self = _dense(Hs, "Hs"), _dense(Hs_self, "Hs_self")
+    F = Hs.shape[1]
+    if out is None:
+        out = torch.empty((A.n_rows, F), dtype=torch.float32, device=Hs.device)
+    b = _vec(bias)
+    flags = FLAG_B_ROWS_PADDED if _padded(Hs) else 0
+    _csr_call((A,), lib.tg_gcn_aggregate_f32, A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _p(A.values),
+              _p(Hs), F, _ld(Hs), _p(Hs_self), _ld(Hs_self), _p(dis), _p(b), ACT[act], _p(out), _ld(out),
+              _p(_ord(A, row_order)), _p(seg_begin), _p(seg_end), int(carry), int(last), flags, _stream())
+    return out
+
+
 def csr_validate(A: CSR) -> None:
     """Tensor::sparse_csr's checks (src/tensor.cpp:46-86) on device arrays."""
     check(lib.tg_csr_validate(A.n_rows, A.n_cols, A.nnz, _p(A.row_ptr), _p(A.col_ind), _stream()))
@@ -498,8 +531,9 @@ def ipc_close_handle(base: int) -> None:
 
 
 def gemm_peers(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, peer_out, peer_flags, bias=None, act=None,
-               alpha: float = 0.0, cols_padded: bool = False) -> torch.Tensor:
-    """out = act(A . B + bias) on the tensor cores, every row also stored at
+               alpha: float = 0.0, cols_padded: bool = False, row_scale=None) -> torch.Tensor:
+    """out = act(A . B + bias) on the tensor cores (rows scaled by
+    ``row_scale`` before the bias when given), every row also stored at
     the same offset of each peer_out[p] (device addresses of other GPUs'
     copies, same leading dimension); after each 128-row tile the counter at
     peer_flags[p] is incremented (release, system scope)."""
@@ -511,7 +545,7 @@ def gemm_peers(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, peer_out, pe
     pf = (C.c_void_p * max(1, n))(*peer_flags)
     b = _vec(bias)
     check(lib.tg_gemm_peers_f32(M, N, K, _p(A), _ld(A), _p(B), _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha,
-                                n, pc, pf, 0x200 if cols_padded else 0, _stream()))
+                                _p(row_scale), n, pc, pf, 0x200 if cols_padded else 0, _stream()))
     return out
 
 
