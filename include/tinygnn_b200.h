@@ -117,6 +117,25 @@ TG_API tg_status tg_gemm_f32(int64_t M, int64_t N, int64_t K, const float* A, in
                              const float* bias, int32_t act, float alpha, int32_t mode,
                              void* stream);
 
+/* C1 = A . B1 and C2 = A . B2 (B1, B2: K x N, ld ldb).  FAST: one
+ * tensor-core pass over A with [B1 | B2] when 2N <= 256 (SAGE's W_neigh and
+ * W_self on the same input); otherwise two tg_gemm_f32 products. */
+TG_API tg_status tg_gemm_pair_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+                                  const float* B1, const float* B2, int64_t ldb, float* C1,
+                                  int64_t ldc1, float* C2, int64_t ldc2, int32_t mode, void* stream);
+
+/* C = act([A1 | A2] . [B1; B2] + bias) (A1: M x K1, A2: M x K2, B1: K1 x N,
+ * B2: K2 x N): SAGELayer's concat of the aggregate and the node's own row
+ * feeding one product (src/layers.cpp:538-752, FAST mode).  FAST with
+ * 16-byte aligned rows: one tensor-core GEMM whose operand loads switch
+ * from A1 to A2 along K -- the concatenation is never stored; otherwise two
+ * products and a sum. */
+TG_API tg_status tg_gemm_cat_f32(int64_t M, int64_t N, int64_t K1, const float* A1, int64_t lda1,
+                                 int64_t K2, const float* A2, int64_t lda2, const float* B1,
+                                 int64_t ldb1, const float* B2, int64_t ldb2, float* C, int64_t ldc,
+                                 const float* bias, int32_t act, float alpha, int32_t mode,
+                                 void* stream);
+
 /* C = act(diag(row_scale) . (A . B) + bias): tg_gemm_f32 with row i of the
  * product multiplied by row_scale[i] (one rounding) before the bias.  No
  * counterpart in the reference; it carries gcn_norm's column scaling in the

@@ -128,3 +128,22 @@ def powerlaw_csr(rng, n, deg, alpha=1.2, weighted=True, diag=True):
     rp = np.cumsum(rp).astype(np.int32)
     v = (rng.random(d.size) + 0.05).astype(np.float32) if weighted else np.ones(d.size, np.float32)
     return rp, d, v
+
+
+def assert_sage_fast_close(got, ref, rp, ci, H, Wn, Ws, what=""):
+    """A FAST-mode SAGE layer (its products on the tensor cores, 3xTF32):
+    a reordered fp32 sum of 2 F_in terms per output, held to
+    |d| <= ATOL + RTOL * sum_k |a_k||b_k| -- the magnitude its rounding acts
+    on (|mean| and |max| of the aggregate are bounded by the largest |h| of
+    the row's neighbours).  An elementwise bound on |ref| cannot hold at
+    cancelling elements for any reordering; logits are checked elementwise
+    by the model tests."""
+    n, fi = H.shape
+    absH = np.abs(H).astype(np.float64)
+    seg = np.repeat(np.arange(n), np.diff(rp))
+    agg_abs = np.zeros((n, fi))
+    np.maximum.at(agg_abs, seg, absH[ci])
+    mag = agg_abs @ np.abs(Wn).astype(np.float64) + absH @ np.abs(Ws).astype(np.float64)
+    err = np.abs(np.asarray(got, np.float64) - np.asarray(ref, np.float64))
+    bad = err > ATOL + RTOL * mag
+    assert not bad.any(), f"{what}: {bad.sum()} outside |d| <= {ATOL} + {RTOL} sum|a||b|; max err {err.max():.3g}"

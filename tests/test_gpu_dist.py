@@ -292,3 +292,29 @@ def test_gcn_norm_scale_matches_gcn_norm_degrees(tg):
             assert_close(fast.cpu().numpy(), exact.cpu().numpy(), kind)
         else:
             assert_bits_equal(fast.cpu().numpy(), exact.cpu().numpy(), kind)
+
+
+@pytest.mark.parametrize("fin", [40, 602])
+def test_fast_sage_model_logits_vs_oracle(tg, fin):
+    """FAST SAGE-mean Model::forward (transform-first, W_neigh and W_self in
+    one tensor-core pass) -- logits within |d| <= 1e-5 + 1e-4 |ref| of the
+    oracle's Model::forward + log_softmax, elementwise."""
+    from tinygnn_b200.dist import Comm, Layer, ShardedModel
+    rng, rp, ci, v, X = _graph(n=20000, seed=31 + fin)
+    X = rng.standard_normal((rp.size - 1, fin)).astype(np.float32)
+    n = rp.size - 1
+    g = lambda i, o: (rng.uniform(-1, 1, (i, o)) * np.sqrt(6.0 / (i + o))).astype(np.float32)  # noqa: E731
+    Wn0, Ws0, Wn1, Ws1 = g(fin, 32), g(fin, 32), g(32, 11), g(32, 11)
+    b0 = (rng.standard_normal(32) * 0.1).astype(np.float32)
+    b1 = (rng.standard_normal(11) * 0.1).astype(np.float32)
+    d = lambda a: torch.as_tensor(a).cuda()  # noqa: E731
+    layers = [Layer("sage", d(Wn0), d(b0), "relu", d(Ws0)), Layer("sage", d(Wn1), d(b1), None, d(Ws1))]
+    Xd = torch.zeros((n, (fin + 3) // 4 * 4), device="cuda")[:, :fin]
+    Xd[:] = d(X)
+    got = ShardedModel(layers, n, Comm(1, 0), "cuda", mode="fast").forward_model(tg.CSR.from_numpy(rp, ci, v), Xd)
+    spec = [dict(type="sage", **{"in": fin, "out": 32}, act="relu"), dict(type="sage", **{"in": 32, "out": 11})]
+    w = {"layer0.weight_neigh": Wn0, "layer0.weight_self": Ws0, "layer0.bias": b0,
+         "layer1.weight_neigh": Wn1, "layer1.weight_self": Ws1, "layer1.bias": b1}
+    oref = P.activation("log_softmax", oracle.model_forward(P, spec, w, rp, ci, v, X))
+    tg.ops.take_device_error()
+    assert_close(got.cpu().numpy(), oref, f"fast sage model fin={fin}")

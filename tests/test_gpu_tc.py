@@ -98,3 +98,71 @@ def test_fast_layers_within_tolerance(tg):
                         torch.as_tensor(b).cuda(), "mean", "relu", mode="fast")
     assert_close(got.cpu().numpy(), P.sage_layer(rp, ci, v, H, W, W2, b, "mean", True), "sage fast")
     tg.ops.take_device_error()
+
+
+@pytest.mark.parametrize("M,K,N", [(1000, 602, 128), (513, 128, 41), (300, 96, 20), (129, 33, 7)])
+def test_tc_gemm_pair_vs_oracle(tg, M, K, N):
+    """C1 = A . B1, C2 = A . B2 in one tensor-core pass ([B1 | B2], columns
+    split in the epilogue into two strided outputs)."""
+    rng = np.random.default_rng(M + K + N)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B1 = (rng.standard_normal((K, N)) / np.sqrt(K)).astype(np.float32)
+    B2 = (rng.standard_normal((K, N)) / np.sqrt(K)).astype(np.float32)
+    ld = 2 * ((N + 3) // 4 * 4)
+    T = torch.full((M, ld), 7.0, device="cuda")
+    half = ld // 2
+    tg.ops.gemm_pair(padded(A), torch.as_tensor(B1).cuda(), torch.as_tensor(B2).cuda(), T[:, :N], T[:, half:half + N])
+    torch.cuda.synchronize()
+    tg.ops.take_device_error()
+    h = T.cpu().numpy()
+    check(h[:, :N], A, B1, "pair C1")
+    check(h[:, half:half + N], A, B2, "pair C2")
+    assert np.all(h[:, N:half] == 7.0) and np.all(h[:, half + N:] == 7.0)
+
+
+@pytest.mark.parametrize("M,K1,K2,N", [(1000, 128, 128, 128), (700, 40, 602, 41), (300, 33, 70, 64), (129, 8, 8, 7)])
+def test_tc_gemm_cat_vs_oracle(tg, M, K1, K2, N):
+    """act([A1 | A2] . [B1; B2] + b) with the concatenation done by the
+    operand loads (K1 not a multiple of the 32-column k-block included)."""
+    rng = np.random.default_rng(M + K1 + K2 + N)
+    A1 = rng.standard_normal((M, K1)).astype(np.float32)
+    A2 = rng.standard_normal((M, K2)).astype(np.float32)
+    B1 = (rng.standard_normal((K1, N)) / np.sqrt(K1 + K2)).astype(np.float32)
+    B2 = (rng.standard_normal((K2, N)) / np.sqrt(K1 + K2)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    got = tg.ops.gemm_cat(padded(A1), padded(A2), torch.as_tensor(B1).cuda(), torch.as_tensor(B2).cuda(),
+                          bias=torch.as_tensor(b).cuda())
+    torch.cuda.synchronize()
+    tg.ops.take_device_error()
+    A = np.concatenate([A1, A2], 1)
+    B = np.concatenate([B1, B2], 0)
+    check(got.cpu().numpy(), A, B, "cat", bias=b)
+    # A2 not 16-byte aligned (a view one float into its buffer): the
+    # two-product path, same tolerance
+    buf = torch.zeros((M, K2 + 1), device="cuda")
+    buf[:, 1:] = torch.as_tensor(A2).cuda()
+    got = tg.ops.gemm_cat(padded(A1), buf[:, 1:], torch.as_tensor(B1).cuda(), torch.as_tensor(B2).cuda(),
+                          bias=torch.as_tensor(b).cuda())
+    check(got.cpu().numpy(), A, B, "cat (fallback when unaligned)", bias=b)
+
+
+@pytest.mark.parametrize("fin,fout,agg", [(64, 128, "mean"), (128, 128, "mean"), (128, 40, "mean"),
+                                          (40, 64, "max"), (602, 41, "mean")])
+def test_fast_sage_layer_paths_vs_oracle(tg, fin, fout, agg):
+    """FAST SAGELayer: aggregate-first with the concat-K tensor-core GEMM
+    (F_in <= F_out, or max), transform-first with the pair GEMM (mean,
+    F_in > F_out); within the tolerance of the reference's layer."""
+    from tests.helpers import assert_sage_fast_close, powerlaw_csr
+    rng = np.random.default_rng(fin * 3 + fout)
+    n = 4000
+    rp, ci, v = powerlaw_csr(rng, n, 10, weighted=False, diag=False)
+    H = rng.standard_normal((n, fin)).astype(np.float32)
+    Wn = (rng.standard_normal((fin, fout)) * 0.1).astype(np.float32)
+    Ws = (rng.standard_normal((fin, fout)) * 0.1).astype(np.float32)
+    b = (rng.standard_normal(fout) * 0.1).astype(np.float32)
+    got = tg.sage_layer(tg.CSR.from_numpy(rp, ci, v), padded(H), torch.as_tensor(Wn).cuda(),
+                        torch.as_tensor(Ws).cuda(), torch.as_tensor(b).cuda(), agg, "relu", mode="fast")
+    torch.cuda.synchronize()
+    tg.ops.take_device_error()
+    assert_sage_fast_close(got.cpu().numpy(), P.sage_layer(rp, ci, v, H, Wn, Ws, b, agg, True), rp, ci, H, Wn, Ws,
+                           f"sage fast {fin}->{fout} {agg}")

@@ -34,6 +34,8 @@ SIGNATURES = {
     "tg_device_count": (i32, []),
     "tg_kernel_launch_count": (u64, []),
     "tg_gemm_f32": (i32, [i64, i64, i64, vp, i64, vp, i64, vp, i64, vp, i32, f32, i32, vp]),
+    "tg_gemm_pair_f32": (i32, [i64, i64, i64, vp, i64, vp, vp, i64, vp, i64, vp, i64, i32, vp]),
+    "tg_gemm_cat_f32": (i32, [i64, i64, i64, vp, i64, i64, vp, i64, vp, i64, vp, i64, vp, i64, vp, i32, f32, i32, vp]),
     "tg_gemm_rowscale_f32": (i32, [i64, i64, i64, vp, i64, vp, i64, vp, i64, vp, vp, i32, f32, i32, vp]),
     "tg_gcn_norm_scale_f32": (i32, [i64, i64, vp, vp, vp, vp]),
     "tg_gcn_aggregate_f32": (i32, [i64, i64, i64, vp, vp, vp, vp, i64, i64, vp, i64, vp, vp, i32, vp, i64, vp, vp, vp,

@@ -191,6 +191,12 @@ void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const
              int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s, const PeerOut& peers = PeerOut{},
              bool c_cols_padded = false, const float* row_scale = nullptr);
 
+void gemm_tc_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B1, const float* B2,
+                  int64_t ldb, float* C1, int64_t ldc1, float* C2, int64_t ldc2, cudaStream_t s);
+void gemm_tc_cat(int64_t M, int64_t N, int64_t K1, const float* A1, int64_t lda1, int64_t K2, const float* A2,
+                 int64_t lda2, const float* B1, int64_t ldb1, const float* B2, int64_t ldb2, float* C, int64_t ldc,
+                 const float* bias, int act, float alpha, cudaStream_t s);
+
 // FAST: tensor cores (3xTF32) when the operands allow TMA; otherwise, and in
 // EXACT mode, the k-sequential FMA kernel.
 void gemm(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
@@ -229,6 +235,50 @@ void gemm_rowscale(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
     const int64_t total = M * N;
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(total, 256), 8 * num_sms()));
     launch("scale_rows", scale_rows_kernel, dim3(grid), dim3(256), 0, s, M, N, C, ldc, rs, bias, act, alpha);
+}
+
+// C1 = A . B1, C2 = A . B2: one tensor-core pass over A in FAST mode when
+// [B1 | B2] fits one tile (2N <= 256), else two products.
+void gemm_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B1, const float* B2,
+               int64_t ldb, float* C1, int64_t ldc1, float* C2, int64_t ldc2, int mode, cudaStream_t s) {
+    if (M == 0 || N == 0) return;
+    if ((mode & 0xff) == TG_MODE_FAST && gemm_tc_supported(2 * N, K, A, lda)) {
+        gemm_tc_pair(M, N, K, A, lda, B1, B2, ldb, C1, ldc1, C2, ldc2, s);
+        return;
+    }
+    gemm(M, N, K, A, lda, B1, ldb, C1, ldc1, nullptr, TG_ACT_NONE, 0.0f, mode, s);
+    gemm(M, N, K, A, lda, B2, ldb, C2, ldc2, nullptr, TG_ACT_NONE, 0.0f, mode, s);
+}
+
+namespace {
+// C = act(C + T + bias) in place (the concatenated product without tensor cores).
+__global__ void add_bias_act_kernel(int64_t M, int64_t N, float* C, int64_t ldc, const float* T, int64_t ldt,
+                                    const float* bias, int act, float alpha) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < M * N; t += stride) {
+        const int64_t i = t / N, j = t % N;
+        float v = __fadd_rn(C[i * ldc + j], T[i * ldt + j]);
+        if (bias) v = __fadd_rn(v, bias[j]);
+        C[i * ldc + j] = apply_act(act, v, alpha);
+    }
+}
+}  // namespace
+
+// C = act([A1 | A2] . [B1; B2] + bias): FAST, one tensor-core pass with the
+// concatenation done by the operand loads; otherwise two products and a sum.
+void gemm_cat(int64_t M, int64_t N, int64_t K1, const float* A1, int64_t lda1, int64_t K2, const float* A2,
+              int64_t lda2, const float* B1, int64_t ldb1, const float* B2, int64_t ldb2, float* C, int64_t ldc,
+              const float* bias, int act, float alpha, int mode, cudaStream_t s) {
+    if (M == 0 || N == 0) return;
+    if ((mode & 0xff) == TG_MODE_FAST && gemm_tc_supported(N, K1, A1, lda1) && gemm_tc_supported(N, K2, A2, lda2)) {
+        gemm_tc_cat(M, N, K1, A1, lda1, K2, A2, lda2, B1, ldb1, B2, ldb2, C, ldc, bias, act, alpha, s);
+        return;
+    }
+    gemm(M, N, K1, A1, lda1, B1, ldb1, C, ldc, nullptr, TG_ACT_NONE, 0.0f, mode, s);
+    Scratch<float> T(static_cast<size_t>(M * N), s);
+    gemm(M, N, K2, A2, lda2, B2, ldb2, T.p, N, nullptr, TG_ACT_NONE, 0.0f, mode, s);
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(M * N, 256), 8 * num_sms()));
+    launch("add_bias_act", add_bias_act_kernel, dim3(grid), dim3(256), 0, s, M, N, C, ldc, T.p, N, bias, act, alpha);
 }
 
 void gemm_dual_exact(int64_t M, int64_t N, int64_t K, const float* A1, int64_t lda1,
@@ -278,6 +328,43 @@ TG_API tg_status tg_gemm_rowscale_f32(int64_t M, int64_t N, int64_t K, const flo
         check_ptr("matmul", "C", C, M > 0 && N > 0);
         check_ptr("matmul", "row_scale", row_scale, M > 0 && N > 0);
         gemm_rowscale(M, N, K, A, lda, B, ldb, C, ldc, row_scale, bias, act, alpha, mode, as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_gemm_pair_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B1,
+                                  const float* B2, int64_t ldb, float* C1, int64_t ldc1, float* C2, int64_t ldc2,
+                                  int32_t mode, void* stream) {
+    return guard([&] {
+        require_device();
+        if (M < 0 || N < 0 || K < 0) invalid("matmul: negative size");
+        check_ld("matmul", "A", lda, K);
+        check_ld("matmul", "B", ldb, N);
+        check_ld("matmul", "C1", ldc1, N);
+        check_ld("matmul", "C2", ldc2, N);
+        check_ptr("matmul", "A", A, M > 0 && K > 0);
+        check_ptr("matmul", "B1/B2", B1 && B2 ? B1 : nullptr, K > 0 && N > 0);
+        check_ptr("matmul", "C1/C2", C1 && C2 ? C1 : nullptr, M > 0 && N > 0);
+        gemm_pair(M, N, K, A, lda, B1, B2, ldb, C1, ldc1, C2, ldc2, mode, as_stream(stream));
+    });
+}
+
+TG_API tg_status tg_gemm_cat_f32(int64_t M, int64_t N, int64_t K1, const float* A1, int64_t lda1, int64_t K2,
+                                 const float* A2, int64_t lda2, const float* B1, int64_t ldb1, const float* B2,
+                                 int64_t ldb2, float* C, int64_t ldc, const float* bias, int32_t act, float alpha,
+                                 int32_t mode, void* stream) {
+    return guard([&] {
+        require_device();
+        if (M < 0 || N < 0 || K1 < 0 || K2 < 0) invalid("matmul: negative size");
+        check_ld("matmul", "A1", lda1, K1);
+        check_ld("matmul", "A2", lda2, K2);
+        check_ld("matmul", "B1", ldb1, N);
+        check_ld("matmul", "B2", ldb2, N);
+        check_ld("matmul", "C", ldc, N);
+        check_ptr("matmul", "A1/B1", A1 && B1 ? A1 : nullptr, M > 0 && K1 > 0 && N > 0);
+        check_ptr("matmul", "A2/B2", A2 && B2 ? A2 : nullptr, M > 0 && K2 > 0 && N > 0);
+        check_ptr("matmul", "C", C, M > 0 && N > 0);
+        gemm_cat(M, N, K1, A1, lda1, K2, A2, lda2, B1, ldb1, B2, ldb2, C, ldc, bias, act, alpha, mode,
+                 as_stream(stream));
     });
 }
 

@@ -117,12 +117,20 @@ struct TcArgs {
     int64_t ncols;  // columns stored: N, or round_up(N, 4) when the rows are padded (vec)
     int vec;        // 16-byte stores (peer copies; ldc % 4 == 0, outputs 16-byte aligned, ncols % 4 == 0)
     const float* rs;  // nullable: row i of the product scaled by rs[i] before the bias (one rounding)
+    // Column split (local epilogue only): columns [nsplit, N) go to C2 at
+    // column - nsplit (ld ldc2); nsplit == N: everything to C.
+    float* C2;
+    int64_t ldc2, nsplit;
+    // Concat along K: k-blocks [0, kb1) come from tmA, the rest from tmA2
+    // (A = [A1 | A2], B = [B1; B2] with B1 zero-padded to kb1 * BK rows).
+    int kb1;
 };
 
 // PEERS: the epilogue also stores to peer copies (and may use 16-byte
 // stores); false compiles the lean local-only epilogue.
 template <int BN, int STAGES_, bool PEERS>
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                         const __grid_constant__ CUtensorMap tmA2,
                                                          const __grid_constant__ CUtensorMap tmBh,
                                                          const __grid_constant__ CUtensorMap tmBl,
                                                          const TcArgs g,
@@ -138,7 +146,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t m0 = static_cast<int64_t>(blockIdx.x) * BM;
-    const int KB = static_cast<int>((g.K + BK - 1) / BK);
+    const int KB = static_cast<int>((g.K + BK - 1) / BK);  // g.K = kb1 * BK + K2 when concatenated
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
@@ -170,7 +178,8 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                 const uint32_t ph = (kb / STAGES) & 1;
                 if (kb >= STAGES && !mbar_wait(&s.empty[st], ph ^ 1, 1)) break;
                 mbar_expect_tx(&s.full[st], STAGE_BYTES);
-                tma_load_2d(s.A[st], &tmA, kb * BK, static_cast<int>(m0), &s.full[st]);
+                if (kb < g.kb1) tma_load_2d(s.A[st], &tmA, kb * BK, static_cast<int>(m0), &s.full[st]);
+                else tma_load_2d(s.A[st], &tmA2, (kb - g.kb1) * BK, static_cast<int>(m0), &s.full[st]);
                 tma_load_2d(s.Bh[st], &tmBh, kb * BK, 0, &s.full[st]);
                 tma_load_2d(s.Bl[st], &tmBl, kb * BK, 0, &s.full[st]);
                 ++issued;
@@ -315,8 +324,9 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                 }
 #pragma unroll 4
                 for (int rr = 0; rr < rows; ++rr) {
-                    const int64_t off = (m0 + q * 32 + rr) * g.ldc;
-                    const float sc = g.rs ? __ldg(g.rs + m0 + q * 32 + rr) : 1.0f;
+                    const int64_t row = m0 + q * 32 + rr;
+                    const int64_t off = row * g.ldc;
+                    const float sc = g.rs ? __ldg(g.rs + row) : 1.0f;
 #pragma unroll
                     for (int k = 0; k < CPL; ++k) {
                         const int col = lane + 32 * k;
@@ -325,6 +335,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                             if (g.rs) v = __fmul_rn(v, sc);
                             if (g.bias) v = __fadd_rn(v, bv[k]);
                             v = apply_act(g.act, v, g.alpha);
+                            if (!PEERS && col >= g.nsplit) {
+                                g.C2[row * g.ldc2 + (col - g.nsplit)] = v;
+                                continue;
+                            }
                             g.C[off + col] = v;
                             if (PEERS)
                                 for (int p = 0; p < peers.n; ++p) peers.c[p][off + col] = v;
@@ -602,15 +616,24 @@ __global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant_
     }
 }
 
-// B (K x N, ld ldb) -> Bt_hi, Bt_lo (N x Kp, K-major), tf32 round-to-nearest split.
-__global__ void split_bt_kernel(const float* B, int64_t ldb, int64_t K, int64_t N, int64_t Kp, float* hi, float* lo) {
+// B (K x N, ld ldb) -> Bt_hi, Bt_lo: rows n < N, columns k < Kseg of a K-major
+// matrix with row stride ldt (zeros for k >= K), tf32 round-to-nearest split.
+__global__ void split_bt_kernel(const float* B, int64_t ldb, int64_t K, int64_t N, int64_t Kseg, int64_t ldt,
+                                float* hi, float* lo) {
     const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (t >= N * Kp) return;
-    const int64_t n = t / Kp, k = t % Kp;
+    if (t >= N * Kseg) return;
+    const int64_t n = t / Kseg, k = t % Kseg;
     const float x = k < K ? B[k * ldb + n] : 0.0f;
     const float h = tf32_rn(x);
-    hi[t] = h;
-    lo[t] = __fsub_rn(x, h);
+    hi[n * ldt + k] = h;
+    lo[n * ldt + k] = __fsub_rn(x, h);
+}
+
+void split_bt(const float* B, int64_t ldb, int64_t K, int64_t N, int64_t Kseg, int64_t ldt, float* hi, float* lo,
+              cudaStream_t s) {
+    if (N * Kseg == 0) return;
+    launch("split_bt", split_bt_kernel, dim3(static_cast<unsigned>(ceil_div(N * Kseg, 256))), dim3(256), 0, s, B, ldb,
+           K, N, Kseg, ldt, hi, lo);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -644,12 +667,13 @@ CUtensorMap make_map(const float* base, int64_t inner, int64_t outer, int64_t ro
 }
 
 template <int BN, int STAGES>
-void launch_tc_s(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g,
-                 const PeerOut& peers, cudaStream_t s) {
+void launch_tc_s(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& bh, const CUtensorMap& bl,
+                 const TcArgs& g, const PeerOut& peers, cudaStream_t s) {
     const size_t smem = sizeof(TcSmem<BN, STAGES>) + 1024;
     auto kern = peers.n > 0 ? gemm_tc_kernel<BN, STAGES, true> : gemm_tc_kernel<BN, STAGES, false>;
     TG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    launch("gemm_tc", kern, dim3(static_cast<unsigned>(ceil_div(g.M, BM))), dim3(192), smem, s, a, bh, bl, g, peers);
+    launch("gemm_tc", kern, dim3(static_cast<unsigned>(ceil_div(g.M, BM))), dim3(192), smem, s, a, a2, bh, bl, g,
+           peers);
 }
 
 constexpr int tcp_stages(int BN) {
@@ -687,12 +711,42 @@ bool use_persistent(bool) {
 // share an SM and one's epilogue overlaps the other's main loop (measured:
 // the K = 128, N = 41 layer-2 GEMM is latency-bound at one CTA per SM).
 template <int BN>
-void launch_tc(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& bl, const TcArgs& g,
-               const PeerOut& peers, cudaStream_t s) {
+void launch_tc(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& bh, const CUtensorMap& bl,
+               const TcArgs& g, const PeerOut& peers, cudaStream_t s) {
     constexpr int kShallow = 2;
     constexpr bool two_fit = 2 * (sizeof(TcSmem<BN, kShallow>) + 1024) <= 227 * 1024;
-    if (two_fit && g.K <= 8 * BK) launch_tc_s<BN, two_fit ? kShallow : stages_for(BN)>(a, bh, bl, g, peers, s);
-    else launch_tc_s<BN, stages_for(BN)>(a, bh, bl, g, peers, s);
+    if (two_fit && g.K <= 8 * BK) launch_tc_s<BN, two_fit ? kShallow : stages_for(BN)>(a, a2, bh, bl, g, peers, s);
+    else launch_tc_s<BN, stages_for(BN)>(a, a2, bh, bl, g, peers, s);
+}
+
+int tile_n(int64_t N) { return N <= 16 ? 16 : N <= 32 ? 32 : N <= 48 ? 48 : N <= 64 ? 64 : N <= 128 ? 128 : 256; }
+
+// Runs the kernel for a prepared B^T (hi at bt, lo at bt + N * ldt) and
+// A maps; g's N, K (and C2 / nsplit / kb1) describe the product.
+void run_tc(const CUtensorMap& ma, const CUtensorMap& ma2, const float* bt, int64_t ldt, const TcArgs& g,
+            const PeerOut& peers, cudaStream_t s) {
+    const int BN = tile_n(g.N);
+    const CUtensorMap mh = make_map(bt, g.K, g.N, ldt, static_cast<uint32_t>(BN));
+    const CUtensorMap ml = make_map(bt + g.N * ldt, g.K, g.N, ldt, static_cast<uint32_t>(BN));
+    if (use_persistent(peers.n > 0) && g.kb1 * BK >= g.K && g.nsplit >= g.N) {
+        switch (BN) {
+            case 16: launch_tcp<16>(ma, mh, ml, g, peers, s); break;
+            case 32: launch_tcp<32>(ma, mh, ml, g, peers, s); break;
+            case 48: launch_tcp<48>(ma, mh, ml, g, peers, s); break;
+            case 64: launch_tcp<64>(ma, mh, ml, g, peers, s); break;
+            case 128: launch_tcp<128>(ma, mh, ml, g, peers, s); break;
+            default: launch_tcp<256>(ma, mh, ml, g, peers, s); break;
+        }
+        return;
+    }
+    switch (BN) {
+        case 16: launch_tc<16>(ma, ma2, mh, ml, g, peers, s); break;
+        case 32: launch_tc<32>(ma, ma2, mh, ml, g, peers, s); break;
+        case 48: launch_tc<48>(ma, ma2, mh, ml, g, peers, s); break;
+        case 64: launch_tc<64>(ma, ma2, mh, ml, g, peers, s); break;
+        case 128: launch_tc<128>(ma, ma2, mh, ml, g, peers, s); break;
+        default: launch_tc<256>(ma, ma2, mh, ml, g, peers, s); break;
+    }
 }
 
 }  // namespace
@@ -705,14 +759,11 @@ void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const
              int64_t ldc, const float* bias, int act, float alpha, cudaStream_t s, const PeerOut& peers,
              bool c_cols_padded, const float* row_scale) {
     if (M == 0 || N == 0) return;
-    const int BN = N <= 16 ? 16 : N <= 32 ? 32 : N <= 48 ? 48 : N <= 64 ? 64 : N <= 128 ? 128 : 256;
+    const int BN = tile_n(N);
     const int64_t Kp = (K + 3) / 4 * 4;
     Scratch<float> bt(static_cast<size_t>(2 * N * Kp), s);
-    launch("split_bt", split_bt_kernel, dim3(static_cast<unsigned>(ceil_div(N * Kp, 256))), dim3(256), 0, s, B, ldb, K,
-           N, Kp, bt.p, bt.p + N * Kp);
+    split_bt(B, ldb, K, N, Kp, Kp, bt.p, bt.p + N * Kp, s);
     const CUtensorMap ma = make_map(A, K, M, lda, BM);
-    const CUtensorMap mh = make_map(bt.p, K, N, Kp, static_cast<uint32_t>(BN));
-    const CUtensorMap ml = make_map(bt.p + N * Kp, K, N, Kp, static_cast<uint32_t>(BN));
     // 16-byte stores (peer copies only) when every output row starts 16-byte
     // aligned and the stored width is a multiple of 4 (N itself, or N padded
     // when the caller's rows have room: those columns receive act(0 + 0)).
@@ -720,26 +771,48 @@ void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const
     bool vec = peers.n > 0 && ldc % 4 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
                (N % 4 == 0 || (c_cols_padded && ldc >= n4));
     for (int p = 0; p < peers.n; ++p) vec = vec && reinterpret_cast<uintptr_t>(peers.c[p]) % 16 == 0;
-    const TcArgs g{C, ldc, M, N, K, bias, act, alpha, vec ? n4 : N, vec ? 1 : 0, row_scale};
-    if (use_persistent(peers.n > 0)) {
-        switch (BN) {
-            case 16: launch_tcp<16>(ma, mh, ml, g, peers, s); break;
-            case 32: launch_tcp<32>(ma, mh, ml, g, peers, s); break;
-            case 48: launch_tcp<48>(ma, mh, ml, g, peers, s); break;
-            case 64: launch_tcp<64>(ma, mh, ml, g, peers, s); break;
-            case 128: launch_tcp<128>(ma, mh, ml, g, peers, s); break;
-            default: launch_tcp<256>(ma, mh, ml, g, peers, s); break;
-        }
-        return;
-    }
-    switch (BN) {
-        case 16: launch_tc<16>(ma, mh, ml, g, peers, s); break;
-        case 32: launch_tc<32>(ma, mh, ml, g, peers, s); break;
-        case 48: launch_tc<48>(ma, mh, ml, g, peers, s); break;
-        case 64: launch_tc<64>(ma, mh, ml, g, peers, s); break;
-        case 128: launch_tc<128>(ma, mh, ml, g, peers, s); break;
-        default: launch_tc<256>(ma, mh, ml, g, peers, s); break;
-    }
+    (void)BN;
+    const TcArgs g{C, ldc, M, N, K, bias, act, alpha, vec ? n4 : N, vec ? 1 : 0, row_scale, nullptr, 0, N,
+                   static_cast<int>(ceil_div(K, BK))};
+    run_tc(ma, ma, bt.p, Kp, g, peers, s);
+}
+
+// C1 = A . B1 and C2 = A . B2 (K x N each) in one pass over A: the product
+// with [B1 | B2] (2N <= 256 columns), its columns split in the epilogue.
+void gemm_tc_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B1, const float* B2,
+                  int64_t ldb, float* C1, int64_t ldc1, float* C2, int64_t ldc2, cudaStream_t s) {
+    if (M == 0 || N == 0) return;
+    const int64_t Kp = (K + 3) / 4 * 4, N2 = 2 * N;
+    Scratch<float> bt(static_cast<size_t>(2 * N2 * Kp), s);
+    float* hi = bt.p;
+    float* lo = bt.p + N2 * Kp;
+    split_bt(B1, ldb, K, N, Kp, Kp, hi, lo, s);                   // rows [0, N) of B^T
+    split_bt(B2, ldb, K, N, Kp, Kp, hi + N * Kp, lo + N * Kp, s); // rows [N, 2N)
+    const CUtensorMap ma = make_map(A, K, M, lda, BM);
+    const TcArgs g{C1, ldc1, M, N2, K, nullptr, TG_ACT_NONE, 0.0f, N2, 0, nullptr, C2, ldc2, N,
+                   static_cast<int>(ceil_div(K, BK))};
+    run_tc(ma, ma, bt.p, Kp, g, PeerOut{}, s);
+}
+
+// C = act([A1 | A2] . [B1; B2] + bias): A1 M x K1, A2 M x K2, B1 K1 x N,
+// B2 K2 x N; the concatenation never exists -- the producer switches tensor
+// maps at k-block kb1 = ceil(K1 / BK) (A1's last block reads zeros past K1,
+// and B1's rows are zero-padded to kb1 * BK).
+void gemm_tc_cat(int64_t M, int64_t N, int64_t K1, const float* A1, int64_t lda1, int64_t K2, const float* A2,
+                 int64_t lda2, const float* B1, int64_t ldb1, const float* B2, int64_t ldb2, float* C, int64_t ldc,
+                 const float* bias, int act, float alpha, cudaStream_t s) {
+    if (M == 0 || N == 0) return;
+    const int kb1 = static_cast<int>(ceil_div(K1, BK));
+    const int64_t K1p = static_cast<int64_t>(kb1) * BK, Kt = K1p + K2, Kp = (Kt + 3) / 4 * 4;
+    Scratch<float> bt(static_cast<size_t>(2 * N * Kp), s);
+    float* hi = bt.p;
+    float* lo = bt.p + N * Kp;
+    split_bt(B1, ldb1, K1, N, K1p, Kp, hi, lo, s);
+    split_bt(B2, ldb2, K2, N, Kp - K1p, Kp, hi + K1p, lo + K1p, s);
+    const CUtensorMap ma1 = make_map(A1, K1, M, lda1, BM);
+    const CUtensorMap ma2 = make_map(A2, K2, M, lda2, BM);
+    const TcArgs g{C, ldc, M, N, Kt, bias, act, alpha, N, 0, nullptr, nullptr, 0, N, kb1};
+    run_tc(ma1, ma2, bt.p, Kp, g, PeerOut{}, s);
 }
 
 // Reads and clears the tensor-core kernels' error word (synchronises `s`).

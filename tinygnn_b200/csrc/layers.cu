@@ -7,9 +7,12 @@
 //       activation in its epilogue.
 //  SAGE (src/layers.cpp:538-752): aggregate-first (mean/max gather into a
 //       scratch, then the interleaved dual product with bias + activation),
-//       bit-identical; or, in FAST mode with F_in > F_out (mean),
-//       transform-first: T = H . [Wn | Ws], then one gather of the Wn half
-//       with the self half, bias and activation fused -- fewer bytes per edge.
+//       bit-identical; FAST does the product as one tensor-core GEMM
+//       [agg | H] . [Wn; Ws] whose operand loads do the concatenation; or,
+//       in FAST mode with F_in > F_out (mean), transform-first: T = H .
+//       [Wn | Ws] in one tensor-core pass over H, then one gather of the Wn
+//       half with the self half, bias and activation fused -- fewer bytes per
+//       edge.
 //  GAT  (src/layers.cpp:945-1129 + src/model.cpp:403-422): gat.cu.
 // ============================================================================
 #include "gather.cuh"
@@ -22,6 +25,11 @@ void gemm(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const fl
 void gemm_dual_exact(int64_t M, int64_t N, int64_t K, const float* A1, int64_t lda1, const float* A2, int64_t lda2,
                      const float* B1, const float* B2, int64_t ldb, float* C, int64_t ldc, const float* bias, int act,
                      float alpha, cudaStream_t s);
+void gemm_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B1, const float* B2,
+               int64_t ldb, float* C1, int64_t ldc1, float* C2, int64_t ldc2, int mode, cudaStream_t s);
+void gemm_cat(int64_t M, int64_t N, int64_t K1, const float* A1, int64_t lda1, int64_t K2, const float* A2,
+              int64_t lda2, const float* B1, int64_t ldb1, const float* B2, int64_t ldb2, float* C, int64_t ldc,
+              const float* bias, int act, float alpha, int mode, cudaStream_t s);
 void gat_layer(int64_t N, int64_t nnz, const int32_t* rp, const int32_t* ci, const float* Hf, int64_t ldh, int64_t F_in, int H,
                int d, const float* W_all, const float* al, const float* ar, const float* bias, float slope,
                bool concat, int act, int post, float* out, int64_t ldo, const int32_t* order, int mode,
@@ -58,16 +66,20 @@ void sage_layer(int64_t N, const int32_t* rp, const int32_t* ci, const float* H,
         if (agg == TG_AGG_MAX) { a.op = GATHER_MAX; a.max_avx_cols = 0; }
         else { a.op = GATHER_SUM; a.mean = 1; }
         gather_rows(a, s);
-        gemm_dual_exact(N, F_out, F_in, A.p, lda, H, ldh, Wn, Ws, F_out, out, ldo, bias, act, 0.0f, s);
+        if (fast)  // [agg | H] . [Wn; Ws] + b on the tensor cores, the concatenation in the operand loads
+            gemm_cat(N, F_out, F_in, A.p, lda, F_in, H, ldh, Wn, F_out, Ws, F_out, out, ldo, bias, act, 0.0f, mode,
+                     s);
+        else       // the reference's interleaved dual product, bit for bit
+            gemm_dual_exact(N, F_out, F_in, A.p, lda, H, ldh, Wn, Ws, F_out, out, ldo, bias, act, 0.0f, s);
         return;
     }
     // Transform first: Tn = H . Wn and Ts = H . Ws (side by side in one
-    // padded buffer), then out_i = act(mean_j Tn[j] + Ts[i] + b).
+    // padded buffer, one tensor-core pass over H), then
+    // out_i = act(mean_j Tn[j] + Ts[i] + b).
     const int64_t half = pad4(F_out);
     const int64_t ldt = 2 * half;
     Scratch<float> T(static_cast<size_t>(N * ldt), s);
-    gemm(N, F_out, F_in, H, ldh, Wn, F_out, T.p, ldt, nullptr, TG_ACT_NONE, 0.0f, mode, s);
-    gemm(N, F_out, F_in, H, ldh, Ws, F_out, T.p + half, ldt, nullptr, TG_ACT_NONE, 0.0f, mode, s);
+    gemm_pair(N, F_out, F_in, H, ldh, Wn, Ws, F_out, T.p, ldt, T.p + half, ldt, mode, s);
     GatherArgs a;
     a.M = N; a.rp = rp; a.ci = ci; a.order = order;
     a.B = T.p; a.ldb = ldt; a.b_padded = true; a.F = F_out;

@@ -140,6 +140,32 @@ def matmul(A: torch.Tensor, B: torch.Tensor, bias=None, act=None, alpha: float =
     return out
 
 
+def gemm_pair(A: torch.Tensor, B1: torch.Tensor, B2: torch.Tensor, out1: torch.Tensor, out2: torch.Tensor,
+              mode: str = "fast"):
+    """out1 = A . B1, out2 = A . B2 (one tensor-core pass over A in FAST mode)."""
+    A, B1, B2 = _dense(A, "A"), _dense(B1, "B1").contiguous(), _dense(B2, "B2").contiguous()
+    M, K = A.shape
+    N = B1.shape[1]
+    check(lib.tg_gemm_pair_f32(M, N, K, _p(A), _ld(A), _p(B1), _p(B2), N, _p(out1), _ld(out1), _p(out2), _ld(out2),
+                               MODE[mode], _stream()))
+    return out1, out2
+
+
+def gemm_cat(A1: torch.Tensor, A2: torch.Tensor, B1: torch.Tensor, B2: torch.Tensor, bias=None, act=None,
+             alpha: float = 0.0, out: Optional[torch.Tensor] = None, mode: str = "fast") -> torch.Tensor:
+    """C = act([A1 | A2] . [B1; B2] + bias) without forming the concatenation."""
+    A1, A2 = _dense(A1, "A1"), _dense(A2, "A2")
+    B1, B2 = _dense(B1, "B1"), _dense(B2, "B2")
+    M, K1 = A1.shape
+    K2, N = A2.shape[1], B1.shape[1]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=A1.device)
+    b = _vec(bias)
+    check(lib.tg_gemm_cat_f32(M, N, K1, _p(A1), _ld(A1), K2, _p(A2), _ld(A2), _p(B1), _ld(B1), _p(B2), _ld(B2),
+                              _p(out), _ld(out), _p(b), ACT[act], alpha, MODE[mode], _stream()))
+    return out
+
+
 def gemm_dual(A1, A2, B1, B2, bias=None, act=None, out=None) -> torch.Tensor:
     """C = interleaved A1.B1 + A2.B2 (SAGE's fused dual GEMV order)."""
     A1, A2, B1, B2 = _dense(A1, "A1"), _dense(A2, "A2"), _dense(B1, "B1"), _dense(B2, "B2")
