@@ -553,19 +553,79 @@ def run_ours(args):
     h_out = torch.empty((rows, CLASSES), dtype=torch.float32).pin_memory()
     e2e_bufs = {}
 
-    def e2e_step():
-        # the public call: host CSR rows + feature rows in, host logits out
+    def e2e_sharded_step():
+        # the row-partitioned Python API: this rank's host CSR rows + feature
+        # rows in, host logits out, uploads pipelined with the compute
         model.forward_from_host(h_rp, h_ci, h_v, h_X, h_out, e2e_bufs)
 
+    # At one GPU, e2e goes through the drop-in boundary a TinyGNN caller
+    # binds: the handle C ABI (tg_tensor_create_csr / _dense from the pinned
+    # host buffers, tg_model_forward = Model::forward, tg_tensor_download of
+    # the logits), every step, each call complete before it returns.
+    hmodel = None
+    h_Xc = None
+    if world == 1 and not args.no_e2e:
+        from tinygnn_b200.handles import HModel, HTensor, set_fast_math
+        prev_fast = set_fast_math(args.mode == "fast")
+        hmodel = HModel()
+        for L in ref_spec(args.workload):
+            if L["type"] == "gcn":
+                hmodel.add_gcn(L["in"], L["out"], act=L.get("act"))
+            else:
+                hmodel.add_sage(L["in"], L["out"], act=L.get("act"))
+        hmodel.load_weights({k: t.cpu().numpy() for k, t in w.items()})
+        h_Xc = X.contiguous().cpu().pin_memory()  # rows of 602 floats, as a caller holds them
+        h_out_api = torch.empty((rows, CLASSES), dtype=torch.float32).pin_memory()
+
+        parts = {"upload_csr": 0.0, "upload_features": 0.0, "forward": 0.0, "download": 0.0, "free": 0.0}
+
+        def e2e_step():
+            # each handle call completes before it returns: host timestamps time it
+            t0 = time.perf_counter()
+            A_t = HTensor.csr(n, n, h_rp, h_ci, h_v)
+            t1 = time.perf_counter()
+            X_t = HTensor.dense(h_Xc, n, FEATS)
+            t2 = time.perf_counter()
+            Y = hmodel.forward(A_t, X_t)
+            Y.download(h_out_api)  # the forward's kernels finish inside this call
+            t3 = time.perf_counter()
+            for t in (Y, X_t, A_t):
+                t.free()
+            t4 = time.perf_counter()
+            parts["upload_csr"] += t1 - t0
+            parts["upload_features"] += t2 - t1
+            parts["forward"] += t3 - t2
+            parts["free"] += t4 - t3
+    else:
+        e2e_step = e2e_sharded_step
+
     e2e_ms = None if args.no_e2e else time_steps(e2e_step, args.steps, min(args.warmup, 3), world)
+    e2e_parts = None
+    if hmodel is not None:  # per timed step (the warm-up steps are in the sums too)
+        calls = args.steps + min(args.warmup, 3)
+        e2e_parts = {k: v / calls * 1e3 for k, v in parts.items() if k != "download"}
+        e2e_parts["forward+download"] = e2e_parts.pop("forward")
+    e2e_sharded_ms = None
+    if hmodel is not None:
+        set_fast_math(prev_fast)
+        e2e_sharded_ms = time_steps(e2e_sharded_step, args.steps, min(args.warmup, 3), world)
     clocks = sampler.stop()
     h2d = (h_rp.numel() + h_ci.numel()) * 4 + (0 if h_v is None else h_v.numel() * 4) + h_X.numel() * 4
     d2h = h_out.numel() * 4
 
     # parity spot check of the e2e logits against the device-resident run
+    # (the ShardedModel path bit for bit; the handle path -- a different
+    # kernel schedule for the same arithmetic -- within the fp32 tolerance)
     ref_out = model.forward_prepared(prepared, X)
     torch.cuda.synchronize()
     e2e_matches = None if args.no_e2e else bool(torch.equal(ref_out.cpu(), h_out))
+    sharded_ms = e2e_sharded_ms if hmodel is not None else e2e_ms
+    api_close = None
+    if hmodel is not None:
+        logits_ref = torch.log_softmax(ref_out.cpu().double(), 1)
+        logits_api = torch.log_softmax(h_out_api.double(), 1)
+        api_close = bool(((logits_api - logits_ref).abs() <= 1e-5 + 1e-4 * logits_ref.abs()).all())
+        hmodel.free()
 
     # roofline of the layer-1 gather (rank-local)
     F = HIDDEN
@@ -627,10 +687,20 @@ def run_ours(args):
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "edges/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": None if e2e_ms is None else e2e_ms / args.steps,
-                    "logits_match_resident_run": e2e_matches,
+                    "api": ("handle C ABI: tg_tensor_create_csr + tg_tensor_create_dense from pinned host buffers, "
+                            "tg_model_forward (Model::forward, gcn_norm inside), tg_tensor_download of the logits"
+                            if hmodel is not None else
+                            "tinygnn_b200.dist.ShardedModel.forward_from_host: this rank's pinned host rows in, "
+                            "host logits out"),
+                    "log_softmax_within_tolerance_of_resident_run": api_close,
+                    "call_ms": e2e_parts,
                     "inputs": ("unweighted CSR: row_ptr + col_ind uploaded, values 1.0 written on the device"
                                if h_v is None else "CSR row_ptr + col_ind + values") + ", features fp32",
                     "note": "rank 0's bytes; every rank moves its own row block"},
+            "e2e_sharded_pipelined": None if sharded_ms is None else {
+                "value": nnz_total / (sharded_ms / args.steps * 1e-3), "unit": "edges/s",
+                "ms_per_step": sharded_ms / args.steps, "logits_match_resident_run": e2e_matches,
+                "api": "tinygnn_b200.dist.ShardedModel.forward_from_host (uploads overlapped with the compute)"},
             "step": ("Model::forward: gcn_norm of the raw adjacency, its row schedule, both layers, log_softmax"
                      if args.workload == "gcn" else
                      "Model::forward: the raw adjacency's row schedule, both layers, log_softmax"),

@@ -13,9 +13,10 @@
  *      Dense matrices are row-major with an explicit leading dimension (ld,
  *      in elements, >= the logical column count).  Results match the
  *      TinyGNN CPU library bit for bit where the entry point says "exact".
- *   2. Handle entry points (tg_tensor_*, tg_model_*), the surface TinyGNN's
- *      own binding (python/tinygnn_ext.cpp) exposes: tensors built from host
- *      arrays, layers/Model, forward on host inputs.
+ *   2. Handle entry points (tg_tensor_*, tg_model_*, at the end of this
+ *      file), the surface TinyGNN's own binding (python/tinygnn_ext.cpp)
+ *      exposes: tensors built from host arrays, Model, forward on host
+ *      inputs, logits back to the host.
  *
  *  References are to TinyGNN source files, path:line.
  * ========================================================================== */
@@ -47,7 +48,7 @@ typedef enum tg_status {
     TG_ERR_CUDA = 4,             /* a CUDA runtime call failed */
     TG_ERR_NCCL = 5,             /* a collective failed */
     TG_ERR_TIMEOUT = 6,          /* a bounded device or host wait ran out */
-    TG_ERR_DEVICE_CHECK = 7,     /* an in-kernel input check failed */
+    TG_ERR_DEVICE_CHECK = 7,     /* reserved (input checks report TG_ERR_INVALID_ARGUMENT) */
     TG_ERR_NO_DEVICE = 8         /* no CUDA device (the library has no CPU path) */
 } tg_status;
 
@@ -473,6 +474,65 @@ TG_API tg_status tg_wait_flags(const uint64_t* flags, const uint64_t* targets, i
  * when one of their bounded waits ran out since the last call (that call's
  * output is then invalid).  Synchronises `stream`. */
 TG_API tg_status tg_take_device_error(void* stream);
+
+/* ── handles: TinyGNN's Tensor and Model over the C ABI ─────────────────── */
+/* The drop-in API (the headers in include/tinygnn: Tensor, Model, layers) behind
+ * opaque handles, for callers that bind C rather than C++ -- the surface of
+ * TinyGNN's own Python binding (python/tinygnn_ext.cpp:195-452: tensors from
+ * host arrays, Model construction, load_weights, forward).  Host buffers are
+ * read or written only inside the call; every call here completes (and
+ * synchronises the calling thread's stream) before it returns.  Calls run on
+ * the current CUDA device. */
+typedef struct tg_tensor_s* tg_tensor;
+typedef struct tg_model_s* tg_model;
+
+/* Tensor::dense (include/tinygnn/tensor.hpp) from host rows of stride ld
+ * (host NULL: zeros). */
+TG_API tg_status tg_tensor_create_dense(int64_t rows, int64_t cols, const float* host, int64_t ld,
+                                        tg_tensor* out);
+/* Tensor::sparse_csr (src/tensor.cpp:142-182) from host arrays: row_ptr
+ * [rows+1], col_ind [nnz], values [nnz] (NULL: every value 1.0, an
+ * unweighted graph).  Checked on the device after the upload with the
+ * reference's checks and messages (TG_ERR_INVALID_ARGUMENT). */
+TG_API tg_status tg_tensor_create_csr(int64_t rows, int64_t cols, int64_t nnz, const int32_t* row_ptr,
+                                      const int32_t* col_ind, const float* values, tg_tensor* out);
+/* A dense tensor's values into host rows of stride ld. */
+TG_API tg_status tg_tensor_download(tg_tensor t, float* host, int64_t ld);
+/* rows, cols, nnz (rows*cols for dense) and format (1 = SparseCSR); each
+ * pointer nullable. */
+TG_API tg_status tg_tensor_shape(tg_tensor t, int64_t* rows, int64_t* cols, int64_t* nnz,
+                                 int32_t* is_csr);
+TG_API void tg_tensor_free(tg_tensor t);
+
+/* Model (src/model.cpp:191-439).  act: TG_ACT_NONE or TG_ACT_RELU (the
+ * layers' Activation); post: 0 none, 1 ReLU, 2 ELU (Model::InterActivation);
+ * aggregator: TG_AGG_MEAN / TG_AGG_MAX. */
+TG_API tg_status tg_model_create(tg_model* out);
+TG_API tg_status tg_model_add_gcn(tg_model m, int64_t in_f, int64_t out_f, int32_t bias, int32_t act,
+                                  int32_t post);
+TG_API tg_status tg_model_add_sage(tg_model m, int64_t in_f, int64_t out_f, int32_t aggregator,
+                                   int32_t bias, int32_t act, int32_t post);
+TG_API tg_status tg_model_add_gat(tg_model m, int64_t in_f, int64_t out_f, int64_t heads,
+                                  int32_t concat, float slope, int32_t bias, int32_t act,
+                                  int32_t post);
+/* Model::load_weights from a TGNN file (src/model.cpp:134-185, 258-305). */
+TG_API tg_status tg_model_load_weights_file(tg_model m, const char* path);
+/* Model::load_weights from named host tensors (the TGNN names
+ * "layer{i}.weight" ..., rows x cols each, row-major). */
+TG_API tg_status tg_model_load_weights(tg_model m, int32_t count, const char* const* names,
+                                       const float* const* data, const int64_t* rows,
+                                       const int64_t* cols);
+/* Model::forward(adjacency, features) -> *out (a new dense tensor): raw
+ * adjacency without self-loops; gcn_norm / add_self_loops once per call like
+ * the reference.  With tg_set_fast_math(1) the GCN layers run on the raw
+ * adjacency with gcn_norm as per-row scale factors (tg_gcn_aggregate_f32)
+ * and the GEMMs on the tensor cores, within the fp32 tolerance; otherwise
+ * bit-identical to the reference. */
+TG_API tg_status tg_model_forward(tg_model m, tg_tensor adjacency, tg_tensor features, tg_tensor* out);
+TG_API void tg_model_free(tg_model m);
+/* FAST (1) or EXACT (0) arithmetic for the handle and C++ APIs, process-wide;
+ * returns the previous setting (tinygnn::set_fast_math). */
+TG_API int32_t tg_set_fast_math(int32_t fast);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -78,3 +78,21 @@ def test_compute_call_without_device_reports_no_device():
     st = _lib.lib.tg_gemm_f32(1, 1, 1, None, 1, None, 1, None, 1, None, 0, 0.0, 0, None)
     assert st == _lib.NO_DEVICE
     assert "no CUDA device" in _lib.last_error()
+
+
+def test_handle_calls_without_device_report_no_device():
+    """The handle C ABI (tg_tensor_* / tg_model_*) has no CPU path either."""
+    import ctypes as C
+    from tinygnn_b200 import _lib
+    if _lib.lib.tg_device_count() > 0:
+        pytest.skip("a device is present")
+    h = C.c_void_p()
+    rp = (C.c_int32 * 2)(0, 0)
+    assert _lib.lib.tg_tensor_create_csr(1, 1, 0, C.cast(rp, C.c_void_p), None, None, C.byref(h)) == _lib.NO_DEVICE
+    assert _lib.lib.tg_tensor_create_dense(2, 2, None, 2, C.byref(h)) == _lib.NO_DEVICE
+    assert "no CUDA device" in _lib.last_error()
+    m = C.c_void_p()
+    assert _lib.lib.tg_model_create(C.byref(m)) == _lib.OK  # host-side object
+    assert _lib.lib.tg_model_add_gcn(m, 4, 2, 1, _lib.ACT_RELU, 0) == _lib.OK
+    assert _lib.lib.tg_model_add_gcn(m, 0, 2, 1, _lib.ACT_RELU, 0) == _lib.INVALID_ARGUMENT
+    _lib.lib.tg_model_free(m)

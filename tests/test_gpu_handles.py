@@ -1,0 +1,108 @@
+"""The handle C ABI (tg_tensor_* / tg_model_*): TinyGNN's Tensor and Model
+driven through C with host buffers, checked against the oracle's
+Model::forward + log_softmax -- bit for bit in EXACT mode, within the fp32
+tolerance in FAST mode -- and malformed input refused with the reference's
+message."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from tests.helpers import assert_bits_equal, assert_close, powerlaw_csr
+
+pytestmark = pytest.mark.gpu
+P = oracle.port
+
+
+def _glorot(rng, i, o):
+    r = np.sqrt(6.0 / (i + o))
+    return rng.uniform(-r, r, (i, o)).astype(np.float32)
+
+
+def _spec_weights(rng, kind, fin):
+    if kind == "gcn":
+        spec = [dict(type="gcn", **{"in": fin, "out": 24}, act="relu"), dict(type="gcn", **{"in": 24, "out": 7})]
+        w = {"layer0.weight": _glorot(rng, fin, 24), "layer0.bias": rng.standard_normal(24).astype(np.float32) * .1,
+             "layer1.weight": _glorot(rng, 24, 7), "layer1.bias": rng.standard_normal(7).astype(np.float32) * .1}
+    elif kind == "sage":
+        spec = [dict(type="sage", **{"in": fin, "out": 24}, act="relu"), dict(type="sage", **{"in": 24, "out": 7})]
+        w = {"layer0.weight_neigh": _glorot(rng, fin, 24), "layer0.weight_self": _glorot(rng, fin, 24),
+             "layer0.bias": rng.standard_normal(24).astype(np.float32) * .1,
+             "layer1.weight_neigh": _glorot(rng, 24, 7), "layer1.weight_self": _glorot(rng, 24, 7),
+             "layer1.bias": rng.standard_normal(7).astype(np.float32) * .1}
+    else:
+        spec = [dict(type="gat", **{"in": fin, "out": 8}, heads=3, concat=True, post="elu"),
+                dict(type="gat", **{"in": 24, "out": 7}, heads=1)]
+        w = {}
+        for h in range(3):
+            w[f"layer0.head{h}.weight"] = _glorot(rng, fin, 8)
+            w[f"layer0.head{h}.attn_left"] = rng.standard_normal(8).astype(np.float32) * .5
+            w[f"layer0.head{h}.attn_right"] = rng.standard_normal(8).astype(np.float32) * .5
+            w[f"layer0.head{h}.bias"] = rng.standard_normal(8).astype(np.float32) * .1
+        w.update({"layer1.head0.weight": _glorot(rng, 24, 7),
+                  "layer1.head0.attn_left": rng.standard_normal(7).astype(np.float32) * .5,
+                  "layer1.head0.attn_right": rng.standard_normal(7).astype(np.float32) * .5,
+                  "layer1.head0.bias": rng.standard_normal(7).astype(np.float32) * .1})
+    return spec, w
+
+
+def _build(spec, w):
+    from tinygnn_b200.handles import HModel
+    m = HModel()
+    for L in spec:
+        if L["type"] == "gcn":
+            m.add_gcn(L["in"], L["out"], act=L.get("act"))
+        elif L["type"] == "sage":
+            m.add_sage(L["in"], L["out"], act=L.get("act"))
+        else:
+            m.add_gat(L["in"], L["out"], heads=L.get("heads", 1), concat=L.get("concat", True), post=L.get("post"))
+    m.load_weights(w)
+    return m
+
+
+@pytest.mark.parametrize("kind", ["gcn", "sage", "gat"])
+@pytest.mark.parametrize("fast", [False, True])
+@pytest.mark.parametrize("weighted", [False, True])
+def test_handle_model_forward_vs_oracle(kind, fast, weighted):
+    import tinygnn_b200 as tg
+    from tinygnn_b200.handles import HTensor, set_fast_math
+    rng = np.random.default_rng(len(kind) * 10 + fast * 2 + weighted)
+    n, fin = 6000, 40
+    rp, ci, v = powerlaw_csr(rng, n, 9, weighted=weighted, diag=False)
+    X = rng.standard_normal((n, fin)).astype(np.float32)
+    spec, w = _spec_weights(rng, kind, fin)
+    prev = set_fast_math(fast)
+    try:
+        m = _build(spec, w)
+        A = HTensor.csr(n, n, rp, ci, v if weighted else None)  # unweighted: values written on the device
+        assert A.shape() == (n, n, ci.size, True)
+        Xt = HTensor.dense(X, n, fin)
+        logits = m.forward(A, Xt).download()
+        tg.ops.take_device_error()
+    finally:
+        set_fast_math(prev)
+    ref = oracle.model_forward(P, spec, w, rp, ci, v, X)
+    if fast or kind == "gat":  # GAT's softmax goes through expf: the fp32 tolerance in either mode
+        assert_close(P.activation("log_softmax", logits), P.activation("log_softmax", ref), f"{kind} fast={fast}")
+    else:
+        assert_bits_equal(logits, ref, f"{kind} exact")
+
+
+def test_handle_tensors_from_pinned_torch_and_errors():
+    """Pinned torch host tensors are accepted as host buffers; a malformed CSR
+    is refused after its upload with the reference's message."""
+    from tinygnn_b200 import _lib
+    from tinygnn_b200.handles import HTensor
+    X = torch.randn(100, 12).pin_memory()
+    t = HTensor.dense(X, 100, 12)
+    out = torch.empty(100, 12).pin_memory()
+    t.download(out)
+    assert torch.equal(out, X)
+    rp = torch.tensor([0, 1, 3], dtype=torch.int32).pin_memory()
+    ci = torch.tensor([0, 5, 1], dtype=torch.int32).pin_memory()
+    with pytest.raises(ValueError, match=r"col_ind\[1\] = 5 is out of bounds for cols=2"):
+        HTensor.csr(2, 2, rp, ci)
+    rp_bad = np.array([0, 2, 1], np.int32)
+    with pytest.raises(ValueError, match=r"row_ptr must be non-decreasing"):
+        HTensor.csr(2, 2, rp_bad, np.array([0, 1], np.int32))
+    assert _lib.lib.tg_tensor_download(None, None, 0) == _lib.INVALID_ARGUMENT

@@ -67,6 +67,20 @@ SIGNATURES = {
     "tg_gcn_norm_rows_degrees_f32": (i32, [i64, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp]),
     "tg_gcn_norm_rows_fill_f32": (i32, [i64, i64, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "tg_set_csr_checks": (i32, [i32]),
+    "tg_tensor_create_dense": (i32, [i64, i64, vp, i64, C.POINTER(vp)]),
+    "tg_tensor_create_csr": (i32, [i64, i64, i64, vp, vp, vp, C.POINTER(vp)]),
+    "tg_tensor_download": (i32, [vp, vp, i64]),
+    "tg_tensor_shape": (i32, [vp, P64, P64, P64, C.POINTER(i32)]),
+    "tg_tensor_free": (None, [vp]),
+    "tg_model_create": (i32, [C.POINTER(vp)]),
+    "tg_model_add_gcn": (i32, [vp, i64, i64, i32, i32, i32]),
+    "tg_model_add_sage": (i32, [vp, i64, i64, i32, i32, i32, i32]),
+    "tg_model_add_gat": (i32, [vp, i64, i64, i64, i32, f32, i32, i32, i32]),
+    "tg_model_load_weights_file": (i32, [vp, C.c_char_p]),
+    "tg_model_load_weights": (i32, [vp, i32, C.POINTER(C.c_char_p), C.POINTER(vp), P64, P64]),
+    "tg_model_forward": (i32, [vp, vp, vp, C.POINTER(vp)]),
+    "tg_model_free": (None, [vp]),
+    "tg_set_fast_math": (i32, [i32]),
     "tg_gcn_layer_f32": (i32, [i64, i64, vp, vp, vp, vp, i64, i64, i64, vp, vp, i32, vp, i64, vp, i32, vp]),
     "tg_sage_layer_f32": (i32, [i64, i64, vp, vp, vp, i64, i64, i64, vp, vp, vp, i32, i32, vp, i64, vp, i32, vp]),
     "tg_gat_layer_f32": (i32, [i64, i64, vp, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp, f32, i32, i32, vp, i64,

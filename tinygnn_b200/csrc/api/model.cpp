@@ -12,7 +12,10 @@
 // ============================================================================
 #include "tinygnn/model.hpp"
 
+#include <algorithm>
 #include <cstring>
+#include <memory>
+#include <utility>
 #include <fstream>
 
 #include "internal.hpp"
@@ -181,6 +184,99 @@ void Model::load_weights(const WeightFile& wf) {
     }
 }
 
+namespace {
+
+// A device int32 buffer from the stream-ordered pool.
+struct DevInts {
+    int32_t* p = nullptr;
+    explicit DevInts(std::size_t n) {
+        void* q = nullptr;
+        detail::cuda(cudaMallocAsync(&q, (n ? n : 1) * sizeof(int32_t), detail::cstream()), "tinygnn allocation");
+        p = static_cast<int32_t*>(q);
+    }
+    ~DevInts() {
+        if (p && cudaFreeAsync(p, detail::cstream()) != cudaSuccess) cudaGetLastError();
+    }
+    DevInts(const DevInts&) = delete;
+    DevInts& operator=(const DevInts&) = delete;
+};
+
+// The raw adjacency prepared once per forward for FAST GCN layers without a
+// normalised copy: dis[i] = 1/sqrt(row sum + 1) (tg_gcn_norm_scale_f32), a
+// longest-first row schedule, and column splits per pass count.
+struct ScaledGraph {
+    const Tensor& A;
+    std::size_t n;
+    DevBuf dis;
+    DevInts order;
+    std::vector<std::pair<int, std::unique_ptr<DevInts>>> splits;
+
+    explicit ScaledGraph(const Tensor& adj) : A(adj), n(adj.rows()), dis(adj.rows()), order(adj.rows()) {
+        const detail::TrustedCsr trusted_csr;
+        check(tg_gcn_norm_scale_f32(static_cast<int64_t>(n), static_cast<int64_t>(A.nnz()), A.device_row_ptr(),
+                                    A.device_data(), dis.p, stream()));
+        check(tg_csr_degree_order(static_cast<int64_t>(n), A.device_row_ptr(), order.p, stream()));
+    }
+
+    const int32_t* split_points(int passes) {
+        for (auto& sp : splits)
+            if (sp.first == passes) return sp.second->p;
+        auto buf = std::make_unique<DevInts>(n * static_cast<std::size_t>(passes + 1));
+        const detail::TrustedCsr trusted_csr;
+        check(tg_csr_column_splits(static_cast<int64_t>(n), A.device_row_ptr(), A.device_col_ind(), passes,
+                                   static_cast<int64_t>((n + passes - 1) / passes), buf->p, stream()));
+        splits.emplace_back(passes, std::move(buf));
+        return splits.back().second->p;
+    }
+};
+
+// A gathered operand above this size is aggregated in column-block passes
+// (each pass's slice of the operand stays in L2; measured on B200 for the
+// 119 MB Reddit-shaped layer-1 operand: 2 passes, -6 %).
+constexpr std::size_t kPassBytes = std::size_t(64) << 20;
+
+// GCNLayer::forward on the raw adjacency in FAST mode: Hs = diag(dis) . (H . W)
+// on the tensor cores, then out = act(dis * (A . Hs + Hs_self) + b) in
+// stored order -- D^-1/2 (A + I) D^-1/2 . HW without the normalised copy.
+Tensor gcn_forward_scaled(const GCNLayer& L, ScaledGraph& g, const Tensor& H) {
+    if (H.format() != StorageFormat::Dense)
+        throw std::invalid_argument("GCNLayer::forward: H must be Dense (got SparseCSR).");
+    if (H.cols() != L.in_features())
+        throw std::invalid_argument("GCNLayer::forward: H has " + std::to_string(H.cols()) +
+                                    " columns but layer expects in_features=" + std::to_string(L.in_features()) +
+                                    ".");
+    if (g.n != H.rows())
+        throw std::invalid_argument("GCNLayer::forward: A_norm has " + std::to_string(g.n) + " rows but H has " +
+                                    std::to_string(H.rows()) + " rows. They must match (N nodes).");
+    const std::size_t N = g.n, Fo = L.out_features();
+    Tensor out = Tensor::dense_device(N, Fo);
+    if (N == 0) return out;
+    Tensor Hs = Tensor::dense_device(N, Fo);  // rows padded to 16 bytes; the padding stays 0
+    check(tg_gemm_rowscale_f32(static_cast<int64_t>(N), static_cast<int64_t>(Fo),
+                               static_cast<int64_t>(L.in_features()), H.device_data(),
+                               static_cast<int64_t>(H.device_ld()), L.weight().device_data(),
+                               static_cast<int64_t>(L.weight().device_ld()), Hs.mutable_device_data(),
+                               static_cast<int64_t>(Hs.device_ld()), g.dis.p, nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST,
+                               stream()));
+    const int passes = static_cast<int>(
+        std::max<std::size_t>(1, (N * Hs.device_ld() * sizeof(float) + kPassBytes - 1) / kPassBytes));
+    const int32_t* sp = passes > 1 ? g.split_points(passes) : nullptr;
+    const detail::TrustedCsr trusted_csr;
+    for (int q = 0; q < passes; ++q)
+        check(tg_gcn_aggregate_f32(
+            static_cast<int64_t>(N), static_cast<int64_t>(N), static_cast<int64_t>(g.A.nnz()), g.A.device_row_ptr(),
+            g.A.device_col_ind(), g.A.device_data(), Hs.device_data(), static_cast<int64_t>(Fo),
+            static_cast<int64_t>(Hs.device_ld()), Hs.device_data(), static_cast<int64_t>(Hs.device_ld()), g.dis.p,
+            L.has_bias() ? L.bias().device_data() : nullptr,
+            L.activation() == Activation::ReLU ? TG_ACT_RELU : TG_ACT_NONE, out.mutable_device_data(),
+            static_cast<int64_t>(out.device_ld()), g.order.p, sp ? sp + static_cast<std::size_t>(q) * N : nullptr,
+            sp ? sp + static_cast<std::size_t>(q + 1) * N : nullptr, q > 0, q == passes - 1, TG_FLAG_B_ROWS_PADDED,
+            stream()));
+    return out;
+}
+
+}  // namespace
+
 Tensor Model::forward(const Tensor& adjacency, const Tensor& features) const {
     if (layers_.empty()) throw std::runtime_error("Model::forward: no layers configured.");
     bool need_norm = false, need_sl = false;
@@ -188,8 +284,23 @@ Tensor Model::forward(const Tensor& adjacency, const Tensor& features) const {
         need_norm |= e.type == LayerEntry::Type::GCN;
         need_sl |= e.type == LayerEntry::Type::GAT;
     }
+    // EXACT (the default): gcn_norm once per call, bit for bit, like the
+    // reference (src/model.cpp:365-381).  FAST: the GCN layers run on the raw
+    // adjacency with gcn_norm as per-row scale factors (within the fp32
+    // tolerance); the same validation as gcn_norm's.
+    const bool scaled = need_norm && fast_math();
+    std::unique_ptr<ScaledGraph> sg;
     Tensor A_gcn, A_sl;
-    if (need_norm) A_gcn = gcn_norm(adjacency);
+    if (scaled) {
+        if (adjacency.format() != StorageFormat::SparseCSR)
+            throw std::invalid_argument("gcn_norm: A must be SparseCSR (got Dense).");
+        if (adjacency.rows() != adjacency.cols())
+            throw std::invalid_argument("gcn_norm: A must be square \xE2\x80\x94 got " +
+                                        detail::shape_str(adjacency.rows(), adjacency.cols()) + ".");
+        sg = std::make_unique<ScaledGraph>(adjacency);
+    } else if (need_norm) {
+        A_gcn = gcn_norm(adjacency);
+    }
     if (need_sl) A_sl = add_self_loops(adjacency);
 
     Tensor H;
@@ -197,7 +308,10 @@ Tensor Model::forward(const Tensor& adjacency, const Tensor& features) const {
     for (const auto& e : layers_) {
         Tensor out;
         switch (e.type) {
-            case LayerEntry::Type::GCN: out = gcn_layers_[e.start_idx].forward(A_gcn, *in); break;
+            case LayerEntry::Type::GCN:
+                out = scaled ? gcn_forward_scaled(gcn_layers_[e.start_idx], *sg, *in)
+                             : gcn_layers_[e.start_idx].forward(A_gcn, *in);
+                break;
             case LayerEntry::Type::SAGE: out = sage_layers_[e.start_idx].forward(adjacency, *in); break;
             case LayerEntry::Type::GAT: {
                 if (e.count == 1) {

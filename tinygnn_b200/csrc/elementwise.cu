@@ -9,6 +9,8 @@
 //  last bits of expf/logf.  These passes are HBM-bound; on the layer path
 //  they are fused into the producing kernel's epilogue instead.
 // ============================================================================
+#include <algorithm>
+
 #include "launch.cuh"
 
 namespace tg {
@@ -192,6 +194,20 @@ void row_softmax(bool log, float* X, int64_t rows, int64_t cols, int64_t ld, cud
     }
     if (log) launch("log_softmax", row_softmax_kernel<true>, grid, dim3(128), 0, s, X, rows, cols, ld);
     else launch("softmax", row_softmax_kernel<false>, grid, dim3(128), 0, s, X, rows, cols, ld);
+}
+
+namespace {
+__global__ void fill_kernel(float* p, int64_t n, float v) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < n; t += stride) p[t] = v;
+}
+}  // namespace
+
+// p[0..n) = v, queued on s (the values of an unweighted CSR).
+void fill_f32(float* p, int64_t n, float v, cudaStream_t s) {
+    if (n <= 0) return;
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(ceil_div(n, 256), 8 * num_sms()));
+    launch("fill", fill_kernel, dim3(grid), dim3(256), 0, s, p, n, v);
 }
 
 }  // namespace tg

@@ -1,0 +1,136 @@
+"""Python side of the handle C ABI (tg_tensor_* / tg_model_*).
+
+TinyGNN's drop-in Tensor and Model driven through the C ABI with host
+buffers, as a caller binding C would: tensors uploaded from host arrays
+(numpy or torch CPU tensors; pinned memory uploads at full PCIe rate), a
+Model built layer by layer with named weights, forward, logits downloaded
+into a host array.  Every call completes before it returns.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Dict, Optional
+
+import numpy as np
+
+from . import _lib
+from ._lib import check, lib
+
+
+def _ptr(a) -> Optional[int]:
+    """Host address of a C-contiguous numpy array or torch CPU tensor (None passes NULL)."""
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+class HTensor:
+    """A tg_tensor: TinyGNN's Tensor in device memory, owned by this object."""
+
+    def __init__(self, handle: C.c_void_p):
+        self.h = handle
+
+    @classmethod
+    def dense(cls, host, rows: int, cols: int, ld: Optional[int] = None) -> "HTensor":
+        h = C.c_void_p()
+        check(lib.tg_tensor_create_dense(rows, cols, _ptr(host), cols if ld is None else ld, C.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def csr(cls, rows: int, cols: int, row_ptr, col_ind, values=None) -> "HTensor":
+        """From host row_ptr / col_ind (int32) and values (float32; None = all 1.0)."""
+        nnz = int(row_ptr[rows]) if rows else 0
+        h = C.c_void_p()
+        check(lib.tg_tensor_create_csr(rows, cols, nnz, _ptr(row_ptr), _ptr(col_ind), _ptr(values), C.byref(h)))
+        return cls(h)
+
+    def shape(self):
+        r, c, n = C.c_int64(), C.c_int64(), C.c_int64()
+        f = C.c_int32()
+        check(lib.tg_tensor_shape(self.h, C.byref(r), C.byref(c), C.byref(n), C.byref(f)))
+        return r.value, c.value, n.value, bool(f.value)
+
+    def download(self, out=None):
+        """The values into ``out`` (a host float32 rows x cols array or tensor) or a new numpy array."""
+        rows, cols, _, _ = self.shape()
+        if out is None:
+            out = np.empty((rows, cols), np.float32)
+        check(lib.tg_tensor_download(self.h, _ptr(out), cols))
+        return out
+
+    def free(self) -> None:
+        if self.h:
+            lib.tg_tensor_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class HModel:
+    """A tg_model: TinyGNN's Model (add_*_layer, load_weights, forward)."""
+
+    POST = {None: 0, "none": 0, "relu": 1, "elu": 2}
+
+    def __init__(self):
+        self.h = C.c_void_p()
+        check(lib.tg_model_create(C.byref(self.h)))
+
+    @staticmethod
+    def _act(a):
+        return _lib.ACT_RELU if a == "relu" else _lib.ACT_NONE
+
+    def add_gcn(self, fin: int, fout: int, bias: bool = True, act="relu", post=None) -> "HModel":
+        check(lib.tg_model_add_gcn(self.h, fin, fout, int(bias), self._act(act), self.POST[post]))
+        return self
+
+    def add_sage(self, fin: int, fout: int, agg: str = "mean", bias: bool = True, act="relu", post=None) -> "HModel":
+        check(lib.tg_model_add_sage(self.h, fin, fout, _lib.AGG_MAX if agg == "max" else _lib.AGG_MEAN, int(bias),
+                                    self._act(act), self.POST[post]))
+        return self
+
+    def add_gat(self, fin: int, fout: int, heads: int = 1, concat: bool = True, slope: float = 0.2,
+                bias: bool = True, act=None, post=None) -> "HModel":
+        check(lib.tg_model_add_gat(self.h, fin, fout, heads, int(concat), slope, int(bias), self._act(act),
+                                   self.POST[post]))
+        return self
+
+    def load_weights(self, weights: Dict[str, np.ndarray]) -> None:
+        names = list(weights)
+        arrs = [np.ascontiguousarray(weights[k], dtype=np.float32) for k in names]
+        arrs = [a.reshape(1, -1) if a.ndim == 1 else a for a in arrs]
+        n = len(names)
+        cn = (C.c_char_p * n)(*[k.encode() for k in names])
+        cd = (C.c_void_p * n)(*[a.ctypes.data for a in arrs])
+        cr = (C.c_int64 * n)(*[a.shape[0] for a in arrs])
+        cc = (C.c_int64 * n)(*[a.shape[1] for a in arrs])
+        check(lib.tg_model_load_weights(self.h, n, cn, cd, cr, cc))
+
+    def load_weights_file(self, path: str) -> None:
+        check(lib.tg_model_load_weights_file(self.h, path.encode()))
+
+    def forward(self, adjacency: HTensor, features: HTensor) -> HTensor:
+        out = C.c_void_p()
+        check(lib.tg_model_forward(self.h, adjacency.h, features.h, C.byref(out)))
+        return HTensor(out)
+
+    def free(self) -> None:
+        if self.h:
+            lib.tg_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def set_fast_math(fast: bool) -> bool:
+    """FAST (True) or EXACT arithmetic for the handle / C++ APIs; returns the previous setting."""
+    return bool(lib.tg_set_fast_math(int(fast)))
