@@ -40,6 +40,19 @@ struct WeightFile {
 
 WeightFile load_weight_file(const std::string& path);
 
+// The exchange step of a row-partitioned forward (no counterpart in the
+// reference): `world` processes, each holding one equal block of
+// R = ceil(n / world) rows; all_gather(buf, count) runs on the calling
+// thread's stream and leaves block q's `count` floats (at buf + q * count,
+// this rank's block filled by the caller) in every rank's buf.
+class RowExchange {
+public:
+    virtual ~RowExchange() = default;
+    virtual int world() const = 0;
+    virtual int rank() const = 0;
+    virtual void all_gather(float* buf, std::size_t count) = 0;
+};
+
 class Model {
 public:
     enum class InterActivation : uint8_t { None = 0, ReLU = 1, ELU = 2 };
@@ -61,6 +74,16 @@ public:
     void load_weights(const WeightFile& wf);
 
     Tensor forward(const Tensor& adjacency, const Tensor& features) const;
+
+    // Model::forward on this process's block of an n-node graph partitioned
+    // into equal row blocks (rows [rank * R, rank * R + rows), R = ceil(n /
+    // world)): adjacency_rows is that block's rows with global column ids
+    // (rows x n), feature_rows its feature rows; returns its output rows.
+    // Every process calls it with the same model.  GCN and SAGE layers; the
+    // result equals the rows of forward() on the whole graph (bit for bit in
+    // EXACT mode).  No counterpart in the reference.
+    Tensor forward_rows(const Tensor& adjacency_rows, std::size_t n, const Tensor& feature_rows,
+                        RowExchange& exchange) const;
 
 private:
     struct LayerEntry {

@@ -534,6 +534,40 @@ TG_API void tg_model_free(tg_model m);
  * returns the previous setting (tinygnn::set_fast_math). */
 TG_API int32_t tg_set_fast_math(int32_t fast);
 
+/* ── several GPUs: the row-partitioned forward ──────────────────────────── */
+/* One process per GPU.  An n-node graph is split into equal 1-D row blocks,
+ * R = ceil(n / world) rows each (rank r: rows [r R, min(n, (r+1) R))); a
+ * rank holds its rows of the adjacency (global column ids) and of the
+ * features.  Each layer's exchanged rows (GCN: H.W -- FAST: scaled by
+ * 1/sqrt(deg); SAGE: H.W_neigh, or H when it aggregates first) are
+ * all-gathered in place over NCCL, then every rank aggregates its own rows.
+ * The logits equal the rows of tg_model_forward on the whole graph (bit for
+ * bit in EXACT mode).  No counterpart in the reference, which runs on one
+ * CPU.  NCCL (libnccl.so.2) is loaded by tg_dist_init. */
+typedef struct tg_dist_s* tg_dist;
+
+/* This rank's row block [*row_begin, *row_end) and, given the whole graph's
+ * host row_ptr (nullable), its entry range [*entry_begin, *entry_end).  Host
+ * only; every output pointer nullable. */
+TG_API tg_status tg_dist_partition_csr(int32_t world, int32_t rank, int64_t n, const int32_t* row_ptr,
+                                       int64_t* row_begin, int64_t* row_end, int64_t* entry_begin,
+                                       int64_t* entry_end);
+/* Joins the communicator of `world` processes on CUDA device `device` (made
+ * current).  Rank 0 writes the communicator id to the file id_path (a path
+ * every rank can read; remove it afterwards); the others wait for it.  Every
+ * wait -- for the file, for all ranks to join, and later for each forward --
+ * gives up after timeout_ms: TG_ERR_TIMEOUT, the communicator aborted. */
+TG_API tg_status tg_dist_init(int32_t world, int32_t rank, int32_t device, const char* id_path,
+                              int32_t timeout_ms, tg_dist* out);
+/* Model::forward on this rank's rows: adjacency_rows (rows x n, global
+ * columns, no self-loops), feature_rows (rows x F_in) -> *out (rows x
+ * F_out).  GCN and SAGE layers.  Every rank calls it with the same model;
+ * it returns once this rank's logits are computed. */
+TG_API tg_status tg_dist_forward(tg_dist d, tg_model m, int64_t n, tg_tensor adjacency_rows,
+                                 tg_tensor feature_rows, tg_tensor* out);
+/* Leaves and frees the communicator (every rank, after its last forward). */
+TG_API tg_status tg_dist_finalize(tg_dist d);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -96,3 +96,27 @@ def test_handle_calls_without_device_report_no_device():
     assert _lib.lib.tg_model_add_gcn(m, 4, 2, 1, _lib.ACT_RELU, 0) == _lib.OK
     assert _lib.lib.tg_model_add_gcn(m, 0, 2, 1, _lib.ACT_RELU, 0) == _lib.INVALID_ARGUMENT
     _lib.lib.tg_model_free(m)
+
+
+def test_dist_partition_csr_rows_and_entries():
+    """tg_dist_partition_csr: equal row blocks of ceil(n / world) rows and
+    their entry ranges (host only, no device needed)."""
+    import numpy as np
+    from tinygnn_b200.handles import partition_rows
+    rp = np.array([0, 2, 2, 5, 9, 9, 12, 13], np.int32)  # n = 7
+    blocks = [partition_rows(3, r, 7, rp) for r in range(3)]
+    assert blocks == [(0, 3, 0, 5), (3, 6, 5, 12), (6, 7, 12, 13)]
+    assert partition_rows(4, 2, 5) == (4, 5, None, None)      # R = 2: rank 2 holds the last row
+    assert partition_rows(4, 3, 5)[:2] == (5, 5)              # ... and rank 3 none
+    from tinygnn_b200 import _lib
+    assert _lib.lib.tg_dist_partition_csr(2, 2, 5, None, None, None, None, None) == _lib.INVALID_ARGUMENT
+
+
+def test_dist_init_without_device_reports_no_device(tmp_path):
+    import ctypes as C
+    from tinygnn_b200 import _lib
+    if _lib.lib.tg_device_count() > 0:
+        pytest.skip("a device is present")
+    h = C.c_void_p()
+    st = _lib.lib.tg_dist_init(1, 0, 0, str(tmp_path / "id").encode(), 1000, C.byref(h))
+    assert st == _lib.NO_DEVICE

@@ -81,6 +81,10 @@ SIGNATURES = {
     "tg_model_forward": (i32, [vp, vp, vp, C.POINTER(vp)]),
     "tg_model_free": (None, [vp]),
     "tg_set_fast_math": (i32, [i32]),
+    "tg_dist_partition_csr": (i32, [i32, i32, i64, vp, P64, P64, P64, P64]),
+    "tg_dist_init": (i32, [i32, i32, i32, C.c_char_p, i32, C.POINTER(vp)]),
+    "tg_dist_forward": (i32, [vp, vp, i64, vp, vp, C.POINTER(vp)]),
+    "tg_dist_finalize": (i32, [vp]),
     "tg_gcn_layer_f32": (i32, [i64, i64, vp, vp, vp, vp, i64, i64, i64, vp, vp, i32, vp, i64, vp, i32, vp]),
     "tg_sage_layer_f32": (i32, [i64, i64, vp, vp, vp, i64, i64, i64, vp, vp, vp, i32, i32, vp, i64, vp, i32, vp]),
     "tg_gat_layer_f32": (i32, [i64, i64, vp, vp, vp, i64, i64, i64, i64, vp, vp, vp, vp, f32, i32, i32, vp, i64,

@@ -24,12 +24,6 @@ void set_last_error(const std::string& m);
 void fill_f32(float* p, int64_t n, float v, cudaStream_t s);
 }  // namespace tg
 
-struct tg_tensor_s {
-    tinygnn::Tensor t;
-};
-struct tg_model_s {
-    tinygnn::Model m;
-};
 
 namespace {
 

@@ -8,6 +8,7 @@
 #include <stdexcept>
 #include <string>
 
+#include "tinygnn/model.hpp"
 #include "tinygnn/tensor.hpp"
 #include "tinygnn_b200.h"
 
@@ -59,3 +60,11 @@ struct TensorAccess {
 };
 
 }  // namespace tinygnn
+
+// The objects behind the handle C ABI's opaque pointers.
+struct tg_tensor_s {
+    tinygnn::Tensor t;
+};
+struct tg_model_s {
+    tinygnn::Model m;
+};

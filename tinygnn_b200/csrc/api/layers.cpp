@@ -68,6 +68,36 @@ struct Contig {
 
 int act_code(Activation a) { return a == Activation::ReLU ? TG_ACT_RELU : TG_ACT_NONE; }
 
+// Two weight matrices (same shape) as device arrays with ld == cols, the
+// layout tg_gemm_pair_f32 takes (Tensor rows are padded to 16 bytes).
+struct DevWeights {
+    const float* wn = nullptr;
+    const float* ws = nullptr;
+    float* owned = nullptr;
+    DevWeights(const Tensor& a, const Tensor& b) {
+        const std::size_t r = a.rows(), c = a.cols();
+        if (a.device_ld() == c && b.device_ld() == c) {
+            wn = a.device_data();
+            ws = b.device_data();
+            return;
+        }
+        owned = dalloc<float>(2 * r * c);
+        detail::cuda(cudaMemcpy2DAsync(owned, c * sizeof(float), a.device_data(), a.device_ld() * sizeof(float),
+                                       c * sizeof(float), r, cudaMemcpyDeviceToDevice, detail::cstream()),
+                     "SAGELayer weights");
+        detail::cuda(cudaMemcpy2DAsync(owned + r * c, c * sizeof(float), b.device_data(), b.device_ld() * sizeof(float),
+                                       c * sizeof(float), r, cudaMemcpyDeviceToDevice, detail::cstream()),
+                     "SAGELayer weights");
+        wn = owned;
+        ws = owned + r * c;
+    }
+    ~DevWeights() {
+        if (owned && cudaFreeAsync(owned, detail::cstream()) != cudaSuccess) cudaGetLastError();
+    }
+    DevWeights(const DevWeights&) = delete;
+    DevWeights& operator=(const DevWeights&) = delete;
+};
+
 void check_weight(const Tensor& w, std::size_t in, std::size_t out, const std::string& who) {
     if (w.format() != StorageFormat::Dense) throw std::invalid_argument(who + ": weight must be Dense.");
     if (w.rows() != in || w.cols() != out)
@@ -234,15 +264,14 @@ Tensor SAGELayer::forward(const Tensor& A, const Tensor& H) const {
     const bool max = aggregator_ == Aggregator::Max;
     const float* bias = use_bias_ ? bias_.device_data() : nullptr;
     if (fast_math() && !max && Fi > Fo) {  // transform first: gather F_out instead of F_in floats per edge
+        // W_neigh and W_self in one tensor-core pass over H (weights are dense with ld == cols)
         Tensor Tn = Tensor::dense_device(N, Fo), Ts = Tensor::dense_device(N, Fo);
-        for (auto* pr : {&Tn, &Ts}) {
-            const Tensor& W = pr == &Tn ? weight_neigh_ : weight_self_;
-            check(tg_gemm_f32(static_cast<int64_t>(N), static_cast<int64_t>(Fo), static_cast<int64_t>(Fi),
-                              H.device_data(), static_cast<int64_t>(H.device_ld()), W.device_data(),
-                              static_cast<int64_t>(W.device_ld()), pr->mutable_device_data(),
-                              static_cast<int64_t>(pr->device_ld()), nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST,
-                              stream()));
-        }
+        DevWeights w(weight_neigh_, weight_self_);
+        check(tg_gemm_pair_f32(static_cast<int64_t>(N), static_cast<int64_t>(Fo), static_cast<int64_t>(Fi),
+                               H.device_data(), static_cast<int64_t>(H.device_ld()), w.wn, w.ws,
+                               static_cast<int64_t>(Fo), Tn.mutable_device_data(), static_cast<int64_t>(Tn.device_ld()),
+                               Ts.mutable_device_data(), static_cast<int64_t>(Ts.device_ld()), TG_MODE_FAST,
+                               stream()));
         const detail::TrustedCsr trusted_csr;
         check(tg_sage_mean_combine_f32(static_cast<int64_t>(N), static_cast<int64_t>(A.cols()),
                                        static_cast<int64_t>(A.nnz()), A.device_row_ptr(), A.device_col_ind(),
@@ -253,13 +282,24 @@ Tensor SAGELayer::forward(const Tensor& A, const Tensor& H) const {
                                        stream()));
         return out;
     }
-    // Aggregate first, then the interleaved dual product (bit-identical).
+    // Aggregate first, then the interleaved dual product (bit-identical), or
+    // in FAST mode one tensor-core GEMM [agg | H] . [Wn; Ws].
     Tensor agg = Tensor::dense_device(N, Fi);
     const detail::TrustedCsr trusted_csr;
     check(tg_sage_aggregate_f32(static_cast<int64_t>(N), static_cast<int64_t>(A.cols()), static_cast<int64_t>(A.nnz()),
                                 A.device_row_ptr(), A.device_col_ind(), H.device_data(), static_cast<int64_t>(Fi),
                                 static_cast<int64_t>(H.device_ld()), agg.mutable_device_data(),
                                 static_cast<int64_t>(agg.device_ld()), max ? TG_AGG_MAX : TG_AGG_MEAN, stream()));
+    if (fast_math()) {
+        check(tg_gemm_cat_f32(static_cast<int64_t>(N), static_cast<int64_t>(Fo), static_cast<int64_t>(Fi),
+                              agg.device_data(), static_cast<int64_t>(agg.device_ld()), static_cast<int64_t>(Fi),
+                              H.device_data(), static_cast<int64_t>(H.device_ld()), weight_neigh_.device_data(),
+                              static_cast<int64_t>(weight_neigh_.device_ld()), weight_self_.device_data(),
+                              static_cast<int64_t>(weight_self_.device_ld()), out.mutable_device_data(),
+                              static_cast<int64_t>(out.device_ld()), bias, act_code(activation_), 0.0f, TG_MODE_FAST,
+                              stream()));
+        return out;
+    }
     check(tg_gemm_dual_f32(static_cast<int64_t>(N), static_cast<int64_t>(Fo), static_cast<int64_t>(Fi),
                            agg.device_data(), static_cast<int64_t>(agg.device_ld()), H.device_data(),
                            static_cast<int64_t>(H.device_ld()), weight_neigh_.device_data(),

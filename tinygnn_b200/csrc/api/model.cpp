@@ -353,4 +353,210 @@ Tensor Model::forward(const Tensor& adjacency, const Tensor& features) const {
     return H;
 }
 
+
+// ── Row-partitioned forward ─────────────────────────────────────────────────
+namespace {
+
+// A (world * R) x ld exchange buffer whose row j is node j; this rank's
+// block starts at row rank * R.
+struct Gathered {
+    DevBuf buf;
+    std::size_t R, ld;
+    Gathered(std::size_t P, std::size_t R_, std::size_t ld_) : buf(P * R_ * ld_), R(R_), ld(ld_) {
+        detail::cuda(cudaMemsetAsync(buf.p, 0, P * R_ * ld_ * sizeof(float), detail::cstream()), "forward_rows");
+    }
+    float* block(int rank) { return buf.p + static_cast<std::size_t>(rank) * R * ld; }
+};
+
+int act_of(Activation a) { return a == Activation::ReLU ? TG_ACT_RELU : TG_ACT_NONE; }
+
+}  // namespace
+
+Tensor Model::forward_rows(const Tensor& A, std::size_t n, const Tensor& X, RowExchange& ex) const {
+    if (layers_.empty()) throw std::runtime_error("Model::forward: no layers configured.");
+    const int P = ex.world(), r = ex.rank();
+    if (P < 1 || r < 0 || r >= P) throw std::invalid_argument("Model::forward_rows: bad world / rank");
+    const std::size_t R = (n + static_cast<std::size_t>(P) - 1) / static_cast<std::size_t>(P);
+    const std::size_t row0 = std::min(n, static_cast<std::size_t>(r) * R);
+    const std::size_t rows = std::min(R, n - row0);
+    if (A.format() != StorageFormat::SparseCSR)
+        throw std::invalid_argument("Model::forward_rows: adjacency rows must be SparseCSR (got Dense).");
+    if (A.rows() != rows || A.cols() != n)
+        throw std::invalid_argument("Model::forward_rows: rank " + std::to_string(r) + " holds rows [" +
+                                    std::to_string(row0) + ", " + std::to_string(row0 + rows) + ") of " +
+                                    std::to_string(n) + "; adjacency rows are " +
+                                    detail::shape_str(A.rows(), A.cols()));
+    if (X.format() != StorageFormat::Dense || X.rows() != rows)
+        throw std::invalid_argument("Model::forward_rows: feature rows must be Dense with " + std::to_string(rows) +
+                                    " rows");
+    bool need_norm = false;
+    for (const auto& e : layers_) {
+        if (e.type == LayerEntry::Type::GAT)
+            throw std::invalid_argument("Model::forward_rows: GAT layers are not supported on partitioned graphs");
+        need_norm |= e.type == LayerEntry::Type::GCN;
+    }
+    const bool fast = fast_math();
+    const int64_t M = static_cast<int64_t>(rows), K = static_cast<int64_t>(n);
+    const detail::TrustedCsr trusted_csr;  // A was checked where it was built
+
+    // Per graph: a longest-first schedule of this block's rows; for GCN in
+    // FAST mode this block's 1/sqrt(deg) (rank-local), in EXACT mode the
+    // normalised block (its degrees all-gathered for the column scale).
+    DevInts order(rows);
+    if (rows) check(tg_csr_degree_order(M, A.device_row_ptr(), order.p, stream()));
+    DevBuf dis(std::max<std::size_t>(rows, 1));
+    Tensor A_gcn;
+    std::unique_ptr<DevInts> rp_n, ci_n;
+    std::unique_ptr<DevBuf> v_n;
+    if (need_norm && fast && rows) {
+        check(tg_gcn_norm_scale_f32(M, static_cast<int64_t>(A.nnz()), A.device_row_ptr(), A.device_data(), dis.p,
+                                    stream()));
+    } else if (need_norm) {
+        Gathered dis_all(static_cast<std::size_t>(P), R, 1);
+        rp_n = std::make_unique<DevInts>(rows + 1);
+        DevInts ins(rows);
+        check(tg_gcn_norm_rows_degrees_f32(M, static_cast<int64_t>(row0), static_cast<int64_t>(A.nnz()),
+                                           A.device_row_ptr(), A.device_col_ind(), A.device_data(), order.p,
+                                           rp_n->p, ins.p, dis_all.block(r), stream()));
+        ex.all_gather(dis_all.buf.p, R);
+        int32_t nnz_n = 0;
+        detail::cuda(cudaMemcpyAsync(&nnz_n, rp_n->p + rows, sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                     detail::cstream()),
+                     "forward_rows");
+        detail::cuda(cudaStreamSynchronize(detail::cstream()), "forward_rows");
+        ci_n = std::make_unique<DevInts>(static_cast<std::size_t>(nnz_n));
+        v_n = std::make_unique<DevBuf>(static_cast<std::size_t>(nnz_n));
+        check(tg_gcn_norm_rows_fill_f32(M, static_cast<int64_t>(row0), K, A.device_row_ptr(), A.device_col_ind(),
+                                        A.device_data(), order.p, rp_n->p, ins.p, dis_all.block(r), dis_all.buf.p,
+                                        ci_n->p, v_n->p, stream()));
+        // the tensor takes the three arrays over (same stream-ordered pool)
+        A_gcn = TensorAccess::csr_from_device(rows, n, rp_n->p, ci_n->p, v_n->p, static_cast<std::size_t>(nnz_n));
+        rp_n->p = nullptr;
+        ci_n->p = nullptr;
+        v_n->p = nullptr;
+    }
+
+    Tensor H;
+    const Tensor* in = &X;
+    for (const auto& e : layers_) {
+        Tensor out;
+        if (e.type == LayerEntry::Type::GCN) {
+            const GCNLayer& L = gcn_layers_[e.start_idx];
+            if (in->cols() != L.in_features())
+                throw std::invalid_argument("GCNLayer::forward: H has " + std::to_string(in->cols()) +
+                                            " columns but layer expects in_features=" +
+                                            std::to_string(L.in_features()) + ".");
+            const std::size_t Fo = L.out_features(), ld = detail::pad4(Fo);
+            Gathered full(static_cast<std::size_t>(P), R, ld);
+            out = Tensor::dense_device(rows, Fo);
+            if (rows) {
+                if (fast)  // Hs = diag(dis) . H . W for this block's rows
+                    check(tg_gemm_rowscale_f32(M, static_cast<int64_t>(Fo), static_cast<int64_t>(L.in_features()),
+                                               in->device_data(), static_cast<int64_t>(in->device_ld()),
+                                               L.weight().device_data(), static_cast<int64_t>(L.weight().device_ld()),
+                                               full.block(r), static_cast<int64_t>(ld), dis.p, nullptr, TG_ACT_NONE,
+                                               0.0f, TG_MODE_FAST, stream()));
+                else
+                    check(tg_gemm_f32(M, static_cast<int64_t>(Fo), static_cast<int64_t>(L.in_features()),
+                                      in->device_data(), static_cast<int64_t>(in->device_ld()), L.weight().device_data(),
+                                      static_cast<int64_t>(L.weight().device_ld()), full.block(r),
+                                      static_cast<int64_t>(ld), nullptr, TG_ACT_NONE, 0.0f, TG_MODE_EXACT, stream()));
+            }
+            ex.all_gather(full.buf.p, R * ld);
+            if (rows) {
+                const float* b = L.has_bias() ? L.bias().device_data() : nullptr;
+                if (fast)
+                    check(tg_gcn_aggregate_f32(M, K, static_cast<int64_t>(A.nnz()), A.device_row_ptr(),
+                                               A.device_col_ind(), A.device_data(), full.buf.p,
+                                               static_cast<int64_t>(Fo), static_cast<int64_t>(ld), full.block(r),
+                                               static_cast<int64_t>(ld), dis.p, b, act_of(L.activation()),
+                                               out.mutable_device_data(), static_cast<int64_t>(out.device_ld()),
+                                               order.p, nullptr, nullptr, 0, 1, TG_FLAG_B_ROWS_PADDED, stream()));
+                else
+                    check(tg_spmm_f32(M, K, static_cast<int64_t>(A_gcn.nnz()), A_gcn.device_row_ptr(),
+                                      A_gcn.device_col_ind(), A_gcn.device_data(), full.buf.p, static_cast<int64_t>(Fo),
+                                      static_cast<int64_t>(ld), out.mutable_device_data(),
+                                      static_cast<int64_t>(out.device_ld()), b, act_of(L.activation()), 0.0f, order.p,
+                                      TG_MODE_EXACT | TG_FLAG_B_ROWS_PADDED, stream()));
+            }
+        } else {  // SAGE
+            const SAGELayer& L = sage_layers_[e.start_idx];
+            const std::size_t Fi = L.in_features(), Fo = L.out_features();
+            if (in->cols() != Fi)
+                throw std::invalid_argument("SAGELayer::forward: H has " + std::to_string(in->cols()) +
+                                            " columns but layer expects in_features=" + std::to_string(Fi) + ".");
+            const bool max = L.aggregator() == SAGELayer::Aggregator::Max;
+            const float* b = L.has_bias() ? L.bias().device_data() : nullptr;
+            out = Tensor::dense_device(rows, Fo);
+            if (fast && !max && Fi > Fo) {
+                // transform first: Tn = H . Wn exchanged, Ts = H . Ws local
+                const std::size_t ld = detail::pad4(Fo);
+                Gathered full(static_cast<std::size_t>(P), R, ld);
+                Tensor Ts = Tensor::dense_device(rows, Fo);
+                if (rows) {
+                    check(tg_gemm_f32(M, static_cast<int64_t>(Fo), static_cast<int64_t>(Fi), in->device_data(),
+                                      static_cast<int64_t>(in->device_ld()), L.weight_neigh().device_data(),
+                                      static_cast<int64_t>(L.weight_neigh().device_ld()), full.block(r),
+                                      static_cast<int64_t>(ld), nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST, stream()));
+                    check(tg_gemm_f32(M, static_cast<int64_t>(Fo), static_cast<int64_t>(Fi), in->device_data(),
+                                      static_cast<int64_t>(in->device_ld()), L.weight_self().device_data(),
+                                      static_cast<int64_t>(L.weight_self().device_ld()), Ts.mutable_device_data(),
+                                      static_cast<int64_t>(Ts.device_ld()), nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST,
+                                      stream()));
+                }
+                ex.all_gather(full.buf.p, R * ld);
+                if (rows)
+                    check(tg_sage_mean_combine_f32(M, K, static_cast<int64_t>(A.nnz()), A.device_row_ptr(),
+                                                   A.device_col_ind(), full.buf.p, static_cast<int64_t>(Fo),
+                                                   static_cast<int64_t>(ld), Ts.device_data(),
+                                                   static_cast<int64_t>(Ts.device_ld()), b, act_of(L.activation()),
+                                                   out.mutable_device_data(), static_cast<int64_t>(out.device_ld()),
+                                                   order.p, TG_FLAG_B_ROWS_PADDED, stream()));
+            } else {
+                // aggregate first: every node's H rows exchanged, this block's
+                // rows aggregated, then the layer's product
+                const std::size_t ld = detail::pad4(Fi);
+                Gathered full(static_cast<std::size_t>(P), R, ld);
+                if (rows)
+                    detail::cuda(cudaMemcpy2DAsync(full.block(r), ld * sizeof(float), in->device_data(),
+                                                   in->device_ld() * sizeof(float), Fi * sizeof(float), rows,
+                                                   cudaMemcpyDeviceToDevice, detail::cstream()),
+                                 "forward_rows");
+                ex.all_gather(full.buf.p, R * ld);
+                if (rows) {
+                    Tensor agg = Tensor::dense_device(rows, Fi);
+                    check(tg_sage_aggregate_f32(M, K, static_cast<int64_t>(A.nnz()), A.device_row_ptr(),
+                                                A.device_col_ind(), full.buf.p, static_cast<int64_t>(Fi),
+                                                static_cast<int64_t>(ld), agg.mutable_device_data(),
+                                                static_cast<int64_t>(agg.device_ld()), max ? TG_AGG_MAX : TG_AGG_MEAN,
+                                                stream()));
+                    if (fast)
+                        check(tg_gemm_cat_f32(M, static_cast<int64_t>(Fo), static_cast<int64_t>(Fi), agg.device_data(),
+                                              static_cast<int64_t>(agg.device_ld()), static_cast<int64_t>(Fi),
+                                              in->device_data(), static_cast<int64_t>(in->device_ld()),
+                                              L.weight_neigh().device_data(),
+                                              static_cast<int64_t>(L.weight_neigh().device_ld()),
+                                              L.weight_self().device_data(),
+                                              static_cast<int64_t>(L.weight_self().device_ld()),
+                                              out.mutable_device_data(), static_cast<int64_t>(out.device_ld()), b,
+                                              act_of(L.activation()), 0.0f, TG_MODE_FAST, stream()));
+                    else
+                        check(tg_gemm_dual_f32(M, static_cast<int64_t>(Fo), static_cast<int64_t>(Fi),
+                                               agg.device_data(), static_cast<int64_t>(agg.device_ld()),
+                                               in->device_data(), static_cast<int64_t>(in->device_ld()),
+                                               L.weight_neigh().device_data(), L.weight_self().device_data(),
+                                               static_cast<int64_t>(L.weight_neigh().device_ld()),
+                                               out.mutable_device_data(), static_cast<int64_t>(out.device_ld()), b,
+                                               act_of(L.activation()), 0.0f, stream()));
+                }
+            }
+        }
+        if (e.post_act == InterActivation::ReLU) relu_inplace(out);
+        else if (e.post_act == InterActivation::ELU) elu_inplace(out);
+        H = std::move(out);
+        in = &H;
+    }
+    return H;
+}
+
 }  // namespace tinygnn

@@ -134,3 +134,33 @@ class HModel:
 def set_fast_math(fast: bool) -> bool:
     """FAST (True) or EXACT arithmetic for the handle / C++ APIs; returns the previous setting."""
     return bool(lib.tg_set_fast_math(int(fast)))
+
+
+def partition_rows(world: int, rank: int, n: int, row_ptr=None):
+    """(row_begin, row_end, entry_begin, entry_end) of rank's equal row block
+    (entries None without row_ptr) -- tg_dist_partition_csr."""
+    vals = [C.c_int64() for _ in range(4)]
+    rp = None if row_ptr is None else np.ascontiguousarray(row_ptr, dtype=np.int32)
+    outs = [C.byref(v) for v in vals[:2]] + ([None, None] if rp is None else [C.byref(v) for v in vals[2:]])
+    check(lib.tg_dist_partition_csr(world, rank, n, None if rp is None else rp.ctypes.data, *outs))
+    rb, re_, eb, ee = (v.value for v in vals)
+    return (rb, re_, eb, ee) if rp is not None else (rb, re_, None, None)
+
+
+class HDist:
+    """A tg_dist: this process's rank of the row-partitioned forward (NCCL)."""
+
+    def __init__(self, world: int, rank: int, device: int, id_path: str, timeout_ms: int = 60000):
+        self.h = C.c_void_p()
+        self.world, self.rank = world, rank
+        check(lib.tg_dist_init(world, rank, device, id_path.encode(), timeout_ms, C.byref(self.h)))
+
+    def forward(self, model: HModel, n: int, adjacency_rows: HTensor, feature_rows: HTensor) -> HTensor:
+        out = C.c_void_p()
+        check(lib.tg_dist_forward(self.h, model.h, n, adjacency_rows.h, feature_rows.h, C.byref(out)))
+        return HTensor(out)
+
+    def finalize(self) -> None:
+        if self.h:
+            h, self.h = self.h, None
+            check(lib.tg_dist_finalize(h))
