@@ -70,8 +70,10 @@ def parse():
                          "(auto: on 2-4 GPUs, for the layers whose exchanged operand is >= 64 MB)")
     ap.add_argument("--blocks-per-rank", default="auto",
                     help="column blocks per rank for the gathers: 'auto' or a count")
-    ap.add_argument("--micro", choices=["hub"], default=None,
-                    help="hub: time one long row through spmm (the heavy-row path) instead of the benchmark")
+    ap.add_argument("--micro", choices=["hub", "l2"], default=None,
+                    help="hub: time one long row through spmm (the heavy-row path); l2: the random-row gather "
+                         "rate of spmm over a 64 MB operand that stays in L2 (the ceiling of the gathers); "
+                         "instead of the benchmark")
     ap.add_argument("--micro-entries", type=int, default=13_531)
     ap.add_argument("--micro-features", type=int, default=128)
     ap.add_argument("--suite", action="store_true",
@@ -467,6 +469,10 @@ def run_ours(args):
     R, r0, r1 = model.R, model.row0, model.row1
     rows = r1 - r0
     A_raw = slice_rows(rp, ci, v, r0, r1, n)
+    # The graph is checked once, as Tensor::sparse_csr checks it when the
+    # caller builds it (src/tensor.cpp:46-86); Model::forward does not re-check.
+    tg.csr_validate(A_raw)
+    A_raw.validated = True
     # Feature rows live at a 16-byte row stride (602 -> 604 floats) so the
     # tensor-core GEMM can read them with TMA; the view is 602 wide.
     Xp = torch.zeros((rows, (FEATS + 3) // 4 * 4), dtype=torch.float32, device=dev)
@@ -559,9 +565,12 @@ def run_ours(args):
         model.forward_from_host(h_rp, h_ci, h_v, h_X, h_out, e2e_bufs)
 
     # At one GPU, e2e goes through the drop-in boundary a TinyGNN caller
-    # binds: the handle C ABI (tg_tensor_create_csr / _dense from the pinned
-    # host buffers, tg_model_forward = Model::forward, tg_tensor_download of
-    # the logits), every step, each call complete before it returns.
+    # binds: tg_model_forward_host (Model::forward from the pinned host CSR
+    # arrays and features, the uploads overlapped with the compute, the
+    # logits written to a pinned host buffer before it returns), every step.
+    # Beside it, the same through the four separate handle calls
+    # (tg_tensor_create_csr / _dense, tg_model_forward, tg_tensor_download),
+    # each complete before it returns.
     hmodel = None
     h_Xc = None
     if world == 1 and not args.no_e2e:
@@ -580,6 +589,9 @@ def run_ours(args):
         parts = {"upload_csr": 0.0, "upload_features": 0.0, "forward": 0.0, "download": 0.0, "free": 0.0}
 
         def e2e_step():
+            hmodel.forward_host(h_rp, h_ci, h_v, h_Xc, FEATS, h_out_api, CLASSES)
+
+        def e2e_calls_step():
             # each handle call completes before it returns: host timestamps time it
             t0 = time.perf_counter()
             A_t = HTensor.csr(n, n, h_rp, h_ci, h_v)
@@ -600,8 +612,11 @@ def run_ours(args):
         e2e_step = e2e_sharded_step
 
     e2e_ms = None if args.no_e2e else time_steps(e2e_step, args.steps, min(args.warmup, 3), world)
-    e2e_parts = None
-    if hmodel is not None:  # per timed step (the warm-up steps are in the sums too)
+    host_api_out = None if hmodel is None else h_out_api.clone()
+    e2e_parts = e2e_calls_ms = None
+    if hmodel is not None:
+        e2e_calls_ms = time_steps(e2e_calls_step, args.steps, min(args.warmup, 3), world)
+        # per timed step (the warm-up steps are in the sums too)
         calls = args.steps + min(args.warmup, 3)
         e2e_parts = {k: v / calls * 1e3 for k, v in parts.items() if k != "download"}
         e2e_parts["forward+download"] = e2e_parts.pop("forward")
@@ -620,11 +635,12 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_matches = None if args.no_e2e else bool(torch.equal(ref_out.cpu(), h_out))
     sharded_ms = e2e_sharded_ms if hmodel is not None else e2e_ms
-    api_close = None
+    api_close = host_equals_calls = None
     if hmodel is not None:
         logits_ref = torch.log_softmax(ref_out.cpu().double(), 1)
-        logits_api = torch.log_softmax(h_out_api.double(), 1)
+        logits_api = torch.log_softmax(host_api_out.double(), 1)
         api_close = bool(((logits_api - logits_ref).abs() <= 1e-5 + 1e-4 * logits_ref.abs()).all())
+        host_equals_calls = bool(torch.equal(host_api_out, h_out_api))  # h_out_api: the four-call path's
         hmodel.free()
 
     # roofline of the layer-1 gather (rank-local)
@@ -687,16 +703,22 @@ def run_ours(args):
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "edges/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": None if e2e_ms is None else e2e_ms / args.steps,
-                    "api": ("handle C ABI: tg_tensor_create_csr + tg_tensor_create_dense from pinned host buffers, "
-                            "tg_model_forward (Model::forward, gcn_norm inside), tg_tensor_download of the logits"
+                    "api": ("handle C ABI: tg_model_forward_host (Model::forward from pinned host CSR arrays + "
+                            "features, uploads overlapped with the compute, gcn_norm inside, logits to a pinned host "
+                            "buffer)"
                             if hmodel is not None else
                             "tinygnn_b200.dist.ShardedModel.forward_from_host: this rank's pinned host rows in, "
                             "host logits out"),
                     "log_softmax_within_tolerance_of_resident_run": api_close,
-                    "call_ms": e2e_parts,
+                    "equals_separate_calls": host_equals_calls,
                     "inputs": ("unweighted CSR: row_ptr + col_ind uploaded, values 1.0 written on the device"
                                if h_v is None else "CSR row_ptr + col_ind + values") + ", features fp32",
                     "note": "rank 0's bytes; every rank moves its own row block"},
+            "e2e_separate_calls": None if e2e_calls_ms is None else {
+                "value": nnz_total / (e2e_calls_ms / args.steps * 1e-3), "unit": "edges/s",
+                "ms_per_step": e2e_calls_ms / args.steps, "call_ms": e2e_parts,
+                "api": "tg_tensor_create_csr + tg_tensor_create_dense (pinned host buffers), tg_model_forward, "
+                       "tg_tensor_download: four calls, each complete before it returns"},
             "e2e_sharded_pipelined": None if sharded_ms is None else {
                 "value": nnz_total / (sharded_ms / args.steps * 1e-3), "unit": "edges/s",
                 "ms_per_step": sharded_ms / args.steps, "logits_match_resident_run": e2e_matches,
@@ -748,6 +770,37 @@ def run_micro_hub(args):
     print(json.dumps({"micro": "hub_row", "entries": args.micro_entries, "features": F, "us_per_call": us,
                       "ns_per_entry": us * 1000 / args.micro_entries,
                       "heavy_min_len": os.environ.get("TINYGNN_B200_HEAVY_MIN_LEN", "auto")}))
+    tg.ops.take_device_error()
+    return 0
+
+
+def run_micro_l2(args):
+    """The gather rate when every operand row hits in L2: 2^17 output rows of
+    320 uniformly random entries each over an operand of 64 MB (under the
+    126 MB L2), through the public spmm, for the two row widths the Reddit
+    GCN gathers (128 and 41 features).  The bytes counted are the operand
+    rows read (entries x features x 4); a gather whose operand spills to HBM
+    cannot beat this rate.  Prints its own JSON lines."""
+    import tinygnn_b200 as tg
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(2)
+    rows, per_row, reps = 1 << 17, 320, 20
+    for F in (128, 41):
+        Fp = (F + 3) // 4 * 4
+        n_cols = (64 << 20) // (Fp * 4)
+        rp = np.arange(rows + 1, dtype=np.int64) * per_row
+        ci = np.sort(rng.integers(0, n_cols, (rows, per_row), dtype=np.int64), axis=1).astype(np.int32).ravel()
+        A = tg.CSR.from_numpy(rp.astype(np.int32), ci, np.ones(ci.size, np.float32), n_cols=n_cols)
+        A = A.with_degree_order()
+        B = torch.randn(n_cols, Fp, device="cuda")[:, :F]
+        out = torch.empty(rows, F, device="cuda")
+        ms = _gpu_ms(lambda: tg.spmm(A, B, out=out), reps=reps)
+        nnz = rows * per_row
+        print(json.dumps({"micro": "l2_gather", "features": F, "operand_mb": n_cols * Fp * 4 / 2**20,
+                          "entries": nnz, "ms_per_call": ms,
+                          "operand_tb_s": nnz * F * 4 / (ms * 1e-3) / 1e12,
+                          "with_indices_tb_s": nnz * (F * 4 + 8) / (ms * 1e-3) / 1e12}))
+        del A, B, out
     tg.ops.take_device_error()
     return 0
 
@@ -933,6 +986,8 @@ def main():
         return run_suite(args)
     if args.micro == "hub":
         return run_micro_hub(args)
+    if args.micro == "l2":
+        return run_micro_l2(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

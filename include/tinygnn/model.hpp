@@ -40,6 +40,10 @@ struct WeightFile {
 
 WeightFile load_weight_file(const std::string& path);
 
+namespace detail {
+struct ForwardGraphs;  // the adjacency variants one forward call uses
+}
+
 // The exchange step of a row-partitioned forward (no counterpart in the
 // reference): `world` processes, each holding one equal block of
 // R = ceil(n / world) rows; all_gather(buf, count) runs on the calling
@@ -85,7 +89,29 @@ public:
     Tensor forward_rows(const Tensor& adjacency_rows, std::size_t n, const Tensor& feature_rows,
                         RowExchange& exchange) const;
 
+    // forward() from host buffers, for callers that hold the graph and the
+    // features in host memory (no counterpart in the reference): the raw
+    // adjacency as CSR arrays (values NULL: an unweighted graph, every value
+    // 1.0, written on the device instead of crossing PCIe) and the n x
+    // feature_cols features at row stride ld_features in; the last layer's
+    // n x out_cols output written to `out` at row stride ld_out before the
+    // call returns.  The uploads run on a copy stream, overlapped with the
+    // compute: the CSR first (checked on the device with Tensor::sparse_csr's
+    // checks as soon as it has landed), then the features in row blocks.
+    // When the first layer is a GCN layer in FAST mode, its GEMM and its
+    // gather pass over block q's columns start as soon as block q has landed,
+    // and when the last layer is a one-pass FAST GCN layer it runs in row
+    // chunks whose outputs go back while the next chunk runs.  Same results
+    // as forward() on tensors holding the same data.  Host buffers in pinned
+    // (page-locked) memory let the copies overlap; pageable ones work, with
+    // the driver's staging and less overlap.
+    void forward_host(std::size_t n, std::size_t nnz, const int32_t* row_ptr, const int32_t* col_ind,
+                      const float* values, const float* features, std::size_t feature_cols,
+                      std::size_t ld_features, float* out, std::size_t out_cols, std::size_t ld_out) const;
+
 private:
+    Tensor run_layer(std::size_t li, detail::ForwardGraphs& g, const Tensor& in) const;
+
     struct LayerEntry {
         enum class Type : uint8_t { GCN, SAGE, GAT };
         Type type;

@@ -529,6 +529,26 @@ TG_API tg_status tg_model_load_weights(tg_model m, int32_t count, const char* co
  * and the GEMMs on the tensor cores, within the fp32 tolerance; otherwise
  * bit-identical to the reference. */
 TG_API tg_status tg_model_forward(tg_model m, tg_tensor adjacency, tg_tensor features, tg_tensor* out);
+/* tg_model_forward from host buffers in one call (Model::forward,
+ * src/model.cpp:358-439, with the tensors' construction from host arrays,
+ * src/tensor.cpp:46-86, folded in): the n x n raw adjacency as CSR arrays
+ * (values NULL: an unweighted graph, every value 1.0, written on the device
+ * instead of crossing PCIe) and the n x feature_cols features at row stride
+ * ld_features in; the last layer's n x out_cols output written to out at row
+ * stride ld_out before the call returns.  The uploads are queued on a copy
+ * stream and overlap the compute: the CSR first (checked on the device with
+ * Tensor::sparse_csr's checks and messages as soon as it has landed), then
+ * the features in row blocks; a FAST GCN first layer multiplies and gathers
+ * block by block as the blocks land, and a one-pass FAST GCN last layer
+ * returns its output in row chunks while the next chunk gathers.  Results
+ * equal tg_model_forward's on tensors holding the same data.  Pinned
+ * (page-locked) host buffers let the copies overlap; pageable ones work with
+ * the driver's staging.  Same calling thread rules as the other handle
+ * calls. */
+TG_API tg_status tg_model_forward_host(tg_model m, int64_t n, int64_t nnz, const int32_t* row_ptr,
+                                       const int32_t* col_ind, const float* values, const float* features,
+                                       int64_t feature_cols, int64_t ld_features, float* out, int64_t out_cols,
+                                       int64_t ld_out);
 TG_API void tg_model_free(tg_model m);
 /* FAST (1) or EXACT (0) arithmetic for the handle and C++ APIs, process-wide;
  * returns the previous setting (tinygnn::set_fast_math). */

@@ -95,6 +95,8 @@ def test_handle_calls_without_device_report_no_device():
     assert _lib.lib.tg_model_create(C.byref(m)) == _lib.OK  # host-side object
     assert _lib.lib.tg_model_add_gcn(m, 4, 2, 1, _lib.ACT_RELU, 0) == _lib.OK
     assert _lib.lib.tg_model_add_gcn(m, 0, 2, 1, _lib.ACT_RELU, 0) == _lib.INVALID_ARGUMENT
+    assert _lib.lib.tg_model_forward_host(m, 1, 0, C.cast(rp, C.c_void_p), None, None, None, 4, 4, None, 2,
+                                          2) == _lib.NO_DEVICE
     _lib.lib.tg_model_free(m)
 
 

@@ -106,3 +106,65 @@ def test_handle_tensors_from_pinned_torch_and_errors():
     with pytest.raises(ValueError, match=r"row_ptr must be non-decreasing"):
         HTensor.csr(2, 2, rp_bad, np.array([0, 1], np.int32))
     assert _lib.lib.tg_tensor_download(None, None, 0) == _lib.INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("kind", ["gcn", "sage", "gat"])
+@pytest.mark.parametrize("fast", [False, True])
+def test_forward_host_equals_forward(kind, fast):
+    """tg_model_forward_host (uploads overlapped with the compute; a FAST GCN
+    first layer in 8 feature blocks / column passes, a FAST GCN last layer in
+    row chunks) gives tg_model_forward's output bit for bit, at the caller's
+    feature stride (41: landing + device repack; 44: straight into place)
+    and output stride (7: device pack; 8: one copy), twice in a row, from
+    pinned and from pageable host buffers."""
+    import tinygnn_b200 as tg
+    from tinygnn_b200.handles import HTensor, set_fast_math
+    rng = np.random.default_rng(100 + len(kind) * 10 + fast)
+    n, fin = 6000, 41
+    weighted = kind == "sage"
+    rp, ci, v = powerlaw_csr(rng, n, 9, weighted=weighted, diag=False)
+    X = rng.standard_normal((n, fin)).astype(np.float32)
+    spec, w = _spec_weights(rng, kind, fin)
+    prev = set_fast_math(fast)
+    try:
+        m = _build(spec, w)
+        ref = m.forward(HTensor.csr(n, n, rp, ci, v if weighted else None), HTensor.dense(X, n, fin)).download()
+        h_rp, h_ci = torch.from_numpy(rp).pin_memory(), torch.from_numpy(ci).pin_memory()
+        h_v = torch.from_numpy(v).pin_memory() if weighted else None
+        for ld_f in (fin, 44):
+            Xh = torch.zeros((n, ld_f)).pin_memory()
+            Xh[:, :fin] = torch.from_numpy(X)
+            for ld_o in (7, 8):
+                for _ in range(2):
+                    out = torch.full((n, ld_o), float("nan")).pin_memory()
+                    m.forward_host(h_rp, h_ci, h_v, Xh, fin, out, 7)
+                    assert_bits_equal(out[:, :7].numpy(), ref, f"{kind} fast={fast} ld_f={ld_f} ld_o={ld_o}")
+        out = np.full((n, 7), np.nan, np.float32)  # pageable numpy buffers
+        m.forward_host(rp, ci, v if weighted else None, X, fin, out, 7)
+        assert_bits_equal(out, ref, f"{kind} fast={fast} pageable")
+        tg.ops.take_device_error()
+    finally:
+        set_fast_math(prev)
+
+
+def test_forward_host_refuses_bad_input():
+    """A malformed CSR is refused once it has landed, with the reference's
+    message; wrong feature widths with the layer's message."""
+    from tinygnn_b200.handles import set_fast_math
+    rng = np.random.default_rng(7)
+    spec, w = _spec_weights(rng, "gcn", 12)
+    for fast in (False, True):
+        prev = set_fast_math(fast)
+        try:
+            m = _build(spec, w)
+            X = np.ones((3, 12), np.float32)
+            out = np.zeros((3, 7), np.float32)
+            rp = np.array([0, 1, 3, 3], np.int32)
+            with pytest.raises(ValueError, match=r"col_ind\[2\] = 9 is out of bounds for cols=3"):
+                m.forward_host(rp, np.array([0, 1, 9], np.int32), None, X, 12, out, 7)
+            with pytest.raises(ValueError, match=r"in_features=12"):
+                m.forward_host(rp, np.array([0, 1, 2], np.int32), None, np.ones((3, 10), np.float32), 10, out, 7)
+            m.forward_host(rp, np.array([0, 1, 2], np.int32), None, X, 12, out, 7)  # still usable
+            assert np.isfinite(out).all()
+        finally:
+            set_fast_math(prev)

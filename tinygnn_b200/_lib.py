@@ -79,6 +79,7 @@ SIGNATURES = {
     "tg_model_load_weights_file": (i32, [vp, C.c_char_p]),
     "tg_model_load_weights": (i32, [vp, i32, C.POINTER(C.c_char_p), C.POINTER(vp), P64, P64]),
     "tg_model_forward": (i32, [vp, vp, vp, C.POINTER(vp)]),
+    "tg_model_forward_host": (i32, [vp, i64, i64, vp, vp, vp, vp, i64, i64, vp, i64, i64]),
     "tg_model_free": (None, [vp]),
     "tg_set_fast_math": (i32, [i32]),
     "tg_dist_partition_csr": (i32, [i32, i32, i64, vp, P64, P64, P64, P64]),

@@ -293,6 +293,22 @@ TG_API tg_status tg_model_forward(tg_model m, tg_tensor adjacency, tg_tensor fea
     });
 }
 
+TG_API tg_status tg_model_forward_host(tg_model m, int64_t n, int64_t nnz, const int32_t* row_ptr,
+                                       const int32_t* col_ind, const float* values, const float* features,
+                                       int64_t feature_cols, int64_t ld_features, float* out, int64_t out_cols,
+                                       int64_t ld_out) {
+    return api([&] {
+        need(m, "tg_model_forward_host: m");
+        if (n < 0 || nnz < 0 || feature_cols < 0 || ld_features < 0 || out_cols < 0 || ld_out < 0)
+            throw std::invalid_argument("tg_model_forward_host: negative size");
+        need(row_ptr, "tg_model_forward_host: row_ptr");
+        no_device_check();
+        m->m.forward_host(static_cast<std::size_t>(n), static_cast<std::size_t>(nnz), row_ptr, col_ind, values,
+                          features, static_cast<std::size_t>(feature_cols), static_cast<std::size_t>(ld_features),
+                          out, static_cast<std::size_t>(out_cols), static_cast<std::size_t>(ld_out));
+    });
+}
+
 TG_API void tg_model_free(tg_model m) { delete m; }
 
 TG_API int32_t tg_set_fast_math(int32_t fast) {

@@ -22,6 +22,10 @@
 #include "tinygnn/graph_loader.hpp"
 #include "tinygnn/ops.hpp"
 
+namespace tg {
+void fill_f32(float* p, int64_t n, float v, cudaStream_t s);
+}  // namespace tg
+
 namespace tinygnn {
 
 using detail::check;
@@ -277,6 +281,86 @@ Tensor gcn_forward_scaled(const GCNLayer& L, ScaledGraph& g, const Tensor& H) {
 
 }  // namespace
 
+namespace detail {
+
+// The adjacency variants one forward call uses (src/model.cpp:363-381): the
+// raw adjacency for SAGE; for GCN layers gcn_norm(A) (EXACT) or the raw
+// adjacency with its per-row scale (FAST, ScaledGraph); add_self_loops(A)
+// for GAT.
+struct ForwardGraphs {
+    const Tensor& adjacency;
+    std::unique_ptr<ScaledGraph> sg;
+    Tensor A_gcn, A_sl;
+
+    ForwardGraphs(const Tensor& adj, bool need_norm, bool need_sl) : adjacency(adj) {
+        // EXACT (the default): gcn_norm once per call, bit for bit, like the
+        // reference (src/model.cpp:365-381).  FAST: the GCN layers run on the
+        // raw adjacency with gcn_norm as per-row scale factors (within the
+        // fp32 tolerance); the same validation as gcn_norm's.
+        if (need_norm && fast_math()) {
+            if (adj.format() != StorageFormat::SparseCSR)
+                throw std::invalid_argument("gcn_norm: A must be SparseCSR (got Dense).");
+            if (adj.rows() != adj.cols())
+                throw std::invalid_argument("gcn_norm: A must be square \xE2\x80\x94 got " +
+                                            detail::shape_str(adj.rows(), adj.cols()) + ".");
+            sg = std::make_unique<ScaledGraph>(adj);
+        } else if (need_norm) {
+            A_gcn = gcn_norm(adj);
+        }
+        if (need_sl) A_sl = add_self_loops(adj);
+    }
+};
+
+}  // namespace detail
+
+Tensor Model::run_layer(std::size_t li, detail::ForwardGraphs& g, const Tensor& in_t) const {
+    const LayerEntry& e = layers_[li];
+    const Tensor* in = &in_t;
+    Tensor out;
+    switch (e.type) {
+        case LayerEntry::Type::GCN:
+            out = g.sg ? gcn_forward_scaled(gcn_layers_[e.start_idx], *g.sg, *in)
+                       : gcn_layers_[e.start_idx].forward(g.A_gcn, *in);
+            break;
+        case LayerEntry::Type::SAGE: out = sage_layers_[e.start_idx].forward(g.adjacency, *in); break;
+        case LayerEntry::Type::GAT: {
+            const Tensor& A_sl = g.A_sl;
+            if (e.count == 1) {
+                out = gat_layers_[e.start_idx].forward(A_sl, *in);
+                break;
+            }
+            // All heads in one pass: W = [W_0 | W_1 | ...], a_l / a_r / b stacked.
+            const GATLayer& h0 = gat_layers_[e.start_idx];
+            const std::size_t heads = e.count, d = h0.out_features(), fi = h0.in_features();
+            if (in->format() != StorageFormat::Dense || in->cols() != fi || in->rows() != A_sl.rows())
+                h0.forward(A_sl, *in);  // raises the reference's validation error
+            DevBuf W(fi * heads * d), al(heads * d), ar(heads * d), b(heads * d);
+            for (std::size_t h = 0; h < heads; ++h) {
+                const GATLayer& L = gat_layers_[e.start_idx + h];
+                pack(W.p, heads * d, h * d, L.weight());
+                pack(al.p, heads * d, h * d, L.attn_left());
+                pack(ar.p, heads * d, h * d, L.attn_right());
+                pack(b.p, heads * d, h * d, L.bias());
+            }
+            const std::size_t ocols = e.gat_concat ? heads * d : d;
+            out = Tensor::dense_device(in->rows(), ocols);
+            const detail::TrustedCsr trusted_csr;
+            check(tg_gat_layer_f32(static_cast<int64_t>(in->rows()), static_cast<int64_t>(A_sl.nnz()),
+                                   A_sl.device_row_ptr(), A_sl.device_col_ind(), in->device_data(),
+                                   static_cast<int64_t>(in->device_ld()), static_cast<int64_t>(fi),
+                                   static_cast<int64_t>(heads), static_cast<int64_t>(d), W.p, al.p, ar.p,
+                                   h0.has_bias() ? b.p : nullptr, h0.negative_slope(), e.gat_concat ? 1 : 0,
+                                   h0.activation() == Activation::ReLU ? TG_ACT_RELU : TG_ACT_NONE,
+                                   out.mutable_device_data(), static_cast<int64_t>(out.device_ld()), nullptr,
+                                   detail::mode(), stream()));
+            break;
+        }
+    }
+    if (e.post_act == InterActivation::ReLU) relu_inplace(out);
+    else if (e.post_act == InterActivation::ELU) elu_inplace(out);
+    return out;
+}
+
 Tensor Model::forward(const Tensor& adjacency, const Tensor& features) const {
     if (layers_.empty()) throw std::runtime_error("Model::forward: no layers configured.");
     bool need_norm = false, need_sl = false;
@@ -284,73 +368,283 @@ Tensor Model::forward(const Tensor& adjacency, const Tensor& features) const {
         need_norm |= e.type == LayerEntry::Type::GCN;
         need_sl |= e.type == LayerEntry::Type::GAT;
     }
-    // EXACT (the default): gcn_norm once per call, bit for bit, like the
-    // reference (src/model.cpp:365-381).  FAST: the GCN layers run on the raw
-    // adjacency with gcn_norm as per-row scale factors (within the fp32
-    // tolerance); the same validation as gcn_norm's.
-    const bool scaled = need_norm && fast_math();
-    std::unique_ptr<ScaledGraph> sg;
-    Tensor A_gcn, A_sl;
-    if (scaled) {
-        if (adjacency.format() != StorageFormat::SparseCSR)
-            throw std::invalid_argument("gcn_norm: A must be SparseCSR (got Dense).");
-        if (adjacency.rows() != adjacency.cols())
-            throw std::invalid_argument("gcn_norm: A must be square \xE2\x80\x94 got " +
-                                        detail::shape_str(adjacency.rows(), adjacency.cols()) + ".");
-        sg = std::make_unique<ScaledGraph>(adjacency);
-    } else if (need_norm) {
-        A_gcn = gcn_norm(adjacency);
-    }
-    if (need_sl) A_sl = add_self_loops(adjacency);
-
+    detail::ForwardGraphs g(adjacency, need_norm, need_sl);
     Tensor H;
     const Tensor* in = &features;
-    for (const auto& e : layers_) {
-        Tensor out;
-        switch (e.type) {
-            case LayerEntry::Type::GCN:
-                out = scaled ? gcn_forward_scaled(gcn_layers_[e.start_idx], *sg, *in)
-                             : gcn_layers_[e.start_idx].forward(A_gcn, *in);
-                break;
-            case LayerEntry::Type::SAGE: out = sage_layers_[e.start_idx].forward(adjacency, *in); break;
-            case LayerEntry::Type::GAT: {
-                if (e.count == 1) {
-                    out = gat_layers_[e.start_idx].forward(A_sl, *in);
-                    break;
-                }
-                // All heads in one pass: W = [W_0 | W_1 | ...], a_l / a_r / b stacked.
-                const GATLayer& h0 = gat_layers_[e.start_idx];
-                const std::size_t heads = e.count, d = h0.out_features(), fi = h0.in_features();
-                if (in->format() != StorageFormat::Dense || in->cols() != fi || in->rows() != A_sl.rows())
-                    h0.forward(A_sl, *in);  // raises the reference's validation error
-                DevBuf W(fi * heads * d), al(heads * d), ar(heads * d), b(heads * d);
-                for (std::size_t h = 0; h < heads; ++h) {
-                    const GATLayer& L = gat_layers_[e.start_idx + h];
-                    pack(W.p, heads * d, h * d, L.weight());
-                    pack(al.p, heads * d, h * d, L.attn_left());
-                    pack(ar.p, heads * d, h * d, L.attn_right());
-                    pack(b.p, heads * d, h * d, L.bias());
-                }
-                const std::size_t ocols = e.gat_concat ? heads * d : d;
-                out = Tensor::dense_device(in->rows(), ocols);
-                const detail::TrustedCsr trusted_csr;
-                check(tg_gat_layer_f32(static_cast<int64_t>(in->rows()), static_cast<int64_t>(A_sl.nnz()),
-                                       A_sl.device_row_ptr(), A_sl.device_col_ind(), in->device_data(),
-                                       static_cast<int64_t>(in->device_ld()), static_cast<int64_t>(fi),
-                                       static_cast<int64_t>(heads), static_cast<int64_t>(d), W.p, al.p, ar.p,
-                                       h0.has_bias() ? b.p : nullptr, h0.negative_slope(), e.gat_concat ? 1 : 0,
-                                       h0.activation() == Activation::ReLU ? TG_ACT_RELU : TG_ACT_NONE,
-                                       out.mutable_device_data(), static_cast<int64_t>(out.device_ld()), nullptr,
-                                       detail::mode(), stream()));
-                break;
-            }
-        }
-        if (e.post_act == InterActivation::ReLU) relu_inplace(out);
-        else if (e.post_act == InterActivation::ELU) elu_inplace(out);
-        H = std::move(out);
+    for (std::size_t li = 0; li < layers_.size(); ++li) {
+        H = run_layer(li, g, *in);
         in = &H;
     }
     return H;
+}
+
+
+// ── Forward from host buffers ──────────────────────────────────────────────
+namespace {
+
+// Feature row blocks (and layer-1 column passes) of the host-input forward
+// when its first layer is a FAST GCN layer: the GEMM and gather pass of
+// block q overlap the upload of block q + 1, and the gather work left after
+// the last block has landed is one block's pass.
+constexpr int kHostBlocks = 8;
+// Row chunks of the last layer's gather (one-pass FAST GCN layers): chunk
+// c's output crosses PCIe while chunk c + 1 gathers.
+constexpr int kOutChunks = 2;
+
+// The calling thread's copy stream on the current device (non-blocking, so
+// it runs beside the per-thread default stream the compute uses).
+cudaStream_t copy_stream() {
+    thread_local std::vector<cudaStream_t> per_device;
+    int dev = 0;
+    detail::cuda(cudaGetDevice(&dev), "Model::forward_host");
+    if (static_cast<int>(per_device.size()) <= dev) per_device.resize(static_cast<std::size_t>(dev) + 1, nullptr);
+    cudaStream_t& s = per_device[static_cast<std::size_t>(dev)];
+    if (!s) detail::cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "Model::forward_host");
+    return s;
+}
+
+struct Event {
+    cudaEvent_t e = nullptr;
+    Event() { detail::cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "Model::forward_host"); }
+    ~Event() {
+        if (e) cudaEventDestroy(e);
+    }
+    Event(const Event&) = delete;
+    Event& operator=(const Event&) = delete;
+    void record(cudaStream_t s) { detail::cuda(cudaEventRecord(e, s), "Model::forward_host"); }
+    void wait_in(cudaStream_t s) { detail::cuda(cudaStreamWaitEvent(s, e, 0), "Model::forward_host"); }
+};
+
+// On scope exit the compute stream waits for everything queued on the copy
+// stream, so buffers freed (stream-ordered) on the compute stream afterwards
+// -- on error paths too -- are no longer being copied.
+struct JoinCopies {
+    cudaStream_t cs;
+    Event done;
+    explicit JoinCopies(cudaStream_t c) : cs(c) {}
+    ~JoinCopies() {
+        if (cudaEventRecord(done.e, cs) != cudaSuccess ||
+            cudaStreamWaitEvent(detail::cstream(), done.e, 0) != cudaSuccess) {
+            cudaGetLastError();
+            cudaStreamSynchronize(cs);
+        }
+    }
+};
+
+// rows x cols of a device matrix (row stride dld) into host memory at row
+// stride ld, on stream s: one DMA when the strides match, else a device-side
+// repack into `pack` (rows x ld floats) first.
+void download_rows(float* host, std::size_t ld, const float* dev, std::size_t dld, std::size_t rows,
+                   std::size_t cols, float* pack, cudaStream_t s) {
+    if (!rows || !cols) return;
+    if (ld == dld) {
+        detail::cuda(cudaMemcpyAsync(host, dev, rows * ld * sizeof(float), cudaMemcpyDeviceToHost, s),
+                     "Model::forward_host");
+        return;
+    }
+    detail::cuda(cudaMemcpy2DAsync(pack, ld * sizeof(float), dev, dld * sizeof(float), cols * sizeof(float), rows,
+                                   cudaMemcpyDeviceToDevice, s),
+                 "Model::forward_host");
+    detail::cuda(cudaMemcpyAsync(host, pack, rows * ld * sizeof(float), cudaMemcpyDeviceToHost, s),
+                 "Model::forward_host");
+}
+
+}  // namespace
+
+void Model::forward_host(std::size_t n, std::size_t nnz, const int32_t* row_ptr, const int32_t* col_ind,
+                         const float* values, const float* features, std::size_t feature_cols,
+                         std::size_t ld_features, float* out, std::size_t out_cols, std::size_t ld_out) const {
+    if (layers_.empty()) throw std::runtime_error("Model::forward: no layers configured.");
+    if (!row_ptr || (nnz && !col_ind)) throw std::invalid_argument("Model::forward_host: null CSR array");
+    if (n && (!features || !out)) throw std::invalid_argument("Model::forward_host: null features or out");
+    if (ld_features < feature_cols) throw std::invalid_argument("Model::forward_host: ld_features < feature_cols");
+    if (ld_out < out_cols) throw std::invalid_argument("Model::forward_host: ld_out < out_cols");
+    if (nnz > static_cast<std::size_t>(INT32_MAX))
+        throw std::invalid_argument("Model::forward_host: nnz exceeds the int32 CSR limit");
+    bool need_norm = false, need_sl = false;
+    for (const auto& e : layers_) {
+        need_norm |= e.type == LayerEntry::Type::GCN;
+        need_sl |= e.type == LayerEntry::Type::GAT;
+    }
+    const cudaStream_t s = detail::cstream(), cs = copy_stream();
+    const bool first_scaled = layers_[0].type == LayerEntry::Type::GCN && fast_math() && n > 0;
+    const int blocks = first_scaled ? static_cast<int>(std::min<std::size_t>(kHostBlocks, n)) : 1;
+    const std::size_t width = n ? (n + static_cast<std::size_t>(blocks) - 1) / static_cast<std::size_t>(blocks) : 0;
+
+    // device buffers (stream-ordered on the compute stream; the CSR arrays
+    // pass to the adjacency tensor once it has been checked)
+    DevInts d_rp(n + 1), d_ci(nnz);
+    DevBuf d_v(nnz);
+    Tensor X = Tensor::dense_device(n, feature_cols);
+    const std::size_t ldx = X.device_ld();
+    std::unique_ptr<DevBuf> landing;
+    if (ld_features != ldx && n && feature_cols) landing = std::make_unique<DevBuf>(n * ld_features);
+    float* x_dst = landing ? landing->p : X.mutable_device_data();
+    Event allocated, csr_ready;
+    std::vector<std::unique_ptr<Event>> x_ready;
+    allocated.record(s);
+    JoinCopies join(cs);  // declared after the buffers: runs before they are freed
+    allocated.wait_in(cs);
+
+    // the uploads, all queued before any host wait
+    detail::cuda(cudaMemcpyAsync(d_rp.p, row_ptr, (n + 1) * sizeof(int32_t), cudaMemcpyHostToDevice, cs),
+                 "Model::forward_host");
+    if (nnz) {
+        detail::cuda(cudaMemcpyAsync(d_ci.p, col_ind, nnz * sizeof(int32_t), cudaMemcpyHostToDevice, cs),
+                     "Model::forward_host");
+        if (values)
+            detail::cuda(cudaMemcpyAsync(d_v.p, values, nnz * sizeof(float), cudaMemcpyHostToDevice, cs),
+                         "Model::forward_host");
+    }
+    csr_ready.record(cs);
+    for (int q = 0; q < blocks; ++q) {
+        const std::size_t a = std::min(n, static_cast<std::size_t>(q) * width), b = std::min(n, a + width);
+        if (b > a && feature_cols)
+            detail::cuda(cudaMemcpyAsync(x_dst + a * (landing ? ld_features : ldx), features + a * ld_features,
+                                         (b - a) * ld_features * sizeof(float), cudaMemcpyHostToDevice, cs),
+                         "Model::forward_host");
+        x_ready.push_back(std::make_unique<Event>());
+        x_ready.back()->record(cs);
+    }
+
+    // the adjacency: checked on the device as soon as it has landed
+    if (nnz && !values) tg::fill_f32(d_v.p, static_cast<int64_t>(nnz), 1.0f, s);
+    csr_ready.wait_in(s);
+    check(tg_csr_validate(static_cast<int64_t>(n), static_cast<int64_t>(n), static_cast<int64_t>(nnz), d_rp.p, d_ci.p,
+                          stream()));
+    Tensor A = TensorAccess::csr_from_device(n, n, d_rp.p, d_ci.p, d_v.p, nnz);
+    d_rp.p = nullptr;  // owned by A from here
+    d_ci.p = nullptr;
+    d_v.p = nullptr;
+    detail::ForwardGraphs g(A, need_norm, need_sl);
+
+    auto repack = [&](std::size_t a, std::size_t b) {
+        if (!landing || b <= a) return;
+        detail::cuda(cudaMemcpy2DAsync(X.mutable_device_data() + a * ldx, ldx * sizeof(float),
+                                       landing->p + a * ld_features, ld_features * sizeof(float),
+                                       feature_cols * sizeof(float), b - a, cudaMemcpyDeviceToDevice, s),
+                     "Model::forward_host");
+    };
+
+    Tensor H;
+    std::size_t first = 0;
+    if (first_scaled) {
+        // Layer 1 per feature block: Hs rows of block q = diag(dis) . X . W,
+        // then the gather pass over the columns of block q (passes in column
+        // order: each output element's chain keeps its stored order).
+        const GCNLayer& L = gcn_layers_[layers_[0].start_idx];
+        if (feature_cols != L.in_features())
+            throw std::invalid_argument("GCNLayer::forward: H has " + std::to_string(feature_cols) +
+                                        " columns but layer expects in_features=" + std::to_string(L.in_features()) +
+                                        ".");
+        const std::size_t Fo = L.out_features();
+        Tensor Hs = Tensor::dense_device(n, Fo);
+        Tensor o = Tensor::dense_device(n, Fo);
+        const std::size_t ldh = Hs.device_ld();
+        const int32_t* sp = blocks > 1 ? g.sg->split_points(blocks) : nullptr;
+        const detail::TrustedCsr trusted_csr;
+        for (int q = 0; q < blocks; ++q) {
+            const std::size_t a = std::min(n, static_cast<std::size_t>(q) * width), b = std::min(n, a + width);
+            x_ready[static_cast<std::size_t>(q)]->wait_in(s);
+            repack(a, b);
+            if (b > a)
+                check(tg_gemm_rowscale_f32(static_cast<int64_t>(b - a), static_cast<int64_t>(Fo),
+                                           static_cast<int64_t>(feature_cols), X.device_data() + a * ldx,
+                                           static_cast<int64_t>(ldx), L.weight().device_data(),
+                                           static_cast<int64_t>(L.weight().device_ld()),
+                                           Hs.mutable_device_data() + a * ldh, static_cast<int64_t>(ldh), g.sg->dis.p + a,
+                                           nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST, stream()));
+            check(tg_gcn_aggregate_f32(
+                static_cast<int64_t>(n), static_cast<int64_t>(n), static_cast<int64_t>(nnz), A.device_row_ptr(),
+                A.device_col_ind(), A.device_data(), Hs.device_data(), static_cast<int64_t>(Fo),
+                static_cast<int64_t>(ldh), Hs.device_data(), static_cast<int64_t>(ldh), g.sg->dis.p,
+                L.has_bias() ? L.bias().device_data() : nullptr,
+                L.activation() == Activation::ReLU ? TG_ACT_RELU : TG_ACT_NONE, o.mutable_device_data(),
+                static_cast<int64_t>(o.device_ld()), g.sg->order.p, sp ? sp + static_cast<std::size_t>(q) * n : nullptr,
+                sp ? sp + static_cast<std::size_t>(q + 1) * n : nullptr, q > 0, q == blocks - 1,
+                TG_FLAG_B_ROWS_PADDED, stream()));
+        }
+        if (layers_[0].post_act == InterActivation::ReLU) relu_inplace(o);
+        else if (layers_[0].post_act == InterActivation::ELU) elu_inplace(o);
+        H = std::move(o);
+        first = 1;
+    } else {
+        x_ready.back()->wait_in(s);
+        repack(0, n);
+    }
+    if (first_scaled) X = Tensor();  // not read again
+    else H = std::move(X);
+
+    const std::size_t last = layers_.size() - 1;
+    for (std::size_t li = first; li < last; ++li) H = run_layer(li, g, H);
+
+    // The last layer, then its output to the host.
+    const LayerEntry& e = layers_[last];
+    bool chunked = false;
+    std::size_t Fo = 0;
+    if (first <= last && e.type == LayerEntry::Type::GCN && g.sg && n >= 2 * kOutChunks &&
+        e.post_act == InterActivation::None) {
+        const GCNLayer& L = gcn_layers_[e.start_idx];
+        Fo = L.out_features();
+        chunked = H.format() == StorageFormat::Dense && H.cols() == L.in_features() && H.rows() == n &&
+                  n * detail::pad4(Fo) * sizeof(float) <= kPassBytes;
+    }
+    if (first <= last && !chunked) H = run_layer(last, g, H);
+    if (!chunked) {
+        if (H.cols() != out_cols)
+            throw std::invalid_argument("Model::forward_host: the last layer has " + std::to_string(H.cols()) +
+                                        " columns, out_cols is " + std::to_string(out_cols));
+        std::unique_ptr<DevBuf> pack;
+        if (ld_out != H.device_ld() && n && out_cols) pack = std::make_unique<DevBuf>(n * ld_out);
+        download_rows(out, ld_out, H.device_data(), H.device_ld(), n, out_cols, pack ? pack->p : nullptr, s);
+        detail::cuda(cudaStreamSynchronize(s), "Model::forward_host");
+        return;
+    }
+    if (Fo != out_cols)
+        throw std::invalid_argument("Model::forward_host: the last layer has " + std::to_string(Fo) +
+                                    " columns, out_cols is " + std::to_string(out_cols));
+    // One-pass FAST GCN layer in row chunks (row-offset views of the CSR,
+    // each chunk with its own longest-first schedule): per row the same
+    // arithmetic as one launch; chunk c's rows go back on the copy stream
+    // while chunk c + 1 gathers.
+    const GCNLayer& L = gcn_layers_[e.start_idx];
+    Tensor Hs = Tensor::dense_device(n, Fo);
+    const std::size_t ldh = Hs.device_ld();
+    check(tg_gemm_rowscale_f32(static_cast<int64_t>(n), static_cast<int64_t>(Fo), static_cast<int64_t>(H.cols()),
+                               H.device_data(), static_cast<int64_t>(H.device_ld()), L.weight().device_data(),
+                               static_cast<int64_t>(L.weight().device_ld()), Hs.mutable_device_data(),
+                               static_cast<int64_t>(ldh), g.sg->dis.p, nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST,
+                               stream()));
+    Tensor o = Tensor::dense_device(n, Fo);
+    const std::size_t ldo = o.device_ld();
+    std::unique_ptr<DevBuf> pack;
+    if (ld_out != ldo) pack = std::make_unique<DevBuf>(n * ld_out);
+    JoinCopies join_out(cs);  // the downloads read o and pack
+    const std::size_t step = (n + kOutChunks - 1) / kOutChunks;
+    DevInts order(n);
+    std::vector<std::unique_ptr<Event>> chunk_done;
+    const detail::TrustedCsr trusted_csr;
+    for (std::size_t a = 0; a < n; a += step) {
+        const std::size_t b = std::min(n, a + step);
+        const int64_t m = static_cast<int64_t>(b - a);
+        check(tg_csr_degree_order(m, A.device_row_ptr() + a, order.p + a, stream()));
+        check(tg_gcn_aggregate_f32(m, static_cast<int64_t>(n), static_cast<int64_t>(nnz), A.device_row_ptr() + a,
+                                   A.device_col_ind(), A.device_data(), Hs.device_data(), static_cast<int64_t>(Fo),
+                                   static_cast<int64_t>(ldh), Hs.device_data() + a * ldh, static_cast<int64_t>(ldh),
+                                   g.sg->dis.p + a, L.has_bias() ? L.bias().device_data() : nullptr,
+                                   L.activation() == Activation::ReLU ? TG_ACT_RELU : TG_ACT_NONE,
+                                   o.mutable_device_data() + a * ldo, static_cast<int64_t>(ldo), order.p + a, nullptr,
+                                   nullptr, 0, 1, TG_FLAG_B_ROWS_PADDED, stream()));
+        chunk_done.push_back(std::make_unique<Event>());
+        chunk_done.back()->record(s);
+        chunk_done.back()->wait_in(cs);
+        download_rows(out + a * ld_out, ld_out, o.device_data() + a * ldo, ldo, b - a, Fo,
+                      pack ? pack->p + a * ld_out : nullptr, cs);
+    }
+    Event copied;
+    copied.record(cs);
+    copied.wait_in(s);
+    detail::cuda(cudaStreamSynchronize(s), "Model::forward_host");
 }
 
 

@@ -565,6 +565,7 @@ class ShardedModel:
             if As.order is None:
                 As.order = ops.degree_order(As)
             self.scale = ops.gcn_norm_scale(As, out=self.scale_buf[:A.n_rows])
+            A.validated = A.validated or As.validated  # same arrays: checked once
             return As
         self.scale = None
         return gcn_norm_rows_scheduled(A, self.row0, self.R, self.comm, dis_all)

@@ -119,6 +119,20 @@ class HModel:
         check(lib.tg_model_forward(self.h, adjacency.h, features.h, C.byref(out)))
         return HTensor(out)
 
+    def forward_host(self, row_ptr, col_ind, values, features, feature_cols: int, out, out_cols: int):
+        """Model::forward from host arrays in one call (tg_model_forward_host):
+        the raw adjacency's CSR arrays (values None: unweighted) and the
+        features (rows x >= feature_cols, C-contiguous) in; the last layer's
+        output written into ``out`` (rows x >= out_cols).  Uploads overlap
+        the compute; pinned torch tensors copy at full PCIe rate."""
+        n = len(row_ptr) - 1
+        nnz = int(row_ptr[n]) if n else 0
+        ld_f = features.shape[1] if len(features.shape) == 2 else feature_cols
+        ld_o = out.shape[1] if len(out.shape) == 2 else out_cols
+        check(lib.tg_model_forward_host(self.h, n, nnz, _ptr(row_ptr), _ptr(col_ind), _ptr(values), _ptr(features),
+                                        feature_cols, ld_f, _ptr(out), out_cols, ld_o))
+        return out
+
     def free(self) -> None:
         if self.h:
             lib.tg_model_free(self.h)
