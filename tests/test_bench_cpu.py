@@ -28,7 +28,7 @@ def test_default_run_is_one_gpu_with_enough_warmup():
 
 def test_committed_traffic_is_the_full_size_capture():
     t = bench.committed_traffic("gather-gcn-L1-full-p1")
-    assert t == 2_542_193_408  # profiles/traffic.txt: both passes + hub-row kernel, full graph
+    assert t == 2_943_328_256  # profiles/traffic.txt: both passes + hub-row kernel, full graph
     assert bench.committed_traffic("no-such-kernel") is None
 
 

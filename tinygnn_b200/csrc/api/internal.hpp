@@ -47,6 +47,39 @@ struct TrustedCsr {
 
 inline std::size_t pad4(std::size_t n) { return (n + 3) / 4 * 4; }
 
+// Two weight matrices (same shape) as device arrays with ld == cols, the
+// layout tg_gemm_pair_f32 takes (Tensor rows are padded to 16 bytes).
+struct DevWeights {
+    const float* wn = nullptr;
+    const float* ws = nullptr;
+    float* owned = nullptr;
+    DevWeights(const Tensor& a, const Tensor& b) {
+        const std::size_t r = a.rows(), c = a.cols();
+        if (a.device_ld() == c && b.device_ld() == c) {
+            wn = a.device_data();
+            ws = b.device_data();
+            return;
+        }
+        void* q = nullptr;
+        detail::cuda(cudaMallocAsync(&q, (r * c > 0 ? 2 * r * c : 1) * sizeof(float), detail::cstream()),
+                     "tinygnn allocation");
+        owned = static_cast<float*>(q);
+        detail::cuda(cudaMemcpy2DAsync(owned, c * sizeof(float), a.device_data(), a.device_ld() * sizeof(float),
+                                       c * sizeof(float), r, cudaMemcpyDeviceToDevice, detail::cstream()),
+                     "SAGELayer weights");
+        detail::cuda(cudaMemcpy2DAsync(owned + r * c, c * sizeof(float), b.device_data(), b.device_ld() * sizeof(float),
+                                       c * sizeof(float), r, cudaMemcpyDeviceToDevice, detail::cstream()),
+                     "SAGELayer weights");
+        wn = owned;
+        ws = owned + r * c;
+    }
+    ~DevWeights() {
+        if (owned && cudaFreeAsync(owned, detail::cstream()) != cudaSuccess) cudaGetLastError();
+    }
+    DevWeights(const DevWeights&) = delete;
+    DevWeights& operator=(const DevWeights&) = delete;
+};
+
 inline std::string shape_str(std::size_t r, std::size_t c) {
     return "(" + std::to_string(r) + "\xC3\x97" + std::to_string(c) + ")";
 }

@@ -68,36 +68,6 @@ struct Contig {
 
 int act_code(Activation a) { return a == Activation::ReLU ? TG_ACT_RELU : TG_ACT_NONE; }
 
-// Two weight matrices (same shape) as device arrays with ld == cols, the
-// layout tg_gemm_pair_f32 takes (Tensor rows are padded to 16 bytes).
-struct DevWeights {
-    const float* wn = nullptr;
-    const float* ws = nullptr;
-    float* owned = nullptr;
-    DevWeights(const Tensor& a, const Tensor& b) {
-        const std::size_t r = a.rows(), c = a.cols();
-        if (a.device_ld() == c && b.device_ld() == c) {
-            wn = a.device_data();
-            ws = b.device_data();
-            return;
-        }
-        owned = dalloc<float>(2 * r * c);
-        detail::cuda(cudaMemcpy2DAsync(owned, c * sizeof(float), a.device_data(), a.device_ld() * sizeof(float),
-                                       c * sizeof(float), r, cudaMemcpyDeviceToDevice, detail::cstream()),
-                     "SAGELayer weights");
-        detail::cuda(cudaMemcpy2DAsync(owned + r * c, c * sizeof(float), b.device_data(), b.device_ld() * sizeof(float),
-                                       c * sizeof(float), r, cudaMemcpyDeviceToDevice, detail::cstream()),
-                     "SAGELayer weights");
-        wn = owned;
-        ws = owned + r * c;
-    }
-    ~DevWeights() {
-        if (owned && cudaFreeAsync(owned, detail::cstream()) != cudaSuccess) cudaGetLastError();
-    }
-    DevWeights(const DevWeights&) = delete;
-    DevWeights& operator=(const DevWeights&) = delete;
-};
-
 void check_weight(const Tensor& w, std::size_t in, std::size_t out, const std::string& who) {
     if (w.format() != StorageFormat::Dense) throw std::invalid_argument(who + ": weight must be Dense.");
     if (w.rows() != in || w.cols() != out)
@@ -266,7 +236,7 @@ Tensor SAGELayer::forward(const Tensor& A, const Tensor& H) const {
     if (fast_math() && !max && Fi > Fo) {  // transform first: gather F_out instead of F_in floats per edge
         // W_neigh and W_self in one tensor-core pass over H (weights are dense with ld == cols)
         Tensor Tn = Tensor::dense_device(N, Fo), Ts = Tensor::dense_device(N, Fo);
-        DevWeights w(weight_neigh_, weight_self_);
+        detail::DevWeights w(weight_neigh_, weight_self_);
         check(tg_gemm_pair_f32(static_cast<int64_t>(N), static_cast<int64_t>(Fo), static_cast<int64_t>(Fi),
                                H.device_data(), static_cast<int64_t>(H.device_ld()), w.wn, w.ws,
                                static_cast<int64_t>(Fo), Tn.mutable_device_data(), static_cast<int64_t>(Tn.device_ld()),

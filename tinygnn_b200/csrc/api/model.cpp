@@ -787,16 +787,13 @@ Tensor Model::forward_rows(const Tensor& A, std::size_t n, const Tensor& X, RowE
                 const std::size_t ld = detail::pad4(Fo);
                 Gathered full(static_cast<std::size_t>(P), R, ld);
                 Tensor Ts = Tensor::dense_device(rows, Fo);
-                if (rows) {
-                    check(tg_gemm_f32(M, static_cast<int64_t>(Fo), static_cast<int64_t>(Fi), in->device_data(),
-                                      static_cast<int64_t>(in->device_ld()), L.weight_neigh().device_data(),
-                                      static_cast<int64_t>(L.weight_neigh().device_ld()), full.block(r),
-                                      static_cast<int64_t>(ld), nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST, stream()));
-                    check(tg_gemm_f32(M, static_cast<int64_t>(Fo), static_cast<int64_t>(Fi), in->device_data(),
-                                      static_cast<int64_t>(in->device_ld()), L.weight_self().device_data(),
-                                      static_cast<int64_t>(L.weight_self().device_ld()), Ts.mutable_device_data(),
-                                      static_cast<int64_t>(Ts.device_ld()), nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST,
-                                      stream()));
+                if (rows) {  // both products in one pass over H (column-split epilogue)
+                    const detail::DevWeights w(L.weight_neigh(), L.weight_self());
+                    check(tg_gemm_pair_f32(M, static_cast<int64_t>(Fo), static_cast<int64_t>(Fi), in->device_data(),
+                                           static_cast<int64_t>(in->device_ld()), w.wn, w.ws,
+                                           static_cast<int64_t>(Fo), full.block(r), static_cast<int64_t>(ld),
+                                           Ts.mutable_device_data(), static_cast<int64_t>(Ts.device_ld()),
+                                           TG_MODE_FAST, stream()));
                 }
                 ex.all_gather(full.buf.p, R * ld);
                 if (rows)
