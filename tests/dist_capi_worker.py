@@ -47,7 +47,9 @@ def main() -> int:
                 time.sleep(0.05)
             got = np.concatenate([np.load(os.path.join(out_dir, f"part{int(fast)}_{q}.npy")) for q in range(world)])
             same = bool(np.array_equal(got.view(np.uint32), full.view(np.uint32)))
-            print(f"fast={fast} same={same}", flush=True)
+            R = -(-n // world)
+            blocks = [float(np.abs(got[q * R:(q + 1) * R] - full[q * R:(q + 1) * R]).max()) for q in range(world)]
+            print(f"fast={fast} same={same} max |diff| per rank block {blocks}", flush=True)
             ok = ok and same
     d.finalize()
     if rank == 0:

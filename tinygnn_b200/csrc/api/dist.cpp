@@ -95,6 +95,18 @@ struct tg_dist_s : tinygnn::RowExchange {
     int world_ = 1, rank_ = 0, device = 0;
     int timeout_ms = 60000;
     bool aborted = false;
+    // NCCL runs on a stream of its own, ordered against the calling thread's
+    // stream by events: the per-thread default stream is a pseudo-handle
+    // that names a different stream in whichever thread uses it, and NCCL
+    // may enqueue a non-blocking communicator's work from its own thread.
+    cudaStream_t ns = nullptr;
+    cudaEvent_t ready = nullptr, gathered = nullptr;
+
+    ~tg_dist_s() {
+        if (gathered) cudaEventDestroy(gathered);
+        if (ready) cudaEventDestroy(ready);
+        if (ns) cudaStreamDestroy(ns);
+    }
 
     int world() const override { return world_; }
     int rank() const override { return rank_; }
@@ -128,14 +140,20 @@ struct tg_dist_s : tinygnn::RowExchange {
         if (aborted || !comm) throw NcclError(TG_ERR_NCCL, "tg_dist: the communicator was aborted");
         if (world_ == 1) return;
         const float* mine = buf + static_cast<std::size_t>(rank_) * count;
-        settle(nccl().allGather(mine, buf, count, ncclFloat, comm, tinygnn::detail::cstream()), "all-gather");
+        const cudaStream_t cs = tinygnn::detail::cstream();
+        tinygnn::detail::cuda(cudaEventRecord(ready, cs), "tg_dist all-gather");
+        tinygnn::detail::cuda(cudaStreamWaitEvent(ns, ready, 0), "tg_dist all-gather");
+        settle(nccl().allGather(mine, buf, count, ncclFloat, comm, ns), "all-gather");
+        tinygnn::detail::cuda(cudaEventRecord(gathered, ns), "tg_dist all-gather");
+        tinygnn::detail::cuda(cudaStreamWaitEvent(cs, gathered, 0), "tg_dist all-gather");
     }
 
     // Waits for the calling thread's stream, watching the communicator.
     void drain(const char* what) {
         const auto deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
         for (;;) {
-            const cudaError_t e = cudaStreamQuery(tinygnn::detail::cstream());
+            cudaError_t e = cudaStreamQuery(tinygnn::detail::cstream());
+            if (e == cudaSuccess && ns) e = cudaStreamQuery(ns);
             if (e == cudaSuccess) return;
             if (e != cudaErrorNotReady) tinygnn::detail::cuda(e, what);
             ncclResult_t st = ncclSuccess;
@@ -218,6 +236,9 @@ TG_API tg_status tg_dist_init(int32_t world, int32_t rank, int32_t device, const
         d->rank_ = rank;
         d->device = device;
         d->timeout_ms = timeout_ms;
+        tinygnn::detail::cuda(cudaStreamCreateWithFlags(&d->ns, cudaStreamNonBlocking), "tg_dist_init");
+        tinygnn::detail::cuda(cudaEventCreateWithFlags(&d->ready, cudaEventDisableTiming), "tg_dist_init");
+        tinygnn::detail::cuda(cudaEventCreateWithFlags(&d->gathered, cudaEventDisableTiming), "tg_dist_init");
         ncclUniqueId id;
         const std::string path(id_path);
         if (rank == 0) {
