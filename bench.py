@@ -789,18 +789,26 @@ def run_micro_l2(args):
         Fp = (F + 3) // 4 * 4
         n_cols = (64 << 20) // (Fp * 4)
         rp = np.arange(rows + 1, dtype=np.int64) * per_row
-        ci = np.sort(rng.integers(0, n_cols, (rows, per_row), dtype=np.int64), axis=1).astype(np.int32).ravel()
-        A = tg.CSR.from_numpy(rp.astype(np.int32), ci, np.ones(ci.size, np.float32), n_cols=n_cols)
-        A = A.with_degree_order()
-        B = torch.randn(n_cols, Fp, device="cuda")[:, :F]
-        out = torch.empty(rows, F, device="cuda")
-        ms = _gpu_ms(lambda: tg.spmm(A, B, out=out), reps=reps)
-        nnz = rows * per_row
-        print(json.dumps({"micro": "l2_gather", "features": F, "operand_mb": n_cols * Fp * 4 / 2**20,
-                          "entries": nnz, "ms_per_call": ms,
-                          "operand_tb_s": nnz * F * 4 / (ms * 1e-3) / 1e12,
-                          "with_indices_tb_s": nnz * (F * 4 + 8) / (ms * 1e-3) / 1e12}))
-        del A, B, out
+        # "uniform": random rows; "sequential": row i reads rows i*320 .. i*320+319
+        # (mod n_cols) -- every 128-byte line of the operand used whole, the
+        # L2 read rate with perfect locality
+        for pattern in ("uniform", "sequential"):
+            if pattern == "uniform":
+                ci = np.sort(rng.integers(0, n_cols, (rows, per_row), dtype=np.int64), axis=1)
+            else:
+                ci = np.sort((np.arange(rows * per_row, dtype=np.int64) % n_cols).reshape(rows, per_row), axis=1)
+            ci = ci.astype(np.int32).ravel()
+            A = tg.CSR.from_numpy(rp.astype(np.int32), ci, np.ones(ci.size, np.float32), n_cols=n_cols)
+            A = A.with_degree_order()
+            B = torch.randn(n_cols, Fp, device="cuda")[:, :F]
+            out = torch.empty(rows, F, device="cuda")
+            ms = _gpu_ms(lambda: tg.spmm(A, B, out=out), reps=reps)
+            nnz = rows * per_row
+            print(json.dumps({"micro": "l2_gather", "pattern": pattern, "features": F,
+                              "operand_mb": n_cols * Fp * 4 / 2**20, "entries": nnz, "ms_per_call": ms,
+                              "operand_tb_s": nnz * F * 4 / (ms * 1e-3) / 1e12,
+                              "with_indices_tb_s": nnz * (F * 4 + 8) / (ms * 1e-3) / 1e12}))
+            del A, B, out
     tg.ops.take_device_error()
     return 0
 

@@ -137,6 +137,21 @@ struct TcArgs {
     int tma_store;
 };
 
+// The activation of V values, the choice made once for all of them (the
+// epilogue's per-element switch over every activation had cost ~2k cycles
+// per 16 columns: 17k of a 128 x 128 tile's ~50k cycles).
+template <int V>
+__device__ __forceinline__ void act_v(float (&v)[V], int act, float alpha) {
+    if (act == TG_ACT_NONE) return;
+    if (act == TG_ACT_RELU) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;  // apply_act's ReLU
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < V; ++j) v[j] = apply_act(act, v[j], alpha);
+}
+
 // PEERS: the epilogue also stores to peer copies (and may use 16-byte
 // stores); false compiles the lean local-only epilogue.
 template <int BN, int STAGES_, bool PEERS>
@@ -262,6 +277,9 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             constexpr int kBoxes = (BN + 31) / 32;  // 32 x 32 boxes per warp (a box is 4 KB whatever BN)
             float* stage = reinterpret_cast<float*>(&s) + static_cast<size_t>(q) * kBoxes * 1024;  // the idle ring
             const float sc = (g.rs && row < g.M) ? __ldg(g.rs + row) : 1.0f;
+            const bool has_rs = g.rs != nullptr, has_bias = g.bias != nullptr;
+            const int act = g.act;
+            const float alpha = g.alpha;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 uint32_t r[16];
@@ -275,13 +293,16 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 float v[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int col = c0 + j;
-                    float x = __uint_as_float(r[j]);
-                    if (g.rs) x = __fmul_rn(x, sc);
-                    if (g.bias) x = __fadd_rn(x, col < g.N ? __ldg(g.bias + col) : 0.0f);
-                    v[j] = apply_act(g.act, x, g.alpha);
+                for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+                if (has_rs) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = __fmul_rn(v[j], sc);
                 }
+                if (has_bias) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], c0 + j < g.N ? __ldg(g.bias + c0 + j) : 0.0f);
+                }
+                act_v<16>(v, act, alpha);
                 float* box = stage + (c0 / 32) * 1024;  // 32 rows x 32 floats
                 const int cb = (c0 % 32) / 4;           // first 16-byte chunk of these 16 columns
 #pragma unroll
@@ -323,6 +344,9 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             static_assert(BM * (BN + 4) <= STAGES * (2 * BM * BK + 2 * BN * BK), "staging tile exceeds the ring");
             const bool vec = PEERS && g.vec;
             const int SB = vec ? BN + 4 : BN + 1;
+            const bool has_rs = g.rs != nullptr, has_bias = g.bias != nullptr;
+            const int act = g.act;
+            const float alpha = g.alpha;
             float* tile = reinterpret_cast<float*>(&s) + static_cast<size_t>(q) * 32 * SB;  // the ring's start
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -366,23 +390,18 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                     for (int k = 0; k < V4; ++k) {
                         const int col = (lane + 32 * k) * 4;
                         if (col < g.ncols) {
-                            float4 v = *reinterpret_cast<const float4*>(tile + rr * SB + col);
-                            if (g.rs) {
-                                v.x = __fmul_rn(v.x, sc);
-                                v.y = __fmul_rn(v.y, sc);
-                                v.z = __fmul_rn(v.z, sc);
-                                v.w = __fmul_rn(v.w, sc);
+                            const float4 t4 = *reinterpret_cast<const float4*>(tile + rr * SB + col);
+                            float x[4] = {t4.x, t4.y, t4.z, t4.w};
+                            if (has_rs) {
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) x[e] = __fmul_rn(x[e], sc);
                             }
-                            if (g.bias) {
-                                v.x = __fadd_rn(v.x, bv[k][0]);
-                                v.y = __fadd_rn(v.y, bv[k][1]);
-                                v.z = __fadd_rn(v.z, bv[k][2]);
-                                v.w = __fadd_rn(v.w, bv[k][3]);
+                            if (has_bias) {
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) x[e] = __fadd_rn(x[e], bv[k][e]);
                             }
-                            v.x = apply_act(g.act, v.x, g.alpha);
-                            v.y = apply_act(g.act, v.y, g.alpha);
-                            v.z = apply_act(g.act, v.z, g.alpha);
-                            v.w = apply_act(g.act, v.w, g.alpha);
+                            act_v<4>(x, act, alpha);
+                            const float4 v = make_float4(x[0], x[1], x[2], x[3]);
                             *reinterpret_cast<float4*>(g.C + off + col) = v;
                             // The same row into every peer's copy of the output (NVLink stores).
                             if (PEERS)
@@ -408,10 +427,11 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                     for (int k = 0; k < CPL; ++k) {
                         const int col = lane + 32 * k;
                         if (col < g.N) {
-                            float v = tile[rr * SB + col];
-                            if (g.rs) v = __fmul_rn(v, sc);
-                            if (g.bias) v = __fadd_rn(v, bv[k]);
-                            v = apply_act(g.act, v, g.alpha);
+                            float x[1] = {tile[rr * SB + col]};
+                            if (has_rs) x[0] = __fmul_rn(x[0], sc);
+                            if (has_bias) x[0] = __fadd_rn(x[0], bv[k]);
+                            act_v<1>(x, act, alpha);
+                            const float v = x[0];
                             if (!PEERS && col >= g.nsplit) {
                                 g.C2[row * g.ldc2 + (col - g.nsplit)] = v;
                                 continue;
@@ -660,10 +680,11 @@ __global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant_
 #pragma unroll 4
                 for (int rr = 0; rr < rows; ++rr) {
                     if (col < g.ncols) {
-                        float v = buf[rr * 33 + lane];
-                        if (g.rs) v = __fmul_rn(v, __ldg(g.rs + r0 + rr));
-                        if (g.bias) v = __fadd_rn(v, bv);
-                        v = apply_act(g.act, v, g.alpha);
+                        float x[1] = {buf[rr * 33 + lane]};
+                        if (g.rs) x[0] = __fmul_rn(x[0], __ldg(g.rs + r0 + rr));
+                        if (g.bias) x[0] = __fadd_rn(x[0], bv);
+                        act_v<1>(x, g.act, g.alpha);
+                        const float v = x[0];
                         const int64_t off = (r0 + rr) * g.ldc + col;
                         g.C[off] = v;
                         for (int p = 0; p < peers.n; ++p) peers.c[p][off] = v;
