@@ -166,4 +166,20 @@ __device__ __forceinline__ float apply_act(int act, float x, float alpha) {
     }
 }
 
+// The activation of V values, the choice made once for all of them: an
+// epilogue that called apply_act per element paid its switch (and the code
+// of every activation) per value -- ~2k cycles per 16 columns in the
+// tensor-core GEMM's epilogue.
+template <int V>
+__device__ __forceinline__ void act_v(float (&v)[V], int act, float alpha) {
+    if (act == TG_ACT_NONE) return;
+    if (act == TG_ACT_RELU) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;  // apply_act's ReLU
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < V; ++j) v[j] = apply_act(act, v[j], alpha);
+}
+
 }  // namespace tg

@@ -178,14 +178,17 @@ struct GatLane {
         for (int s = 0; s < SPL; ++s) {
             if (!live[s]) continue;
             const float inv = ssum[s] > 0.0f ? __fdiv_rn(1.0f, ssum[s]) : 0.0f;
+            float v[VEC];
 #pragma unroll
-            for (int k = 0; k < VEC; ++k) {
-                float v = __fmul_rn(acc[s][k], inv);
-                if (a.bias) v = __fadd_rn(v, __ldg(a.bias + fo[s] + k));
-                v = apply_act(a.act, v, 0.0f);
-                v = apply_act(a.post, v, 1.0f);  // ELU alpha 1 (Model's inter-layer ELU)
-                a.out[row * a.ldo + fo[s] + k] = v;
+            for (int k = 0; k < VEC; ++k) v[k] = __fmul_rn(acc[s][k], inv);
+            if (a.bias) {
+#pragma unroll
+                for (int k = 0; k < VEC; ++k) v[k] = __fadd_rn(v[k], __ldg(a.bias + fo[s] + k));
             }
+            act_v<VEC>(v, a.act, 0.0f);
+            act_v<VEC>(v, a.post, 1.0f);  // ELU alpha 1 (Model's inter-layer ELU)
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) a.out[row * a.ldo + fo[s] + k] = v[k];
         }
     }
 };

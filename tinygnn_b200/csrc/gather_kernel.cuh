@@ -146,15 +146,24 @@ __device__ __forceinline__ void finish_acc(const GatherArgs& a, int64_t row, int
         }
     }
 #pragma unroll
-    for (int k = 0; k < VEC; ++k) {
-        float v = acc[k];
-        if (OP == GATHER_MAX && deg == 0) v = 0.0f;
-        if (OP == GATHER_SUM && a.mean && deg > 0) v = __fmul_rn(v, inv_deg);
-        if (a.self) v = __fadd_rn(v, sv[k]);
-        if (a.row_scale) v = __fmul_rn(v, rs);
-        if (a.bias) v = __fadd_rn(v, bv[k]);
-        x[k] = apply_act(a.act, v, a.alpha);
+    for (int k = 0; k < VEC; ++k) x[k] = (OP == GATHER_MAX && deg == 0) ? 0.0f : acc[k];
+    if (OP == GATHER_SUM && a.mean && deg > 0) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) x[k] = __fmul_rn(x[k], inv_deg);
     }
+    if (a.self) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) x[k] = __fadd_rn(x[k], sv[k]);
+    }
+    if (a.row_scale) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) x[k] = __fmul_rn(x[k], rs);
+    }
+    if (a.bias) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) x[k] = __fadd_rn(x[k], bv[k]);
+    }
+    act_v<VEC>(x, a.act, a.alpha);
     if (vec_io) {
         stv<VEC>(a.C + row * a.ldc + fo, x);
     } else {

@@ -144,14 +144,21 @@ __global__ void __launch_bounds__(256) gemm_exact_kernel(const GemmArgs g) {
     for (int i = 0; i < TM; ++i) {
         const int64_t m = m0 + ty * TM + i;
         if (m >= g.M) break;
+        float v[TN];
+#pragma unroll
+        for (int j = 0; j < TN; ++j) v[j] = acc[i][j];
+        if (g.bias) {
+#pragma unroll
+            for (int j = 0; j < TN; ++j) {
+                const int64_t n = n0 + tx * TN + j;
+                v[j] = __fadd_rn(v[j], n < g.N ? __ldg(g.bias + n) : 0.0f);
+            }
+        }
+        act_v<TN>(v, g.act, g.alpha);
 #pragma unroll
         for (int j = 0; j < TN; ++j) {
             const int64_t n = n0 + tx * TN + j;
-            if (n < g.N) {
-                float v = acc[i][j];
-                if (g.bias) v = __fadd_rn(v, __ldg(g.bias + n));
-                g.C[m * g.ldc + n] = apply_act(g.act, v, g.alpha);
-            }
+            if (n < g.N) g.C[m * g.ldc + n] = v[j];
         }
     }
 }

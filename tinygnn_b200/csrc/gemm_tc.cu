@@ -137,21 +137,6 @@ struct TcArgs {
     int tma_store;
 };
 
-// The activation of V values, the choice made once for all of them (the
-// epilogue's per-element switch over every activation had cost ~2k cycles
-// per 16 columns: 17k of a 128 x 128 tile's ~50k cycles).
-template <int V>
-__device__ __forceinline__ void act_v(float (&v)[V], int act, float alpha) {
-    if (act == TG_ACT_NONE) return;
-    if (act == TG_ACT_RELU) {
-#pragma unroll
-        for (int j = 0; j < V; ++j) v[j] = v[j] > 0.0f ? v[j] : 0.0f;  // apply_act's ReLU
-        return;
-    }
-#pragma unroll
-    for (int j = 0; j < V; ++j) v[j] = apply_act(act, v[j], alpha);
-}
-
 // PEERS: the epilogue also stores to peer copies (and may use 16-byte
 // stores); false compiles the lean local-only epilogue.
 template <int BN, int STAGES_, bool PEERS>
