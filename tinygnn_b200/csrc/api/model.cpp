@@ -13,6 +13,7 @@
 #include "tinygnn/model.hpp"
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <utility>
@@ -385,11 +386,23 @@ namespace {
 // Feature row blocks (and layer-1 column passes) of the host-input forward
 // when its first layer is a FAST GCN layer: the GEMM and gather pass of
 // block q overlap the upload of block q + 1, and the gather work left after
-// the last block has landed is one block's pass.
-constexpr int kHostBlocks = 8;
-// Row chunks of the last layer's gather (one-pass FAST GCN layers): chunk
-// c's output crosses PCIe while chunk c + 1 gathers.
-constexpr int kOutChunks = 2;
+// the last block has landed is one block's pass.  Row chunks of the last
+// layer's gather (one-pass FAST GCN layers): chunk c's output crosses PCIe
+// while chunk c + 1 gathers.  TINYGNN_B200_HOST_BLOCKS /
+// TINYGNN_B200_HOST_OUT_CHUNKS override the counts.
+int env_count(const char* name, int dflt) {
+    const char* e = std::getenv(name);
+    const int v = e ? std::atoi(e) : 0;
+    return v > 0 && v <= 64 ? v : dflt;
+}
+int host_blocks() {
+    static const int v = env_count("TINYGNN_B200_HOST_BLOCKS", 16);
+    return v;
+}
+int out_chunks() {
+    static const int v = env_count("TINYGNN_B200_HOST_OUT_CHUNKS", 2);
+    return v;
+}
 
 // The calling thread's copy stream on the current device (non-blocking, so
 // it runs beside the per-thread default stream the compute uses).
@@ -468,21 +481,26 @@ void Model::forward_host(std::size_t n, std::size_t nnz, const int32_t* row_ptr,
     }
     const cudaStream_t s = detail::cstream(), cs = copy_stream();
     const bool first_scaled = layers_[0].type == LayerEntry::Type::GCN && fast_math() && n > 0;
-    const int blocks = first_scaled ? static_cast<int>(std::min<std::size_t>(kHostBlocks, n)) : 1;
+    const int blocks = first_scaled ? static_cast<int>(std::min<std::size_t>(host_blocks(), n)) : 1;
     const std::size_t width = n ? (n + static_cast<std::size_t>(blocks) - 1) / static_cast<std::size_t>(blocks) : 0;
 
     // device buffers (stream-ordered on the compute stream; the CSR arrays
     // pass to the adjacency tensor once it has been checked)
     DevInts d_rp(n + 1), d_ci(nnz);
     DevBuf d_v(nnz);
-    Tensor X = Tensor::dense_device(n, feature_cols);
-    const std::size_t ldx = X.device_ld();
+    const std::size_t ldx = detail::pad4(feature_cols);
     std::unique_ptr<DevBuf> landing;
     if (ld_features != ldx && n && feature_cols) landing = std::make_unique<DevBuf>(n * ld_features);
-    float* x_dst = landing ? landing->p : X.mutable_device_data();
     Event allocated, csr_ready;
     std::vector<std::unique_ptr<Event>> x_ready;
-    allocated.record(s);
+    // The copies may start once their destinations exist; the features'
+    // device tensor (zero-filled: 0.1 ms for 561 MB) is created after that
+    // point when they land in a separate buffer first.
+    Tensor X;
+    if (landing) allocated.record(s);
+    X = Tensor::dense_device(n, feature_cols);
+    if (!landing) allocated.record(s);
+    float* x_dst = landing ? landing->p : X.mutable_device_data();
     JoinCopies join(cs);  // declared after the buffers: runs before they are freed
     allocated.wait_in(cs);
 
@@ -582,7 +600,8 @@ void Model::forward_host(std::size_t n, std::size_t nnz, const int32_t* row_ptr,
     const LayerEntry& e = layers_[last];
     bool chunked = false;
     std::size_t Fo = 0;
-    if (first <= last && e.type == LayerEntry::Type::GCN && g.sg && n >= 2 * kOutChunks &&
+    const int chunks = out_chunks();
+    if (first <= last && e.type == LayerEntry::Type::GCN && g.sg && n >= 2 * static_cast<std::size_t>(chunks) &&
         e.post_act == InterActivation::None) {
         const GCNLayer& L = gcn_layers_[e.start_idx];
         Fo = L.out_features();
@@ -620,7 +639,7 @@ void Model::forward_host(std::size_t n, std::size_t nnz, const int32_t* row_ptr,
     std::unique_ptr<DevBuf> pack;
     if (ld_out != ldo) pack = std::make_unique<DevBuf>(n * ld_out);
     JoinCopies join_out(cs);  // the downloads read o and pack
-    const std::size_t step = (n + kOutChunks - 1) / kOutChunks;
+    const std::size_t step = (n + static_cast<std::size_t>(chunks) - 1) / static_cast<std::size_t>(chunks);
     DevInts order(n);
     std::vector<std::unique_ptr<Event>> chunk_done;
     const detail::TrustedCsr trusted_csr;

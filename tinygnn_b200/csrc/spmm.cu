@@ -220,38 +220,42 @@ __global__ void order_count_kernel(int64_t M, const int32_t* rp, int32_t* counts
 }
 
 // Single-block exclusive scan over n ints, in place (n = NBUCKET * nblocks).
+// Thread t owns one contiguous run of ceil(n / blockDim) entries: it sums
+// its run, the block scans the 1024 run sums once (warp shuffles, then the
+// warp totals), and each thread writes its run's prefixes -- two passes over
+// the 117 KB of counts and three barriers, where a block-wide step per 1024
+// entries had taken ~30 us on the Reddit-shaped graph.
 __global__ void order_scan_kernel(int32_t* x, int64_t n) {
     __shared__ int32_t warp_sums[32];
-    __shared__ int32_t carry;
-    if (threadIdx.x == 0) carry = 0;
+    const int64_t per = (n + blockDim.x - 1) / blockDim.x;
+    const int64_t b = static_cast<int64_t>(threadIdx.x) * per;
+    const int64_t e = b + per < n ? b + per : n;
+    int32_t sum = 0;
+    for (int64_t i = b; i < e; ++i) sum += x[i];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int32_t incl = sum;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int32_t t = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += t;
+    }
+    if (lane == 31) warp_sums[w] = incl;
     __syncthreads();
-    for (int64_t base = 0; base < n; base += blockDim.x) {
-        const int64_t i = base + threadIdx.x;
-        const int32_t v = i < n ? x[i] : 0;
-        int32_t incl = v;
-        const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (w == 0) {
+        int32_t ws = lane < static_cast<int>(blockDim.x >> 5) ? warp_sums[lane] : 0;
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
-            const int32_t t = __shfl_up_sync(0xffffffffu, incl, d);
-            if (lane >= d) incl += t;
+            const int32_t t = __shfl_up_sync(0xffffffffu, ws, d);
+            if (lane >= d) ws += t;
         }
-        if (lane == 31) warp_sums[w] = incl;
-        __syncthreads();
-        if (w == 0) {
-            int32_t ws = lane < (blockDim.x >> 5) ? warp_sums[lane] : 0;
-#pragma unroll
-            for (int d = 1; d < 32; d <<= 1) {
-                const int32_t t = __shfl_up_sync(0xffffffffu, ws, d);
-                if (lane >= d) ws += t;
-            }
-            warp_sums[lane] = ws;  // inclusive over warps
-        }
-        __syncthreads();
-        const int32_t warp_off = w ? warp_sums[w - 1] : 0;
-        if (i < n) x[i] = carry + warp_off + incl - v;
-        __syncthreads();
-        if (threadIdx.x == blockDim.x - 1) carry += warp_off + incl;
-        __syncthreads();
+        warp_sums[lane] = ws;  // inclusive over warps
+    }
+    __syncthreads();
+    int32_t run = (w ? warp_sums[w - 1] : 0) + incl - sum;  // exclusive prefix of this thread's run
+    for (int64_t i = b; i < e; ++i) {
+        const int32_t v = x[i];
+        x[i] = run;
+        run += v;
     }
 }
 
