@@ -901,7 +901,30 @@ def run_suite(args):
     ms = _gpu_ms(cora, reps=200, warm=10)
     spec = [dict(type="gcn", **{"in": 1433, "out": 16}, act="relu"), dict(type="gcn", **{"in": 16, "out": 7})]
     w = {"layer0.weight": h(W0), "layer0.bias": h(b0), "layer1.weight": h(W1), "layer1.bias": h(b1)}
-    emit({"suite": "gcn-cora-shape", "nodes": n, "nnz_norm": int(tg.gcn_norm(A).nnz), "gpu_ms": ms},
+    # The same forward recorded once as a CUDA graph (tg_model_capture, FAST)
+    # and replayed: one graph launch instead of ~20 kernel launches; each
+    # tg_graph_replay call returns when the forward has finished.
+    from tinygnn_b200.handles import HModel, HTensor, set_fast_math
+    prev_fast = set_fast_math(True)
+    hm = HModel().add_gcn(1433, 16, act="relu").add_gcn(16, 7, act=None)
+    hm.load_weights(w)
+    At = HTensor.csr(n, n, h(rp).astype(np.int32), h(ci).astype(np.int32), h(v).astype(np.float32))
+    Xt = HTensor.dense(np.ascontiguousarray(h(X), dtype=np.float32), n, 1433)
+    graph = hm.capture(At, Xt)
+    for _ in range(10):
+        graph.replay()
+    reps = 500
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        graph.replay()
+    graph_ms = (time.perf_counter() - t0) / reps * 1e3
+    graph.free()
+    hm.free()
+    set_fast_math(prev_fast)
+    emit({"suite": "gcn-cora-shape", "nodes": n, "nnz_norm": int(tg.gcn_norm(A).nnz), "gpu_ms": ms,
+          "gpu_ms_graph_replay": graph_ms,
+          "graph_replay": "Model::forward (FAST gcn_norm scale, both layers) recorded by tg_model_capture, "
+                          "host-timed synchronous tg_graph_replay calls (launch + run + wait)"},
          *_ref_model_runner(spec, w, n, rp, ci, v, X))
 
     # 2. spmm, R-MAT 2^20 / 2^24 draws, values U(0,1], F in {16, 64, 128, 256}

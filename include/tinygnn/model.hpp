@@ -14,6 +14,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <memory>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -43,6 +44,31 @@ WeightFile load_weight_file(const std::string& path);
 namespace detail {
 struct ForwardGraphs;  // the adjacency variants one forward call uses
 }
+
+// A Model::forward recorded once as a CUDA graph and replayed (no
+// counterpart in the reference).  For small graphs a forward is a couple of
+// dozen short kernels whose launches cost more than their work; a replay
+// issues them as one graph launch.  The graph reads the adjacency and
+// feature tensors it was captured with -- their device memory, with
+// whatever it holds at replay time -- so those tensors must outlive it and
+// keep their shapes; the output lives in the graph's own tensor.
+class ForwardGraph {
+public:
+    ForwardGraph();
+    ForwardGraph(ForwardGraph&&) noexcept;
+    ForwardGraph& operator=(ForwardGraph&&) noexcept;
+    ~ForwardGraph();
+    // Runs the captured forward again on the calling thread's stream and
+    // returns its output (complete when the stream reaches it).
+    const Tensor& replay();
+    const Tensor& output() const;
+
+    struct Impl;
+
+private:
+    friend class Model;
+    std::unique_ptr<Impl> impl_;
+};
 
 // The exchange step of a row-partitioned forward (no counterpart in the
 // reference): `world` processes, each holding one equal block of
@@ -108,6 +134,13 @@ public:
     void forward_host(std::size_t n, std::size_t nnz, const int32_t* row_ptr, const int32_t* col_ind,
                       const float* values, const float* features, std::size_t feature_cols,
                       std::size_t ld_features, float* out, std::size_t out_cols, std::size_t ld_out) const;
+
+    // forward(adjacency, features) recorded as a CUDA graph after one eager
+    // run (no counterpart in the reference).  Every call the forward makes
+    // must be asynchronous: FAST-mode GCN and SAGE layers are; EXACT
+    // gcn_norm and GAT's self-loops read a size back to the host, and their
+    // capture is refused (std::runtime_error).  Output equals forward()'s.
+    ForwardGraph capture(const Tensor& adjacency, const Tensor& features) const;
 
 private:
     Tensor run_layer(std::size_t li, detail::ForwardGraphs& g, const Tensor& in) const;

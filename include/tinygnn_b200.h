@@ -550,6 +550,20 @@ TG_API tg_status tg_model_forward_host(tg_model m, int64_t n, int64_t nnz, const
                                        int64_t feature_cols, int64_t ld_features, float* out, int64_t out_cols,
                                        int64_t ld_out);
 TG_API void tg_model_free(tg_model m);
+/* Model::forward(adjacency, features) recorded once as a CUDA graph (after
+ * one eager run) and replayed: for small graphs, where launching a
+ * forward's couple of dozen kernels costs more than their work.  The graph
+ * reads the two tensors' device memory at each replay, so they must outlive
+ * it (new values can be written into them between replays); FAST-mode GCN
+ * and SAGE layers only (EXACT gcn_norm and GAT's self-loops read a size back
+ * to the host: TG_ERR_RUNTIME).  No counterpart in the reference. */
+typedef struct tg_graph_s* tg_graph;
+TG_API tg_status tg_model_capture(tg_model m, tg_tensor adjacency, tg_tensor features, tg_graph* out);
+/* Runs the captured forward again; complete when it returns. */
+TG_API tg_status tg_graph_replay(tg_graph g);
+/* The last replay's (or the capture's) output into host rows of stride ld. */
+TG_API tg_status tg_graph_download(tg_graph g, float* host, int64_t ld);
+TG_API void tg_graph_free(tg_graph g);
 /* FAST (1) or EXACT (0) arithmetic for the handle and C++ APIs, process-wide;
  * returns the previous setting (tinygnn::set_fast_math). */
 TG_API int32_t tg_set_fast_math(int32_t fast);

@@ -168,3 +168,44 @@ def test_forward_host_refuses_bad_input():
             assert np.isfinite(out).all()
         finally:
             set_fast_math(prev)
+
+
+@pytest.mark.parametrize("kind", ["gcn", "sage"])
+def test_captured_forward_replays_forward(kind):
+    """tg_model_capture records FAST Model::forward as a CUDA graph; replays
+    give tg_model_forward's output bit for bit, repeatedly; forwards that read
+    a size back to the host (EXACT gcn_norm, GAT self-loops) are refused."""
+    import tinygnn_b200 as tg
+    from tinygnn_b200.handles import HTensor, set_fast_math
+    rng = np.random.default_rng(300 + len(kind))
+    n, fin = 2708, 40  # Cora-sized: the launch-bound case the graph is for
+    rp, ci, v = powerlaw_csr(rng, n, 4, weighted=False, diag=False)
+    X = rng.standard_normal((n, fin)).astype(np.float32)
+    spec, w = _spec_weights(rng, kind, fin)
+    prev = set_fast_math(True)
+    try:
+        m = _build(spec, w)
+        A, Xt = HTensor.csr(n, n, rp, ci, None), HTensor.dense(X, n, fin)
+        ref = m.forward(A, Xt).download()
+        g = m.capture(A, Xt)
+        for _ in range(3):
+            out = np.full((n, 7), np.nan, np.float32)
+            g.replay().download(out)
+            assert_bits_equal(out, ref, f"{kind} replay")
+        g.free()
+        tg.ops.take_device_error()
+        set_fast_math(False)
+        me = _build(spec, w)
+        if kind == "gcn":
+            with pytest.raises(RuntimeError, match="cannot be recorded"):
+                me.capture(A, Xt)
+        spec_g, w_g = _spec_weights(rng, "gat", fin)
+        set_fast_math(True)
+        mg = _build(spec_g, w_g)
+        with pytest.raises(RuntimeError, match="cannot be recorded"):
+            mg.capture(A, Xt)
+        # the thread's stream is usable after a refused capture
+        again = m.forward(A, Xt).download()
+        assert_bits_equal(again, ref, f"{kind} after refused capture")
+    finally:
+        set_fast_math(prev)

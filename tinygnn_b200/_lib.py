@@ -81,6 +81,10 @@ SIGNATURES = {
     "tg_model_forward": (i32, [vp, vp, vp, C.POINTER(vp)]),
     "tg_model_forward_host": (i32, [vp, i64, i64, vp, vp, vp, vp, i64, i64, vp, i64, i64]),
     "tg_model_free": (None, [vp]),
+    "tg_model_capture": (i32, [vp, vp, vp, C.POINTER(vp)]),
+    "tg_graph_replay": (i32, [vp]),
+    "tg_graph_download": (i32, [vp, vp, i64]),
+    "tg_graph_free": (None, [vp]),
     "tg_set_fast_math": (i32, [i32]),
     "tg_dist_partition_csr": (i32, [i32, i32, i64, vp, P64, P64, P64, P64]),
     "tg_dist_init": (i32, [i32, i32, i32, C.c_char_p, i32, C.POINTER(vp)]),

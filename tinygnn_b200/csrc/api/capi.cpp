@@ -166,33 +166,45 @@ TG_API tg_status tg_tensor_create_csr(int64_t rows, int64_t cols, int64_t nnz, c
     });
 }
 
+}  // extern "C"
+
+namespace {
+
+// A dense tensor's values into host rows of stride ld; complete on return.
+void download_dense(const Tensor& x, float* host, int64_t ld) {
+    if (x.format() != tinygnn::StorageFormat::Dense)
+        throw std::invalid_argument("tg_tensor_download: only Dense tensors can be downloaded");
+    if (ld < static_cast<int64_t>(x.cols())) throw std::invalid_argument("tg_tensor_download: ld < cols");
+    const std::size_t r = x.rows(), c = x.cols(), dld = x.device_ld();
+    if (r && c) {
+        if (static_cast<std::size_t>(ld) == dld) {
+            cuda(cudaMemcpyAsync(host, x.device_data(), r * dld * sizeof(float), cudaMemcpyDeviceToHost, cstream()),
+                 "tg_tensor_download");
+        } else {
+            // pack to the host's stride on the device, then one DMA
+            float* pack = device_alloc<float>(r * static_cast<std::size_t>(ld));
+            cuda(cudaMemcpy2DAsync(pack, static_cast<std::size_t>(ld) * sizeof(float), x.device_data(),
+                                   dld * sizeof(float), c * sizeof(float), r, cudaMemcpyDeviceToDevice,
+                                   cstream()),
+                 "tg_tensor_download");
+            cuda(cudaMemcpyAsync(host, pack, r * static_cast<std::size_t>(ld) * sizeof(float),
+                                 cudaMemcpyDeviceToHost, cstream()),
+                 "tg_tensor_download");
+            cuda(cudaFreeAsync(pack, cstream()), "tg_tensor_download");
+        }
+    }
+    cuda(cudaStreamSynchronize(cstream()), "tg_tensor_download");
+}
+
+}  // namespace
+
+extern "C" {
+
 TG_API tg_status tg_tensor_download(tg_tensor t, float* host, int64_t ld) {
     return api([&] {
         need(t, "tg_tensor_download: t");
         need(host, "tg_tensor_download: host");
-        const Tensor& x = t->t;
-        if (x.format() != tinygnn::StorageFormat::Dense)
-            throw std::invalid_argument("tg_tensor_download: only Dense tensors can be downloaded");
-        if (ld < static_cast<int64_t>(x.cols())) throw std::invalid_argument("tg_tensor_download: ld < cols");
-        const std::size_t r = x.rows(), c = x.cols(), dld = x.device_ld();
-        if (r && c) {
-            if (static_cast<std::size_t>(ld) == dld) {
-                cuda(cudaMemcpyAsync(host, x.device_data(), r * dld * sizeof(float), cudaMemcpyDeviceToHost, cstream()),
-                     "tg_tensor_download");
-            } else {
-                // pack to the host's stride on the device, then one DMA
-                float* pack = device_alloc<float>(r * static_cast<std::size_t>(ld));
-                cuda(cudaMemcpy2DAsync(pack, static_cast<std::size_t>(ld) * sizeof(float), x.device_data(),
-                                       dld * sizeof(float), c * sizeof(float), r, cudaMemcpyDeviceToDevice,
-                                       cstream()),
-                     "tg_tensor_download");
-                cuda(cudaMemcpyAsync(host, pack, r * static_cast<std::size_t>(ld) * sizeof(float),
-                                     cudaMemcpyDeviceToHost, cstream()),
-                     "tg_tensor_download");
-                cuda(cudaFreeAsync(pack, cstream()), "tg_tensor_download");
-            }
-        }
-        cuda(cudaStreamSynchronize(cstream()), "tg_tensor_download");
+        download_dense(t->t, host, ld);
     });
 }
 
@@ -310,6 +322,37 @@ TG_API tg_status tg_model_forward_host(tg_model m, int64_t n, int64_t nnz, const
 }
 
 TG_API void tg_model_free(tg_model m) { delete m; }
+
+TG_API tg_status tg_model_capture(tg_model m, tg_tensor adjacency, tg_tensor features, tg_graph* out) {
+    return api([&] {
+        need(m, "tg_model_capture: m");
+        need(adjacency, "tg_model_capture: adjacency");
+        need(features, "tg_model_capture: features");
+        need(out, "tg_model_capture: out");
+        *out = nullptr;
+        no_device_check();
+        auto h = std::make_unique<tg_graph_s>(tg_graph_s{m->m.capture(adjacency->t, features->t)});
+        *out = h.release();
+    });
+}
+
+TG_API tg_status tg_graph_replay(tg_graph g) {
+    return api([&] {
+        need(g, "tg_graph_replay: g");
+        g->g.replay();
+        cuda(cudaStreamSynchronize(cstream()), "tg_graph_replay");
+    });
+}
+
+TG_API tg_status tg_graph_download(tg_graph g, float* host, int64_t ld) {
+    return api([&] {
+        need(g, "tg_graph_download: g");
+        need(host, "tg_graph_download: host");
+        download_dense(g->g.output(), host, ld);
+    });
+}
+
+TG_API void tg_graph_free(tg_graph g) { delete g; }
 
 TG_API int32_t tg_set_fast_math(int32_t fast) {
     const int32_t prev = tinygnn::fast_math() ? 1 : 0;

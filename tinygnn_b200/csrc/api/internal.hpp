@@ -101,3 +101,6 @@ struct tg_tensor_s {
 struct tg_model_s {
     tinygnn::Model m;
 };
+struct tg_graph_s {
+    tinygnn::ForwardGraph g;
+};

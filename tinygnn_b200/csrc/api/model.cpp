@@ -380,6 +380,74 @@ Tensor Model::forward(const Tensor& adjacency, const Tensor& features) const {
 }
 
 
+// ── Captured forward (CUDA graph) ───────────────────────────────────────────
+struct ForwardGraph::Impl {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    Tensor out;
+    ~Impl() {
+        if (exec) cudaGraphExecDestroy(exec);
+        if (graph) cudaGraphDestroy(graph);
+    }
+};
+
+ForwardGraph::ForwardGraph() = default;
+ForwardGraph::ForwardGraph(ForwardGraph&&) noexcept = default;
+ForwardGraph& ForwardGraph::operator=(ForwardGraph&&) noexcept = default;
+ForwardGraph::~ForwardGraph() = default;
+
+const Tensor& ForwardGraph::output() const {
+    if (!impl_) throw std::runtime_error("ForwardGraph: empty (not captured)");
+    return impl_->out;
+}
+
+const Tensor& ForwardGraph::replay() {
+    if (!impl_) throw std::runtime_error("ForwardGraph: empty (not captured)");
+    detail::cuda(cudaGraphLaunch(impl_->exec, detail::cstream()), "ForwardGraph::replay");
+    return impl_->out;
+}
+
+ForwardGraph Model::capture(const Tensor& adjacency, const Tensor& features) const {
+    // One eager run first: it uploads host-newer inputs and weights, and sets
+    // up what the kernels create on first use (attributes, the side stream).
+    const Tensor first = forward(adjacency, features);
+    auto impl = std::make_unique<ForwardGraph::Impl>();
+    impl->out = Tensor::dense_device(first.rows(), first.cols());
+    const cudaStream_t s = detail::cstream();
+    detail::cuda(cudaStreamSynchronize(s), "Model::capture");
+    detail::cuda(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "Model::capture");
+    cudaGraph_t g = nullptr;
+    try {
+        // the forward's temporaries (its output included) are allocated and
+        // freed inside the graph; the result is copied into impl->out
+        const Tensor y = forward(adjacency, features);
+        if (y.rows() > 0 && y.cols() > 0)
+            detail::cuda(cudaMemcpy2DAsync(impl->out.mutable_device_data(), impl->out.device_ld() * sizeof(float),
+                                           y.device_data(), y.device_ld() * sizeof(float), y.cols() * sizeof(float),
+                                           y.rows(), cudaMemcpyDeviceToDevice, s),
+                         "Model::capture");
+    } catch (...) {
+        cudaStreamEndCapture(s, &g);
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        throw std::runtime_error(
+            "Model::capture: this forward cannot be recorded as a CUDA graph (a step reads a size back to the "
+            "host: EXACT gcn_norm, GAT self-loops); use FAST mode GCN / SAGE layers, or forward()");
+    }
+    const cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (e != cudaSuccess || !g) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        throw std::runtime_error(std::string("Model::capture: recording failed: ") + cudaGetErrorString(e));
+    }
+    impl->graph = g;
+    detail::cuda(cudaGraphInstantiate(&impl->exec, g, 0), "Model::capture");
+    ForwardGraph fg;
+    fg.impl_ = std::move(impl);
+    return fg;
+}
+
+
 // ── Forward from host buffers ──────────────────────────────────────────────
 namespace {
 

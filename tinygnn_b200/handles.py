@@ -133,9 +133,43 @@ class HModel:
                                         feature_cols, ld_f, _ptr(out), out_cols, ld_o))
         return out
 
+    def capture(self, adjacency: HTensor, features: HTensor) -> "HGraph":
+        """forward(adjacency, features) recorded as a CUDA graph (tg_model_capture)."""
+        g = C.c_void_p()
+        check(lib.tg_model_capture(self.h, adjacency.h, features.h, C.byref(g)))
+        return HGraph(g, (adjacency, features))
+
     def free(self) -> None:
         if self.h:
             lib.tg_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class HGraph:
+    """A tg_graph: a captured Model::forward, replayed on its input tensors."""
+
+    def __init__(self, handle: C.c_void_p, inputs):
+        self.h = handle
+        self._inputs = inputs  # the graph reads their device memory: keep them alive
+
+    def replay(self) -> "HGraph":
+        check(lib.tg_graph_replay(self.h))
+        return self
+
+    def download(self, out):
+        """The output into ``out`` (a host float32 rows x cols array or tensor)."""
+        check(lib.tg_graph_download(self.h, _ptr(out), out.shape[1]))
+        return out
+
+    def free(self) -> None:
+        if self.h:
+            lib.tg_graph_free(self.h)
             self.h = None
 
     def __del__(self):
