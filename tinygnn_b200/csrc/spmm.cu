@@ -222,16 +222,26 @@ __global__ void order_count_kernel(int64_t M, const int32_t* rp, int32_t* counts
 // Single-block exclusive scan over n ints, in place (n = NBUCKET * nblocks).
 // Thread t owns one contiguous run of ceil(n / blockDim) entries: it sums
 // its run, the block scans the 1024 run sums once (warp shuffles, then the
-// warp totals), and each thread writes its run's prefixes -- two passes over
-// the 117 KB of counts and three barriers, where a block-wide step per 1024
-// entries had taken ~30 us on the Reddit-shaped graph.
+// warp totals), and each thread writes its run's prefixes.  With SMEM the
+// counts are staged through shared memory with coalesced loads and stores
+// (the runs are then read at an odd stride: no bank conflicts); a run read
+// straight from global memory is a chain of dependent-latency loads (~25 us
+// for the Reddit-shaped graph's 29,184 counts).
+template <bool SMEM>
 __global__ void order_scan_kernel(int32_t* x, int64_t n) {
+    extern __shared__ int32_t sx[];
     __shared__ int32_t warp_sums[32];
+    int32_t* v = x;
+    if (SMEM) {
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) sx[i] = x[i];
+        __syncthreads();
+        v = sx;
+    }
     const int64_t per = (n + blockDim.x - 1) / blockDim.x;
     const int64_t b = static_cast<int64_t>(threadIdx.x) * per;
     const int64_t e = b + per < n ? b + per : n;
     int32_t sum = 0;
-    for (int64_t i = b; i < e; ++i) sum += x[i];
+    for (int64_t i = b; i < e; ++i) sum += v[i];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     int32_t incl = sum;
 #pragma unroll
@@ -253,9 +263,13 @@ __global__ void order_scan_kernel(int32_t* x, int64_t n) {
     __syncthreads();
     int32_t run = (w ? warp_sums[w - 1] : 0) + incl - sum;  // exclusive prefix of this thread's run
     for (int64_t i = b; i < e; ++i) {
-        const int32_t v = x[i];
-        x[i] = run;
-        run += v;
+        const int32_t c = v[i];
+        v[i] = run;
+        run += c;
+    }
+    if (SMEM) {
+        __syncthreads();
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) x[i] = sx[i];
     }
 }
 
@@ -312,7 +326,15 @@ void csr_degree_order(int64_t M, const int32_t* rp, int32_t* out, cudaStream_t s
     const int64_t nb = ceil_div(M, ORDER_BLOCK);
     Scratch<int32_t> counts(static_cast<size_t>(nb) * NBUCKET, s);
     launch("order_count", order_count_kernel, dim3(static_cast<unsigned>(nb)), dim3(ORDER_BLOCK), 0, s, M, rp, counts.p);
-    launch("order_scan", order_scan_kernel, dim3(1), dim3(1024), 0, s, counts.p, nb * NBUCKET);
+    const int64_t n = nb * NBUCKET;
+    constexpr int64_t kScanSmemMax = 200 * 1024;  // counts staged through shared memory up to this size
+    if (n * 4 <= kScanSmemMax) {
+        const int smem = static_cast<int>(n * 4);
+        TG_CUDA(cudaFuncSetAttribute(order_scan_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        launch("order_scan", order_scan_kernel<true>, dim3(1), dim3(1024), static_cast<size_t>(smem), s, counts.p, n);
+    } else {
+        launch("order_scan", order_scan_kernel<false>, dim3(1), dim3(1024), 0, s, counts.p, n);
+    }
     launch("order_scatter", order_scatter_kernel, dim3(static_cast<unsigned>(nb)), dim3(ORDER_BLOCK), 0, s, M, rp,
            static_cast<const int32_t*>(counts.p), out);
 }

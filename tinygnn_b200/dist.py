@@ -296,6 +296,8 @@ class ShardedModel:
         # while a forward runs (set by forward_model / forward_from_host).
         self.scale: Optional[torch.Tensor] = None
         self.scale_buf = torch.empty(max(self.rows, 1), dtype=torch.float32, device=device)
+        self._prep_stream = None  # _normalise's side stream (schedule, split points)
+        self._prep_ready = None   # its completion, joined by the first gather
 
     def _scaled(self, li: int) -> bool:
         """Layer li is a GCN layer run in the factored FAST form."""
@@ -380,6 +382,7 @@ class ShardedModel:
             self.pex.close()
 
     def _pass(self, li: int, A: CSR, lo, hi, carry: bool, last: bool) -> torch.Tensor:
+        self._join_prep()
         L = self.layers[li]
         fo = L.W.shape[1]
         B = self.full[li][:self.n, :fo]
@@ -394,6 +397,12 @@ class ShardedModel:
             return ops.sage_mean_combine(A, B, self.selfs[li][:, :fo], bias=L.b, act=L.act, out=self.outs[li])
         return ops.sage_mean_combine_segment(A, B, self.selfs[li][:, :fo], lo, hi, self.outs[li], carry, last,
                                              bias=L.b, act=L.act)
+
+    def _join_prep(self) -> None:
+        """The current stream waits for _normalise's side-stream work (once)."""
+        if self._prep_ready is not None:
+            torch.cuda.current_stream().wait_event(self._prep_ready)
+            self._prep_ready = None
 
     def aggregate(self, li: int, A_gcn: Optional[CSR], A_raw: Optional[CSR]) -> torch.Tensor:
         """Single pass over the whole (already exchanged) operand."""
@@ -500,6 +509,7 @@ class ShardedModel:
         cur.wait_event(csr_ready)
         A = CSR(self.rows, self.n, d_rp, d_ci, d_v)
         A_gcn = self._normalise(A, bufs["dis"])
+        self._join_prep()
         if single and nb > 1:
             # Layer 1 per feature block: GEMM of block q's rows, then the gather
             # pass over the columns of block q (exact: passes in column order).
@@ -562,10 +572,32 @@ class ShardedModel:
             return None
         if self.mode == "fast":
             As = CSR(A.n_rows, A.n_cols, A.row_ptr, A.col_ind, A.values, A.order, A.validated)
-            if As.order is None:
-                As.order = ops.degree_order(As)
+            if not As.validated:
+                ops.csr_validate(As)  # Tensor::sparse_csr's checks, once, before any kernel reads As
+                As.validated = True
+            # The row schedule and the column-pass split points run on a side
+            # stream beside the scale and the first GEMM, which need neither;
+            # the first gather joins them (_join_prep).
+            cur = torch.cuda.current_stream()
+            side = self._prep_stream
+            if side is None:
+                side = self._prep_stream = torch.cuda.Stream(device=self.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                if As.order is None:
+                    As.order = ops.degree_order(As)
+                made = [As.order]
+                if not self.pipeline:
+                    for li, L in enumerate(self.layers):
+                        sp = self.pass_splits(As, self.passes[li]) if L.kind == "gcn" else None
+                        if sp is not None:
+                            made.append(sp)
+            for t in made:  # used on the current stream from here on
+                t.record_stream(cur)
+            self._prep_ready = torch.cuda.Event()
+            self._prep_ready.record(side)
             self.scale = ops.gcn_norm_scale(As, out=self.scale_buf[:A.n_rows])
-            A.validated = A.validated or As.validated  # same arrays: checked once
+            A.validated = True  # same arrays: checked once
             return As
         self.scale = None
         return gcn_norm_rows_scheduled(A, self.row0, self.R, self.comm, dis_all)
