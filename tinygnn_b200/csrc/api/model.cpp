@@ -468,7 +468,7 @@ int host_blocks() {
     return v;
 }
 int out_chunks() {
-    static const int v = env_count("TINYGNN_B200_HOST_OUT_CHUNKS", 2);
+    static const int v = env_count("TINYGNN_B200_HOST_OUT_CHUNKS", 3);
     return v;
 }
 
