@@ -112,7 +112,7 @@ def test_handle_tensors_from_pinned_torch_and_errors():
 @pytest.mark.parametrize("fast", [False, True])
 def test_forward_host_equals_forward(kind, fast):
     """tg_model_forward_host (uploads overlapped with the compute; a FAST GCN
-    first layer in 8 feature blocks / column passes, a FAST GCN last layer in
+    first layer in 16 feature blocks / column passes, a FAST GCN last layer in
     row chunks) gives tg_model_forward's output bit for bit, at the caller's
     feature stride (41: landing + device repack; 44: straight into place)
     and output stride (7: device pack; 8: one copy), twice in a row, from

@@ -47,6 +47,28 @@ struct TrustedCsr {
 
 inline std::size_t pad4(std::size_t n) { return (n + 3) / 4 * 4; }
 
+// A device array from the stream-ordered pool (the calling thread's
+// stream), freed on scope exit in stream order.
+template <class T>
+struct DevArray {
+    T* p = nullptr;
+    explicit DevArray(std::size_t n) {
+        void* q = nullptr;
+        cuda(cudaMallocAsync(&q, (n ? n : 1) * sizeof(T), cstream()), "tinygnn allocation");
+        p = static_cast<T*>(q);
+    }
+    ~DevArray() {
+        if (p && cudaFreeAsync(p, cstream()) != cudaSuccess) cudaGetLastError();
+    }
+    DevArray(const DevArray&) = delete;
+    DevArray& operator=(const DevArray&) = delete;
+};
+
+// A gathered operand above this size is aggregated in column-block passes
+// (each pass's slice of the operand stays in L2; measured on B200 for the
+// 119 MB Reddit-shaped layer-1 operand: 2 passes, -6 %).
+constexpr std::size_t kPassBytes = std::size_t(64) << 20;
+
 // Two weight matrices (same shape) as device arrays with ld == cols, the
 // layout tg_gemm_pair_f32 takes (Tensor rows are padded to 16 bytes).
 struct DevWeights {

@@ -5,6 +5,8 @@
 // ============================================================================
 #include "tinygnn/layers.hpp"
 
+#include <algorithm>
+
 #include "internal.hpp"
 
 namespace tinygnn {
@@ -242,14 +244,36 @@ Tensor SAGELayer::forward(const Tensor& A, const Tensor& H) const {
                                static_cast<int64_t>(Fo), Tn.mutable_device_data(), static_cast<int64_t>(Tn.device_ld()),
                                Ts.mutable_device_data(), static_cast<int64_t>(Ts.device_ld()), TG_MODE_FAST,
                                stream()));
+        // The combine gathers Tn rows in a longest-first schedule, in column
+        // passes when Tn is larger than kPassBytes (each pass's slice stays
+        // in L2; the passes carry each output element's chain through out).
         const detail::TrustedCsr trusted_csr;
-        check(tg_sage_mean_combine_f32(static_cast<int64_t>(N), static_cast<int64_t>(A.cols()),
-                                       static_cast<int64_t>(A.nnz()), A.device_row_ptr(), A.device_col_ind(),
-                                       Tn.device_data(), static_cast<int64_t>(Fo), static_cast<int64_t>(Tn.device_ld()),
-                                       Ts.device_data(), static_cast<int64_t>(Ts.device_ld()), bias,
-                                       act_code(activation_), out.mutable_device_data(),
-                                       static_cast<int64_t>(out.device_ld()), nullptr, TG_FLAG_B_ROWS_PADDED,
-                                       stream()));
+        const std::size_t K = A.cols();
+        const int64_t M = static_cast<int64_t>(N);
+        detail::DevArray<int32_t> order(N);
+        check(tg_csr_degree_order(M, A.device_row_ptr(), order.p, stream()));
+        const int passes = static_cast<int>(std::max<std::size_t>(
+            1, (K * Tn.device_ld() * sizeof(float) + detail::kPassBytes - 1) / detail::kPassBytes));
+        if (passes == 1) {
+            check(tg_sage_mean_combine_f32(M, static_cast<int64_t>(K), static_cast<int64_t>(A.nnz()),
+                                           A.device_row_ptr(), A.device_col_ind(), Tn.device_data(),
+                                           static_cast<int64_t>(Fo), static_cast<int64_t>(Tn.device_ld()),
+                                           Ts.device_data(), static_cast<int64_t>(Ts.device_ld()), bias,
+                                           act_code(activation_), out.mutable_device_data(),
+                                           static_cast<int64_t>(out.device_ld()), order.p, TG_FLAG_B_ROWS_PADDED,
+                                           stream()));
+            return out;
+        }
+        detail::DevArray<int32_t> sp(N * static_cast<std::size_t>(passes + 1));
+        check(tg_csr_column_splits(M, A.device_row_ptr(), A.device_col_ind(), passes,
+                                   static_cast<int64_t>((K + passes - 1) / passes), sp.p, stream()));
+        for (int q = 0; q < passes; ++q)
+            check(tg_sage_mean_combine_segment_f32(
+                M, static_cast<int64_t>(K), A.device_row_ptr(), A.device_col_ind(), sp.p + static_cast<std::size_t>(q) * N,
+                sp.p + static_cast<std::size_t>(q + 1) * N, Tn.device_data(), static_cast<int64_t>(Fo),
+                static_cast<int64_t>(Tn.device_ld()), Ts.device_data(), static_cast<int64_t>(Ts.device_ld()), bias,
+                act_code(activation_), out.mutable_device_data(), static_cast<int64_t>(out.device_ld()), order.p,
+                q > 0, q == passes - 1, TG_FLAG_B_ROWS_PADDED, stream()));
         return out;
     }
     // Aggregate first, then the interleaved dual product (bit-identical), or

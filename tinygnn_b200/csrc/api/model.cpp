@@ -46,21 +46,7 @@ T read_le(std::ifstream& f, const char* ctx) {
     return v;
 }
 
-float* dalloc(std::size_t n) {
-    void* p = nullptr;
-    detail::cuda(cudaMallocAsync(&p, (n ? n : 1) * sizeof(float), detail::cstream()), "tinygnn allocation");
-    return static_cast<float*>(p);
-}
-
-struct DevBuf {
-    float* p = nullptr;
-    explicit DevBuf(std::size_t n) : p(dalloc(n)) {}
-    ~DevBuf() {
-        if (p && cudaFreeAsync(p, detail::cstream()) != cudaSuccess) cudaGetLastError();
-    }
-    DevBuf(const DevBuf&) = delete;
-    DevBuf& operator=(const DevBuf&) = delete;
-};
+using DevBuf = detail::DevArray<float>;
 
 // Packs rows x cols of `src` (device, row stride ld) into dst at column offset.
 void pack(float* dst, std::size_t dst_ld, std::size_t col0, const Tensor& src) {
@@ -191,20 +177,7 @@ void Model::load_weights(const WeightFile& wf) {
 
 namespace {
 
-// A device int32 buffer from the stream-ordered pool.
-struct DevInts {
-    int32_t* p = nullptr;
-    explicit DevInts(std::size_t n) {
-        void* q = nullptr;
-        detail::cuda(cudaMallocAsync(&q, (n ? n : 1) * sizeof(int32_t), detail::cstream()), "tinygnn allocation");
-        p = static_cast<int32_t*>(q);
-    }
-    ~DevInts() {
-        if (p && cudaFreeAsync(p, detail::cstream()) != cudaSuccess) cudaGetLastError();
-    }
-    DevInts(const DevInts&) = delete;
-    DevInts& operator=(const DevInts&) = delete;
-};
+using DevInts = detail::DevArray<int32_t>;
 
 // The raw adjacency prepared once per forward for FAST GCN layers without a
 // normalised copy: dis[i] = 1/sqrt(row sum + 1) (tg_gcn_norm_scale_f32), a
@@ -235,10 +208,7 @@ struct ScaledGraph {
     }
 };
 
-// A gathered operand above this size is aggregated in column-block passes
-// (each pass's slice of the operand stays in L2; measured on B200 for the
-// 119 MB Reddit-shaped layer-1 operand: 2 passes, -6 %).
-constexpr std::size_t kPassBytes = std::size_t(64) << 20;
+using detail::kPassBytes;
 
 // GCNLayer::forward on the raw adjacency in FAST mode: Hs = diag(dis) . (H . W)
 // on the tensor cores, then out = act(dis * (A . Hs + Hs_self) + b) in
@@ -549,7 +519,15 @@ void Model::forward_host(std::size_t n, std::size_t nnz, const int32_t* row_ptr,
     }
     const cudaStream_t s = detail::cstream(), cs = copy_stream();
     const bool first_scaled = layers_[0].type == LayerEntry::Type::GCN && fast_math() && n > 0;
-    const int blocks = first_scaled ? static_cast<int>(std::min<std::size_t>(host_blocks(), n)) : 1;
+    // a FAST transform-first SAGE-mean first layer pipelines the same way
+    bool first_sage = false;
+    if (layers_[0].type == LayerEntry::Type::SAGE && fast_math() && n > 0) {
+        const SAGELayer& L = sage_layers_[layers_[0].start_idx];
+        first_sage = L.aggregator() == SAGELayer::Aggregator::Mean && L.in_features() > L.out_features() &&
+                     feature_cols == L.in_features();
+    }
+    const bool pipelined = first_scaled || first_sage;
+    const int blocks = pipelined ? static_cast<int>(std::min<std::size_t>(host_blocks(), n)) : 1;
     const std::size_t width = n ? (n + static_cast<std::size_t>(blocks) - 1) / static_cast<std::size_t>(blocks) : 0;
 
     // device buffers (stream-ordered on the compute stream; the CSR arrays
@@ -654,11 +632,62 @@ void Model::forward_host(std::size_t n, std::size_t nnz, const int32_t* row_ptr,
         else if (layers_[0].post_act == InterActivation::ELU) elu_inplace(o);
         H = std::move(o);
         first = 1;
+    } else if (first_sage) {
+        // Layer 1 per feature block: Tn and Ts rows of block q = X . W_neigh
+        // and X . W_self (one tensor-core pass), then the combine pass over
+        // the columns of block q; the last pass adds Ts, bias, activation.
+        const SAGELayer& L = sage_layers_[layers_[0].start_idx];
+        const std::size_t Fo = L.out_features();
+        Tensor Tn = Tensor::dense_device(n, Fo), Ts = Tensor::dense_device(n, Fo);
+        Tensor o = Tensor::dense_device(n, Fo);
+        const std::size_t ldn = Tn.device_ld(), lds = Ts.device_ld();
+        const detail::DevWeights w(L.weight_neigh(), L.weight_self());
+        DevInts order(n);
+        const detail::TrustedCsr trusted_csr;
+        check(tg_csr_degree_order(static_cast<int64_t>(n), A.device_row_ptr(), order.p, stream()));
+        std::unique_ptr<DevInts> sp;
+        if (blocks > 1) {
+            sp = std::make_unique<DevInts>(n * static_cast<std::size_t>(blocks + 1));
+            check(tg_csr_column_splits(static_cast<int64_t>(n), A.device_row_ptr(), A.device_col_ind(), blocks,
+                                       static_cast<int64_t>(width), sp->p, stream()));
+        }
+        const float* bias = L.has_bias() ? L.bias().device_data() : nullptr;
+        const int act = L.activation() == Activation::ReLU ? TG_ACT_RELU : TG_ACT_NONE;
+        for (int q = 0; q < blocks; ++q) {
+            const std::size_t a = std::min(n, static_cast<std::size_t>(q) * width), b = std::min(n, a + width);
+            x_ready[static_cast<std::size_t>(q)]->wait_in(s);
+            repack(a, b);
+            if (b > a)
+                check(tg_gemm_pair_f32(static_cast<int64_t>(b - a), static_cast<int64_t>(Fo),
+                                       static_cast<int64_t>(feature_cols), X.device_data() + a * ldx,
+                                       static_cast<int64_t>(ldx), w.wn, w.ws, static_cast<int64_t>(Fo),
+                                       Tn.mutable_device_data() + a * ldn, static_cast<int64_t>(ldn),
+                                       Ts.mutable_device_data() + a * lds, static_cast<int64_t>(lds), TG_MODE_FAST,
+                                       stream()));
+            if (sp)
+                check(tg_sage_mean_combine_segment_f32(
+                    static_cast<int64_t>(n), static_cast<int64_t>(n), A.device_row_ptr(), A.device_col_ind(),
+                    sp->p + static_cast<std::size_t>(q) * n, sp->p + static_cast<std::size_t>(q + 1) * n,
+                    Tn.device_data(), static_cast<int64_t>(Fo), static_cast<int64_t>(ldn), Ts.device_data(),
+                    static_cast<int64_t>(lds), bias, act, o.mutable_device_data(), static_cast<int64_t>(o.device_ld()),
+                    order.p, q > 0, q == blocks - 1, TG_FLAG_B_ROWS_PADDED, stream()));
+            else
+                check(tg_sage_mean_combine_f32(static_cast<int64_t>(n), static_cast<int64_t>(n),
+                                               static_cast<int64_t>(nnz), A.device_row_ptr(), A.device_col_ind(),
+                                               Tn.device_data(), static_cast<int64_t>(Fo), static_cast<int64_t>(ldn),
+                                               Ts.device_data(), static_cast<int64_t>(lds), bias, act,
+                                               o.mutable_device_data(), static_cast<int64_t>(o.device_ld()), order.p,
+                                               TG_FLAG_B_ROWS_PADDED, stream()));
+        }
+        if (layers_[0].post_act == InterActivation::ReLU) relu_inplace(o);
+        else if (layers_[0].post_act == InterActivation::ELU) elu_inplace(o);
+        H = std::move(o);
+        first = 1;
     } else {
         x_ready.back()->wait_in(s);
         repack(0, n);
     }
-    if (first_scaled) X = Tensor();  // not read again
+    if (pipelined) X = Tensor();  // not read again
     else H = std::move(X);
 
     const std::size_t last = layers_.size() - 1;
