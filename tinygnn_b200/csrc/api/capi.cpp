@@ -301,6 +301,7 @@ TG_API tg_status tg_model_forward(tg_model m, tg_tensor adjacency, tg_tensor fea
         *out = nullptr;
         no_device_check();
         auto h = std::make_unique<tg_tensor_s>(tg_tensor_s{m->m.forward(adjacency->t, features->t)});
+        cuda(cudaStreamSynchronize(cstream()), "tg_model_forward");  // complete on return, like every handle call
         *out = h.release();
     });
 }

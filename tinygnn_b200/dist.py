@@ -298,6 +298,8 @@ class ShardedModel:
         self.scale_buf = torch.empty(max(self.rows, 1), dtype=torch.float32, device=device)
         self._prep_stream = None  # _normalise's side stream (schedule, split points)
         self._prep_ready = None   # its completion, joined by the first gather
+        self._order_buf = None    # the schedule of the rows, rewritten every forward
+        self._split_bufs = {}     # column-pass split points by pass count
 
     def _scaled(self, li: int) -> bool:
         """Layer li is a GCN layer run in the factored FAST form."""
@@ -508,7 +510,7 @@ class ShardedModel:
             d_v.fill_(1.0)
         cur.wait_event(csr_ready)
         A = CSR(self.rows, self.n, d_rp, d_ci, d_v)
-        A_gcn = self._normalise(A, bufs["dis"])
+        A_gcn = self._normalise(A, bufs["dis"], scratch=True)
         self._join_prep()
         if single and nb > 1:
             # Layer 1 per feature block: GEMM of block q's rows, then the gather
@@ -561,12 +563,14 @@ class ShardedModel:
         self.scale = None
         return h_out
 
-    def _normalise(self, A: CSR, dis_all: torch.Tensor) -> Optional[CSR]:
+    def _normalise(self, A: CSR, dis_all: torch.Tensor, scratch: bool = False) -> Optional[CSR]:
         """What Model::forward does to the raw adjacency rows before the GCN
         layers (src/model.cpp:365-381), with a longest-first row schedule:
         EXACT -- the normalised copy, bit for bit; FAST -- the raw rows plus
         this rank's 1/sqrt(deg) (self.scale), for the factored layers.
-        None when no layer is a GCN layer."""
+        None when no layer is a GCN layer.  ``scratch``: the schedule and split
+        points go into buffers the model rewrites every call (a forward that does
+        not keep the returned CSR); otherwise they are the CSR's own."""
         if not any(L.kind == "gcn" for L in self.layers):
             self.scale = None
             return None
@@ -575,9 +579,21 @@ class ShardedModel:
             if not As.validated:
                 ops.csr_validate(As)  # Tensor::sparse_csr's checks, once, before any kernel reads As
                 As.validated = True
+            if not scratch:
+                if As.order is None:
+                    As.order = ops.degree_order(As)
+                self.scale = ops.gcn_norm_scale(As, out=self.scale_buf[:A.n_rows])
+                A.validated = True
+                return As
             # The row schedule and the column-pass split points run on a side
             # stream beside the scale and the first GEMM, which need neither;
-            # the first gather joins them (_join_prep).
+            # the first gather joins them (_join_prep).  They go into buffers
+            # the model keeps: the side stream starts after all earlier work
+            # of the current stream (the previous forward's reads of them),
+            # and no per-call allocation crosses streams (freed blocks of
+            # another stream are reusable only once the GPU has caught up,
+            # which made the allocator grow, and synchronise, while the host
+            # ran ahead).
             cur = torch.cuda.current_stream()
             side = self._prep_stream
             if side is None:
@@ -585,15 +601,22 @@ class ShardedModel:
             side.wait_stream(cur)
             with torch.cuda.stream(side):
                 if As.order is None:
-                    As.order = ops.degree_order(As)
-                made = [As.order]
+                    if self._order_buf is None or self._order_buf.numel() < As.n_rows:
+                        self._order_buf = torch.empty(max(As.n_rows, 1), dtype=torch.int32, device=self.device)
+                    As.order = ops.degree_order(As, out=self._order_buf[:As.n_rows])
                 if not self.pipeline:
                     for li, L in enumerate(self.layers):
-                        sp = self.pass_splits(As, self.passes[li]) if L.kind == "gcn" else None
-                        if sp is not None:
-                            made.append(sp)
-            for t in made:  # used on the current stream from here on
-                t.record_stream(cur)
+                        p = self.passes[li]
+                        if L.kind != "gcn" or p == 1:
+                            continue
+                        buf = self._split_bufs.get(p)
+                        if buf is None or buf.shape[1] != As.n_rows:
+                            buf = self._split_bufs[p] = torch.empty((p + 1, As.n_rows), dtype=torch.int32,
+                                                                     device=self.device)
+                        cache = As.__dict__.setdefault("_splits", {})
+                        key = (p, -(-self.n // p))
+                        if key not in cache:
+                            cache[key] = ops.column_splits(As, p, key[1], out=buf)
             self._prep_ready = torch.cuda.Event()
             self._prep_ready.record(side)
             self.scale = ops.gcn_norm_scale(As, out=self.scale_buf[:A.n_rows])
@@ -602,13 +625,13 @@ class ShardedModel:
         self.scale = None
         return gcn_norm_rows_scheduled(A, self.row0, self.R, self.comm, dis_all)
 
-    def prepare(self, A_raw: CSR, dis_all: Optional[torch.Tensor] = None):
+    def prepare(self, A_raw: CSR, dis_all: Optional[torch.Tensor] = None, scratch: bool = False):
         """The per-graph part of Model::forward for this rank's raw adjacency
         rows: (A for the GCN layers, A for the SAGE layers, this rank's GCN
         scale or None) -- see _normalise."""
         if dis_all is None and self.mode != "fast":
             dis_all = torch.zeros(self.R * self.comm.world, dtype=torch.float32, device=self.device)
-        A_gcn = self._normalise(A_raw, dis_all)
+        A_gcn = self._normalise(A_raw, dis_all, scratch)
         scale, self.scale = self.scale, None
         A_sage = A_raw
         if A_gcn is not None and self.mode == "fast":
@@ -631,7 +654,7 @@ class ShardedModel:
                       dis_all: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Model::forward on this rank's raw adjacency rows (no self-loops) and
         feature rows in HBM: normalisation, the layers, log_softmax."""
-        return self.forward_prepared(self.prepare(A_raw, dis_all), X, log_softmax)
+        return self.forward_prepared(self.prepare(A_raw, dis_all, scratch=True), X, log_softmax)
 
     def _chunked_last_layer(self, A_gcn: Optional[CSR], A_raw: CSR, h_out: torch.Tensor,
                             cp: torch.cuda.Stream, chunks: int) -> None:

@@ -266,9 +266,10 @@ def spmm(A: CSR, B: torch.Tensor, bias=None, act=None, alpha: float = 0.0, row_o
     return out
 
 
-def column_splits(A: CSR, nblocks: int, width: int) -> torch.Tensor:
+def column_splits(A: CSR, nblocks: int, width: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """(nblocks+1) x n_rows split points of sorted rows at column multiples of `width`."""
-    out = torch.empty((nblocks + 1, A.n_rows), dtype=torch.int32, device=A.row_ptr.device)
+    if out is None:
+        out = torch.empty((nblocks + 1, A.n_rows), dtype=torch.int32, device=A.row_ptr.device)
     _csr_call((A,), lib.tg_csr_column_splits, A.n_rows, _p(A.row_ptr), _p(A.col_ind), nblocks, width, _p(out), _stream())
     return out
 
@@ -313,9 +314,10 @@ def sage_mean_combine(A: CSR, Tn: torch.Tensor, Ts: torch.Tensor, bias=None, act
     return out
 
 
-def degree_order(A: CSR) -> torch.Tensor:
+def degree_order(A: CSR, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Rows by decreasing stored length (a schedule for the gather kernels)."""
-    out = torch.empty(A.n_rows, dtype=torch.int32, device=A.row_ptr.device)
+    if out is None:
+        out = torch.empty(A.n_rows, dtype=torch.int32, device=A.row_ptr.device)
     check(lib.tg_csr_degree_order(A.n_rows, _p(A.row_ptr), _p(out), _stream()))
     return out
 
