@@ -651,6 +651,7 @@ def run_ours(args):
     alg_gbs = alg_bytes / (gather_ms * 1e-3) / 1e9
     peak, peak_kind = measured_peaks()
     traffic = committed_traffic(f"gather-{args.workload}-L1-{'small' if args.small else 'full'}-p{world}")
+    l2_ceiling = committed_traffic("l2-random-gather-512B")
     # frac is the DRAM fraction: ncu's DRAM bytes per launch over this run's
     # launch time.  The no-reuse algorithmic model counts every gathered row
     # as a DRAM read although L2 serves most of them, so its "fraction" runs
@@ -668,6 +669,10 @@ def run_ours(args):
             "limiter": "L2 latency (long-scoreboard stalls; most gathered rows hit L2), not DRAM bandwidth",
             "algorithmic": {"label": "L2-assisted (algorithmic, no-reuse model nnz*(8+4F) + rows*(4+4F) + 4)",
                             "bytes_per_launch": alg_bytes, "achieved": alg_gbs, "frac_of_peak": alg_gbs / peak},
+            "l2_bound": None if l2_ceiling is None else {
+                "ceiling": l2_ceiling / 1e9, "unit": "GB/s", "frac": alg_gbs / (l2_ceiling / 1e9),
+                "what": "the algorithmic bytes per launch against the rate the same kernel gathers uniformly random "
+                        "512-byte rows from an L2-resident operand (bench.py --micro l2, profiles/traffic.txt)"},
             "compulsory_bytes_per_launch": compulsory}
 
     cpu = None
