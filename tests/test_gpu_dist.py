@@ -318,3 +318,34 @@ def test_fast_sage_model_logits_vs_oracle(tg, fin):
     oref = P.activation("log_softmax", oracle.model_forward(P, spec, w, rp, ci, v, X))
     tg.ops.take_device_error()
     assert_close(got.cpu().numpy(), oref, f"fast sage model fin={fin}")
+
+
+def test_fast_forward_model_reuses_its_buffers_across_graphs(tg):
+    """forward_model keeps the per-call schedule and split points in buffers
+    the model rewrites every call: forwards on different graphs in turn each
+    give the prepared (own-buffer) forward's logits bit for bit."""
+    from tinygnn_b200.dist import Comm, Layer, ShardedModel
+    rng = np.random.default_rng(5)
+    n, fin = 30000, 40
+    W0 = torch.as_tensor((rng.standard_normal((fin, 32)) * 0.2).astype(np.float32)).cuda()
+    W1 = torch.as_tensor((rng.standard_normal((32, 11)) * 0.2).astype(np.float32)).cuda()
+    b0 = torch.as_tensor((rng.standard_normal(32) * 0.1).astype(np.float32)).cuda()
+    b1 = torch.as_tensor((rng.standard_normal(11) * 0.1).astype(np.float32)).cuda()
+    # passes=2: the layer-1 gather in column passes (split points in the model's buffer)
+    m = ShardedModel([Layer("gcn", W0, b0, "relu"), Layer("gcn", W1, b1, None)], n, Comm(1, 0), "cuda",
+                     mode="fast", passes=2)
+    graphs = []
+    for deg in (14, 3, 22):
+        rp, ci, v = powerlaw_csr(rng, n, deg, weighted=False, diag=False)
+        X = torch.as_tensor(rng.standard_normal((n, fin)).astype(np.float32)).cuda()
+        A = tg.CSR.from_numpy(rp, ci, v)
+        ref = m.forward_prepared(m.prepare(A), X).clone()
+        graphs.append((A, X, ref))
+    for _ in range(2):  # queued back to back: each call rewrites the buffers the previous one read
+        for A, X, _ in graphs:
+            m.forward_model(tg.CSR(A.n_rows, A.n_cols, A.row_ptr, A.col_ind, A.values), X)
+    torch.cuda.synchronize()
+    for (A, X, ref) in graphs:
+        got = m.forward_model(tg.CSR(A.n_rows, A.n_cols, A.row_ptr, A.col_ind, A.values), X).clone()
+        assert_bits_equal(got.cpu().numpy(), ref.cpu().numpy(), "forward_model after other graphs")
+    tg.ops.take_device_error()
