@@ -358,40 +358,57 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             __syncwarp();
             const int rows = static_cast<int>(g.M - (m0 + q * 32) < 32 ? g.M - (m0 + q * 32) : 32);
             if (vec) {
-                constexpr int V4 = (BN / 4 + 31) / 32;  // 4-column groups per lane: lane + 32k
-                float bv[V4][4];
-#pragma unroll
-                for (int k = 0; k < V4; ++k)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int col = (lane + 32 * k) * 4 + e;
-                        bv[k][e] = (g.bias && col < g.N) ? __ldg(g.bias + col) : 0.0f;  // padding: 0
-                    }
-#pragma unroll 8
-                for (int rr = 0; rr < rows; ++rr) {  // 8 rows' loads in flight
+                // One 16-byte vector of row rr at column col: row scale, bias,
+                // activation, then into C and every peer copy (NVLink stores).
+                auto put = [&](int rr, int col, const float (&bb)[4]) {
                     const int64_t off = (m0 + q * 32 + rr) * g.ldc;
                     const float sc = g.rs ? __ldg(g.rs + m0 + q * 32 + rr) : 1.0f;
+                    const float4 t4 = *reinterpret_cast<const float4*>(tile + rr * SB + col);
+                    float x[4] = {t4.x, t4.y, t4.z, t4.w};
+                    if (has_rs) {
 #pragma unroll
-                    for (int k = 0; k < V4; ++k) {
-                        const int col = (lane + 32 * k) * 4;
-                        if (col < g.ncols) {
-                            const float4 t4 = *reinterpret_cast<const float4*>(tile + rr * SB + col);
-                            float x[4] = {t4.x, t4.y, t4.z, t4.w};
-                            if (has_rs) {
+                        for (int e = 0; e < 4; ++e) x[e] = __fmul_rn(x[e], sc);
+                    }
+                    if (has_bias) {
 #pragma unroll
-                                for (int e = 0; e < 4; ++e) x[e] = __fmul_rn(x[e], sc);
-                            }
-                            if (has_bias) {
+                        for (int e = 0; e < 4; ++e) x[e] = __fadd_rn(x[e], bb[e]);
+                    }
+                    act_v<4>(x, act, alpha);
+                    const float4 v = make_float4(x[0], x[1], x[2], x[3]);
+                    *reinterpret_cast<float4*>(g.C + off + col) = v;
+                    if (PEERS)
+                        for (int p = 0; p < peers.n; ++p) *reinterpret_cast<float4*>(peers.c[p] + off + col) = v;
+                };
+                // Lanes per row: a row of BN columns is BN / 4 vectors.  Narrow
+                // tiles store 32 / G rows per instruction (a 44-float row had
+                // kept 21 of 32 lanes idle with one row per instruction).
+                constexpr int G = BN / 4 <= 4 ? 4 : (BN / 4 <= 8 ? 8 : (BN / 4 <= 16 ? 16 : 32));
+                if constexpr (G < 32) {
+                    constexpr int RPI = 32 / G;
+                    const int col = (lane % G) * 4;
+                    float b4[4];
 #pragma unroll
-                                for (int e = 0; e < 4; ++e) x[e] = __fadd_rn(x[e], bv[k][e]);
-                            }
-                            act_v<4>(x, act, alpha);
-                            const float4 v = make_float4(x[0], x[1], x[2], x[3]);
-                            *reinterpret_cast<float4*>(g.C + off + col) = v;
-                            // The same row into every peer's copy of the output (NVLink stores).
-                            if (PEERS)
-                                for (int p = 0; p < peers.n; ++p)
-                                    *reinterpret_cast<float4*>(peers.c[p] + off + col) = v;
+                    for (int e = 0; e < 4; ++e) b4[e] = (g.bias && col + e < g.N) ? __ldg(g.bias + col + e) : 0.0f;
+                    if (col < g.ncols) {
+#pragma unroll 4
+                        for (int rr = lane / G; rr < rows; rr += RPI) put(rr, col, b4);
+                    }
+                } else {
+                    constexpr int V4 = (BN / 4 + 31) / 32;  // 4-column groups per lane: lane + 32k
+                    float bv[V4][4];
+#pragma unroll
+                    for (int k = 0; k < V4; ++k)
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int col = (lane + 32 * k) * 4 + e;
+                            bv[k][e] = (g.bias && col < g.N) ? __ldg(g.bias + col) : 0.0f;  // padding: 0
+                        }
+#pragma unroll 8
+                    for (int rr = 0; rr < rows; ++rr) {  // 8 rows' loads in flight
+#pragma unroll
+                        for (int k = 0; k < V4; ++k) {
+                            const int col = (lane + 32 * k) * 4;
+                            if (col < g.ncols) put(rr, col, bv[k]);
                         }
                     }
                 }
