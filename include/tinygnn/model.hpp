@@ -124,8 +124,9 @@ public:
     // call returns.  The uploads run on a copy stream, overlapped with the
     // compute: the CSR first (checked on the device with Tensor::sparse_csr's
     // checks as soon as it has landed), then the features in row blocks.
-    // When the first layer is a GCN layer in FAST mode, its GEMM and its
-    // gather pass over block q's columns start as soon as block q has landed,
+    // When the first layer is a GCN layer (or a transform-first SAGE-mean
+    // layer) in FAST mode, its GEMM and its gather pass over block q's
+    // columns start as soon as block q has landed,
     // and when the last layer is a one-pass FAST GCN layer it runs in row
     // chunks whose outputs go back while the next chunk runs.  Same results
     // as forward() on tensors holding the same data.  Host buffers in pinned

@@ -538,8 +538,8 @@ TG_API tg_status tg_model_forward(tg_model m, tg_tensor adjacency, tg_tensor fea
  * stride ld_out before the call returns.  The uploads are queued on a copy
  * stream and overlap the compute: the CSR first (checked on the device with
  * Tensor::sparse_csr's checks and messages as soon as it has landed), then
- * the features in row blocks; a FAST GCN first layer multiplies and gathers
- * block by block as the blocks land, and a one-pass FAST GCN last layer
+ * the features in row blocks; a FAST GCN (or transform-first SAGE-mean)
+ * first layer multiplies and gathers block by block as the blocks land, and a one-pass FAST GCN last layer
  * returns its output in row chunks while the next chunk gathers.  Results
  * equal tg_model_forward's on tensors holding the same data.  Pinned
  * (page-locked) host buffers let the copies overlap; pageable ones work with
