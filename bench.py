@@ -238,11 +238,16 @@ def cpu_impl():
     """(kind, cores): the CPU implementation the reference arm and the
     cpu_baseline leg time -- the reference library compiled from its own
     sources (oracle/_ref) where it was built, else the C restatement of its
-    algorithms (oracle/tg_oracle.c, OpenMP over every host thread)."""
+    algorithms (oracle/tg_oracle.c) -- set to every host core this process
+    may run on (torchrun starts its ranks with OMP_NUM_THREADS=1)."""
     import oracle
-    if oracle.ref is not None:
-        return "reference", oracle.ref.max_threads()
-    return "port", oracle.port.max_threads()
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        cores = os.cpu_count() or 1
+    impl = ("reference", oracle.ref) if oracle.ref is not None else ("port", oracle.port)
+    impl[1].set_num_threads(cores)
+    return impl[0], impl[1].max_threads()
 
 
 def _host(t, dtype):

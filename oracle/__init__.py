@@ -90,9 +90,13 @@ class _Port:
         L.orc_sage_layer.argtypes = [_i64, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _i32, _i32, _vp]
         L.orc_gat_layer.argtypes = [_i64, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _f32, _i32, _vp]
         L.orc_max_threads.restype = _i32
+        L.orc_set_num_threads.argtypes = [_i32]
 
     def max_threads(self) -> int:
         return self.lib.orc_max_threads()
+
+    def set_num_threads(self, n: int) -> None:
+        self.lib.orc_set_num_threads(n)
 
     def matmul(self, A, B):
         A, B = _f(A), _f(B)

@@ -40,6 +40,15 @@ EXPORT int orc_max_threads(void) {
 #endif
 }
 
+/* Sets that team size (n > 0). */
+EXPORT void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 /* ── matmul: src/ops.cpp:70-162 ───────────────────────────────────────────
  * (i, k, j) loop order; C starts at zero; every C[i][j] is one fused
  * multiply-add chain over k in increasing order (ops.cpp:121-159). */
