@@ -498,6 +498,12 @@ TG_API tg_status tg_tensor_create_csr(int64_t rows, int64_t cols, int64_t nnz, c
                                       const int32_t* col_ind, const float* values, tg_tensor* out);
 /* A dense tensor's values into host rows of stride ld. */
 TG_API tg_status tg_tensor_download(tg_tensor t, float* host, int64_t ld);
+/* New values into an existing tensor from the host, its shape and structure
+ * kept: a dense tensor's rows x cols from host rows of stride ld; a CSR
+ * tensor's nnz values (ld ignored; row_ptr / col_ind unchanged).  A tensor a
+ * captured forward reads (tg_model_capture) takes new inputs this way
+ * between replays. */
+TG_API tg_status tg_tensor_upload(tg_tensor t, const float* host, int64_t ld);
 /* rows, cols, nnz (rows*cols for dense) and format (1 = SparseCSR); each
  * pointer nullable. */
 TG_API tg_status tg_tensor_shape(tg_tensor t, int64_t* rows, int64_t* cols, int64_t* nnz,

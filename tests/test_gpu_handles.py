@@ -209,3 +209,35 @@ def test_captured_forward_replays_forward(kind):
         assert_bits_equal(again, ref, f"{kind} after refused capture")
     finally:
         set_fast_math(prev)
+
+
+def test_tensor_upload_feeds_a_captured_forward():
+    """tg_tensor_upload writes new values into a tensor (dense rows at the
+    host's stride, or a CSR's values): downloads read them back, and a
+    captured forward replayed after new features and new edge weights were
+    uploaded equals tg_model_forward on fresh tensors, bit for bit."""
+    import tinygnn_b200 as tg
+    from tinygnn_b200.handles import HTensor, set_fast_math
+    rng = np.random.default_rng(410)
+    n, fin = 3000, 41  # 41-wide host rows land beside the 44-float device stride
+    rp, ci, v = powerlaw_csr(rng, n, 5, weighted=True, diag=False)
+    X1 = rng.standard_normal((n, fin)).astype(np.float32)
+    X2 = rng.standard_normal((n, fin)).astype(np.float32)
+    v2 = (rng.random(ci.size) + 0.1).astype(np.float32)
+    spec, w = _spec_weights(rng, "gcn", fin)
+    prev = set_fast_math(True)
+    try:
+        m = _build(spec, w)
+        A, Xt = HTensor.csr(n, n, rp, ci, v), HTensor.dense(X1, n, fin)
+        g = m.capture(A, Xt)
+        Xt.upload(X2)
+        assert np.array_equal(Xt.download(), X2)
+        A.upload(v2)
+        out = np.empty((n, 7), np.float32)
+        g.replay().download(out)
+        ref = m.forward(HTensor.csr(n, n, rp, ci, v2), HTensor.dense(X2, n, fin)).download()
+        assert_bits_equal(out, ref, "replay after uploads")
+        g.free()
+        tg.ops.take_device_error()
+    finally:
+        set_fast_math(prev)

@@ -70,6 +70,7 @@ SIGNATURES = {
     "tg_tensor_create_dense": (i32, [i64, i64, vp, i64, C.POINTER(vp)]),
     "tg_tensor_create_csr": (i32, [i64, i64, i64, vp, vp, vp, C.POINTER(vp)]),
     "tg_tensor_download": (i32, [vp, vp, i64]),
+    "tg_tensor_upload": (i32, [vp, vp, i64]),
     "tg_tensor_shape": (i32, [vp, P64, P64, P64, C.POINTER(i32)]),
     "tg_tensor_free": (None, [vp]),
     "tg_model_create": (i32, [C.POINTER(vp)]),

@@ -200,6 +200,42 @@ void download_dense(const Tensor& x, float* host, int64_t ld) {
 
 extern "C" {
 
+TG_API tg_status tg_tensor_upload(tg_tensor t, const float* host, int64_t ld) {
+    return api([&] {
+        need(t, "tg_tensor_upload: t");
+        need(host, "tg_tensor_upload: host");
+        no_device_check();
+        Tensor& x = t->t;
+        if (x.format() == tinygnn::StorageFormat::SparseCSR) {
+            if (x.nnz())
+                cuda(cudaMemcpyAsync(x.mutable_device_data(), host, x.nnz() * sizeof(float), cudaMemcpyHostToDevice,
+                                     cstream()),
+                     "tg_tensor_upload");
+        } else {
+            const std::size_t r = x.rows(), c = x.cols(), dld = x.device_ld();
+            if (ld < static_cast<int64_t>(c)) throw std::invalid_argument("tg_tensor_upload: ld < cols");
+            if (r && c) {
+                if (static_cast<std::size_t>(ld) == dld) {
+                    cuda(cudaMemcpyAsync(x.mutable_device_data(), host, r * dld * sizeof(float),
+                                         cudaMemcpyHostToDevice, cstream()),
+                         "tg_tensor_upload");
+                } else {  // one DMA of the host rows as they lie, then the repack on the device
+                    float* land = device_alloc<float>(r * static_cast<std::size_t>(ld));
+                    cuda(cudaMemcpyAsync(land, host, r * static_cast<std::size_t>(ld) * sizeof(float),
+                                         cudaMemcpyHostToDevice, cstream()),
+                         "tg_tensor_upload");
+                    cuda(cudaMemcpy2DAsync(x.mutable_device_data(), dld * sizeof(float), land,
+                                           static_cast<std::size_t>(ld) * sizeof(float), c * sizeof(float), r,
+                                           cudaMemcpyDeviceToDevice, cstream()),
+                         "tg_tensor_upload");
+                    cuda(cudaFreeAsync(land, cstream()), "tg_tensor_upload");
+                }
+            }
+        }
+        cuda(cudaStreamSynchronize(cstream()), "tg_tensor_upload");
+    });
+}
+
 TG_API tg_status tg_tensor_download(tg_tensor t, float* host, int64_t ld) {
     return api([&] {
         need(t, "tg_tensor_download: t");

@@ -60,6 +60,13 @@ class HTensor:
         check(lib.tg_tensor_download(self.h, _ptr(out), cols))
         return out
 
+    def upload(self, host) -> "HTensor":
+        """New values from the host, shape and structure kept: a dense tensor's
+        rows (host rows x cols, C-contiguous), or a CSR tensor's nnz values."""
+        ld = host.shape[1] if len(host.shape) == 2 else 0
+        check(lib.tg_tensor_upload(self.h, _ptr(host), ld))
+        return self
+
     def free(self) -> None:
         if self.h:
             lib.tg_tensor_free(self.h)
