@@ -62,9 +62,10 @@ def parse():
     ap.add_argument("--edges", type=int, default=0, help="override the edge count (profiling on a smaller graph)")
     ap.add_argument("--passes", default="auto",
                     help="column passes per gather after the all-gather (auto: operand bytes / 64 MB)")
-    ap.add_argument("--exchange", choices=["auto", "peer", "nccl"], default="auto",
+    ap.add_argument("--exchange", default="auto",
                     help="N > 1: peer = the GEMM stores its tiles into every GPU's gather buffer over NVLink; "
-                         "nccl = GEMM then NCCL all-gather / broadcasts (auto: peer in fast mode)")
+                         "nccl = GEMM then NCCL all-gather / broadcasts (auto: peer in fast mode); "
+                         "or one per layer, comma-separated (e.g. peer,nccl)")
     ap.add_argument("--pipeline", choices=["auto", "on", "off"], default="auto",
                     help="N > 1: per-rank async broadcasts with a gather pass per arriving block "
                          "(auto: on 2-4 GPUs, for the layers whose exchanged operand is >= 64 MB)")
@@ -470,7 +471,8 @@ def run_ours(args):
     bpr = args.blocks_per_rank if args.blocks_per_rank == "auto" else int(args.blocks_per_rank)
     passes = args.passes if args.passes == "auto" else int(args.passes)
     model = ShardedModel(layer_stack(args.workload, w), n, comm, dev, mode=args.mode, blocks_per_rank=bpr, passes=passes,
-                         pipeline={"auto": "auto", "on": True, "off": False}[args.pipeline], exchange=args.exchange)
+                         pipeline={"auto": "auto", "on": True, "off": False}[args.pipeline],
+                         exchange=args.exchange.split(",") if "," in args.exchange else args.exchange)
     R, r0, r1 = model.R, model.row0, model.row1
     rows = r1 - r0
     A_raw = slice_rows(rp, ci, v, r0, r1, n)

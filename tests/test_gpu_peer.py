@@ -26,9 +26,13 @@ def tg():
 
 
 @pytest.mark.parametrize("M,K,N,ld,padded", [(1000, 64, 128, 128, False), (300, 128, 41, 44, False),
-                                              (300, 128, 41, 44, True), (129, 604, 128, 132, False)])
-def test_gemm_peers_stores_every_copy_and_counts_tiles(tg, M, K, N, ld, padded):
-    """Rows land in every copy; with padded rows (16-byte stores) the padding gets act(0) = 0."""
+                                              (300, 128, 41, 44, True), (129, 604, 128, 132, False),
+                                              (1000, 96, 44, 44, False)])
+@pytest.mark.parametrize("persistent", ["0", "1"])
+def test_gemm_peers_stores_every_copy_and_counts_tiles(tg, M, K, N, ld, padded, persistent, monkeypatch):
+    """Rows land in every copy; with padded rows (16-byte stores) the padding gets act(0) = 0.
+    Both kernels: one CTA per tile, and the persistent one (TINYGNN_B200_GEMM_PERSISTENT=1)."""
+    monkeypatch.setenv("TINYGNN_B200_GEMM_PERSISTENT", persistent)
     rng = np.random.default_rng(M + N)
     A = torch.as_tensor(rng.standard_normal((M, K)).astype(np.float32)).cuda()
     W = torch.as_tensor((rng.standard_normal((K, N)) * 0.1).astype(np.float32)).cuda()
@@ -49,6 +53,34 @@ def test_gemm_peers_stores_every_copy_and_counts_tiles(tg, M, K, N, ld, padded):
             assert torch.all(p[:, N:n4] == 0.0), "padding columns must hold act(0)"
             assert torch.all(p[:, n4:] == 7.0), "stored outside the copy's columns"
         assert flags.tolist() == [call * tiles] * 3
+    tg.ops.take_device_error()
+
+
+@pytest.mark.parametrize("M,K,N,ld,padded", [(40000, 64, 128, 128, False), (40000, 128, 41, 44, True),
+                                              (38001, 200, 256, 256, False)])
+def test_gemm_peers_persistent_matches_per_tile(tg, M, K, N, ld, padded, monkeypatch):
+    """More tiles than SMs (each persistent CTA walks several tiles, alternating its two
+    accumulators), row scale + bias + activation: both kernels bit-identical in every copy."""
+    rng = np.random.default_rng(M)
+    A = torch.as_tensor(rng.standard_normal((M, K)).astype(np.float32)).cuda()
+    W = torch.as_tensor((rng.standard_normal((K, N)) * 0.1).astype(np.float32)).cuda()
+    b = torch.as_tensor(rng.standard_normal(N).astype(np.float32)).cuda()
+    rs = torch.as_tensor(rng.uniform(0.1, 2.0, M).astype(np.float32)).cuda()
+    got = {}
+    for persistent in ("0", "1"):
+        monkeypatch.setenv("TINYGNN_B200_GEMM_PERSISTENT", persistent)
+        out = torch.full((M, ld), 7.0, device="cuda")
+        peers = [torch.full((M, ld), 7.0, device="cuda") for _ in range(2)]
+        flags = torch.zeros(2, dtype=torch.int64, device="cuda")
+        tg.ops.gemm_peers(A, W, out[:, :N], [p.data_ptr() for p in peers],
+                          [flags.data_ptr() + 8 * i for i in range(2)], bias=b, act="leaky_relu", alpha=0.1,
+                          cols_padded=padded, row_scale=rs)
+        torch.cuda.synchronize()
+        assert flags.tolist() == [-(-M // 128)] * 2
+        for i, p in enumerate(peers):
+            assert torch.equal(p, out), f"copy {i} differs from the local output"
+        got[persistent] = out.cpu().numpy()
+    assert_bits_equal(got["1"], got["0"], "persistent vs per-tile")
     tg.ops.take_device_error()
 
 

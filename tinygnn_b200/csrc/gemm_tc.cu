@@ -123,7 +123,7 @@ struct TcArgs {
     int act;
     float alpha;
     int64_t ncols;  // columns stored: N, or round_up(N, 4) when the rows are padded (vec)
-    int vec;        // 16-byte stores (peer copies; ldc % 4 == 0, outputs 16-byte aligned, ncols % 4 == 0)
+    int vec;        // 16-byte stores allowed (ldc % 4 == 0, outputs 16-byte aligned, ncols % 4 == 0)
     const float* rs;  // nullable: row i of the product scaled by rs[i] before the bias (one rounding)
     // Column split (local epilogue only): columns [nsplit, N) go to C2 at
     // column - nsplit (ld ldc2); nsplit == N: everything to C.
@@ -328,7 +328,14 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             // one peer, 0.31 vs 0.38 ms.)
             static_assert(BM * (BN + 4) <= STAGES * (2 * BM * BK + 2 * BN * BK), "staging tile exceeds the ring");
             const bool vec = PEERS && g.vec;
-            const int SB = vec ? BN + 4 : BN + 1;
+            // Flat: output rows exactly ncols wide (a gather buffer), so a
+            // warp's 32 rows are one contiguous block, 128-byte aligned
+            // whenever 32 * ncols * 4 is (ncols % 4 == 0): staged at stride
+            // ncols and stored as whole 512-byte warp segments -- for narrow
+            // rows (44 floats) per-row stores had sent partial lines over
+            // NVLink.
+            const bool flat = vec && g.ldc == g.ncols;
+            const int SB = flat ? static_cast<int>(g.ncols) : (vec ? BN + 4 : BN + 1);
             const bool has_rs = g.rs != nullptr, has_bias = g.bias != nullptr;
             const int act = g.act;
             const float alpha = g.alpha;
@@ -347,9 +354,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                 if (vec) {
 #pragma unroll
                     for (int j = 0; j < 16; j += 4)
-                        *reinterpret_cast<float4*>(tile + lane * SB + c0 + j) =
-                            make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                                        __uint_as_float(r[j + 3]));
+                        if (!flat || c0 + j < SB)  // flat rows hold ncols columns only
+                            *reinterpret_cast<float4*>(tile + lane * SB + c0 + j) =
+                                make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
                 } else {
 #pragma unroll
                     for (int j = 0; j < 16; ++j) tile[lane * SB + c0 + j] = __uint_as_float(r[j]);
@@ -357,7 +365,33 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             }
             __syncwarp();
             const int rows = static_cast<int>(g.M - (m0 + q * 32) < 32 ? g.M - (m0 + q * 32) : 32);
-            if (vec) {
+            if (flat) {
+                // Vector v of the block: element e = 4v is row e / ncols,
+                // column e % ncols (a vector never crosses a row).
+                const int nc = SB;
+                const int nv = rows > 0 ? rows * nc / 4 : 0;
+                const int64_t base = (m0 + q * 32) * g.ldc;
+#pragma unroll 4
+                for (int v = lane; v < nv; v += 32) {
+                    const int e = 4 * v, rr = e / nc, col = e - rr * nc;
+                    const float4 t4 = *reinterpret_cast<const float4*>(tile + e);
+                    float x[4] = {t4.x, t4.y, t4.z, t4.w};
+                    if (has_rs) {
+                        const float sc = __ldg(g.rs + m0 + q * 32 + rr);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) x[k] = __fmul_rn(x[k], sc);
+                    }
+                    if (has_bias) {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) x[k] = __fadd_rn(x[k], col + k < g.N ? __ldg(g.bias + col + k) : 0.0f);
+                    }
+                    act_v<4>(x, act, alpha);
+                    const float4 val = make_float4(x[0], x[1], x[2], x[3]);
+                    *reinterpret_cast<float4*>(g.C + base + e) = val;
+                    if (PEERS)
+                        for (int p = 0; p < peers.n; ++p) *reinterpret_cast<float4*>(peers.c[p] + base + e) = val;
+                }
+            } else if (vec) {
                 // One 16-byte vector of row rr at column col: row scale, bias,
                 // activation, then into C and every peer copy (NVLink stores).
                 auto put = [&](int rr, int col, const float (&bb)[4]) {
@@ -491,18 +525,20 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 //   warp 1      TMEM (2 accumulators) and the MMAs into accumulator t % 2;
 //   warps 2-5   the 3xTF32 split of each A stage;
 //   warps 6-9   the epilogue: 32-column chunks TMEM -> registers -> a
-//               per-warp 32 x 33 staging buffer -> one 128-byte row segment
-//               per store instruction (+ bias, activation), to C and to every
-//               peer copy; the accumulator is released as soon as its last
-//               chunk is read; a tile's peer counters are bumped after its
-//               stores (system-scope fence, release add).
+//               per-warp staging buffer -> row segments (+ row scale, bias,
+//               activation) into C and every peer copy: with 16-byte stores
+//               (g.vec) four rows' 128-byte segments per store instruction,
+//               else one row's segment of 4-byte stores; the accumulator is
+//               released as soon as its last chunk is read; a tile's peer
+//               counters are bumped after its stores (system-scope fence,
+//               release add).
 template <int BN, int STAGES>
 struct TcpSmem {
     float A[STAGES][BM * BK];
     float Al[STAGES][BM * BK];
     float Bh[STAGES][BN * BK];
     float Bl[STAGES][BN * BK];
-    float out[4][32 * 33];
+    float out[4][32 * 36];  // per epilogue warp: 32 rows x 32 columns, row stride 33 (scalar) or 36 (16-byte)
     uint64_t full[STAGES], split[STAGES], empty[STAGES], acc_full[2], acc_empty[2], drain;
     uint32_t tmem;
 };
@@ -640,6 +676,9 @@ __global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant_
         const int e = threadIdx.x - 192;
         const int q = warp & 3;  // this warp's TMEM lane quarter = its 32 rows of a tile
         float* buf = s.out[warp - 6];
+        const bool vec = g.vec != 0, has_rs = g.rs != nullptr, has_bias = g.bias != nullptr;
+        const int act = g.act;
+        const float alpha = g.alpha;
         int lt = 0;
         for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
             const int acc = lt & 1;
@@ -673,23 +712,63 @@ __global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant_
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
                 }
+                if (vec) {
+                    // Row stride 36: a quarter-warp's 16-byte writes (rows
+                    // lane..lane+7) and reads (8 vectors of one row) each
+                    // cover the 32 banks once.
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (c0 + j < BN) buf[lane * 33 + j] = __uint_as_float(r[j]);
-                __syncwarp();
-                const int col = c0 + lane;
-                const float bv = (g.bias && col < g.N) ? __ldg(g.bias + col) : 0.0f;
+                    for (int j = 0; j < 32; j += 4)
+                        if (c0 + j < BN)
+                            *reinterpret_cast<float4*>(buf + lane * 36 + j) =
+                                make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                            __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                    __syncwarp();
+                    // Lane = (row in a group of 4, 4-column vector): one store
+                    // instruction writes four rows' 128-byte segments.
+                    const int cv = (lane & 7) * 4, col = c0 + cv;
+                    if (col < g.ncols) {  // ncols = round_up(N, 4) <= BN
+                        float b4[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) b4[k] = (has_bias && col + k < g.N) ? __ldg(g.bias + col + k) : 0.0f;
 #pragma unroll 4
-                for (int rr = 0; rr < rows; ++rr) {
-                    if (col < g.ncols) {
-                        float x[1] = {buf[rr * 33 + lane]};
-                        if (g.rs) x[0] = __fmul_rn(x[0], __ldg(g.rs + r0 + rr));
-                        if (g.bias) x[0] = __fadd_rn(x[0], bv);
-                        act_v<1>(x, g.act, g.alpha);
-                        const float v = x[0];
-                        const int64_t off = (r0 + rr) * g.ldc + col;
-                        g.C[off] = v;
-                        for (int p = 0; p < peers.n; ++p) peers.c[p][off] = v;
+                        for (int rr = lane >> 3; rr < rows; rr += 4) {
+                            const float4 t4 = *reinterpret_cast<const float4*>(buf + rr * 36 + cv);
+                            float x[4] = {t4.x, t4.y, t4.z, t4.w};
+                            if (has_rs) {
+                                const float sc = __ldg(g.rs + r0 + rr);
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) x[k] = __fmul_rn(x[k], sc);
+                            }
+                            if (has_bias) {
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) x[k] = __fadd_rn(x[k], b4[k]);
+                            }
+                            act_v<4>(x, act, alpha);
+                            const float4 v = make_float4(x[0], x[1], x[2], x[3]);
+                            const int64_t off = (r0 + rr) * g.ldc + col;
+                            *reinterpret_cast<float4*>(g.C + off) = v;
+                            for (int p = 0; p < peers.n; ++p) *reinterpret_cast<float4*>(peers.c[p] + off) = v;
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (c0 + j < BN) buf[lane * 33 + j] = __uint_as_float(r[j]);
+                    __syncwarp();
+                    const int col = c0 + lane;
+                    const float bv = (has_bias && col < g.N) ? __ldg(g.bias + col) : 0.0f;
+#pragma unroll 4
+                    for (int rr = 0; rr < rows; ++rr) {
+                        if (col < g.ncols) {
+                            float x[1] = {buf[rr * 33 + lane]};
+                            if (has_rs) x[0] = __fmul_rn(x[0], __ldg(g.rs + r0 + rr));
+                            if (has_bias) x[0] = __fadd_rn(x[0], bv);
+                            act_v<1>(x, act, alpha);
+                            const float v = x[0];
+                            const int64_t off = (r0 + rr) * g.ldc + col;
+                            g.C[off] = v;
+                            for (int p = 0; p < peers.n; ++p) peers.c[p][off] = v;
+                        }
                     }
                 }
                 __syncwarp();  // buf is rewritten by the next chunk
@@ -795,18 +874,24 @@ void launch_tcp(const CUtensorMap& a, const CUtensorMap& bh, const CUtensorMap& 
     launch("gemm_tc", kern, dim3(grid), dim3(320), smem, s, a, bh, bl, g, peers);
 }
 
-// Which kernel: the per-tile one unless TINYGNN_B200_GEMM_PERSISTENT=1.  The
-// persistent kernel is correct but measured slower in the GCN forward on
-// B200, both for local output (232,965 x 602 x 128: 0.36 vs 0.33 ms;
-// 232,965 x 128 x 41: 0.16 vs 0.11 ms) and with a peer copy over NVLink
-// (2-GPU forward 3.49 vs 3.37 ms) -- its overlap of epilogue and main loop
-// does not yet pay for its one-CTA-per-SM ring.
-bool use_persistent(bool) {
-    static const bool v = [] {
-        const char* e = std::getenv("TINYGNN_B200_GEMM_PERSISTENT");
-        return e && e[0] == '1';
-    }();
-    return v;
+// Which kernel.  The persistent one overlaps a tile's epilogue -- above all
+// its stores to peer copies -- with the next tile's main loop; the per-tile
+// one has the TMA-store epilogue and, for short K, two CTAs per SM.
+// Measured on B200 (CUDA events; same-device copies standing in for peers):
+//   232,965 x 602 x 128, row-scaled:  local 0.245 vs 0.287 ms, one copy
+//   0.27 vs 0.41, three 0.33 vs 0.45; 116,483 rows: local 0.145 vs 0.162,
+//   one copy 0.16 vs 0.23; in the 2-GPU forward (copy over NVLink) the
+//   layer-1 GEMM 0.215 vs 0.294 ms;
+//   232,965 x 128 x 41: local 0.095 vs 0.080, one copy 0.15 vs 0.12;
+//   with 4-byte stores (unaligned output) the persistent kernel is slower.
+// So: the persistent kernel for K > 256 with 16-byte stores and more tiles
+// than SMs, else the per-tile one; TINYGNN_B200_GEMM_PERSISTENT=1 / 0
+// forces either (read on every call).
+bool use_persistent(bool vec, int64_t K, int64_t tiles) {
+    const char* e = std::getenv("TINYGNN_B200_GEMM_PERSISTENT");
+    if (e && e[0] == '1') return true;
+    if (e && e[0] == '0') return false;
+    return vec && K > 8 * BK && tiles > num_sms();
 }
 
 // A deep ring for long K; for short K (a few k-blocks per tile, where one
@@ -845,7 +930,7 @@ void run_tc(const CUtensorMap& ma, const CUtensorMap& ma2, const float* bt, int6
         if (g.nsplit < g.N) mc2 = make_map(g.C2, g.N - g.nsplit, g.M, g.ldc2, 32);
         g.tma_store = 1;
     }
-    if (use_persistent(peers.n > 0) && g.kb1 * BK >= g.K && g.nsplit >= g.N) {
+    if (use_persistent(g.vec != 0, g.K, ceil_div(g.M, BM)) && g.kb1 * BK >= g.K && g.nsplit >= g.N) {
         switch (BN) {
             case 16: launch_tcp<16>(ma, mh, ml, g, peers, s); break;
             case 32: launch_tcp<32>(ma, mh, ml, g, peers, s); break;
@@ -881,11 +966,12 @@ void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const
     Scratch<float> bt(static_cast<size_t>(2 * N * Kp), s);
     split_bt(B, ldb, K, N, Kp, Kp, bt.p, bt.p + N * Kp, s);
     const CUtensorMap ma = make_map(A, K, M, lda, BM);
-    // 16-byte stores (peer copies only) when every output row starts 16-byte
-    // aligned and the stored width is a multiple of 4 (N itself, or N padded
-    // when the caller's rows have room: those columns receive act(0 + 0)).
+    // 16-byte stores (the persistent kernel, and the per-tile one's peer
+    // epilogue) when every output row starts 16-byte aligned and the stored
+    // width is a multiple of 4 (N itself, or N padded when the caller's rows
+    // have room: those columns receive act(0 + 0)).
     const int64_t n4 = (N + 3) / 4 * 4;
-    bool vec = peers.n > 0 && ldc % 4 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
+    bool vec = ldc % 4 == 0 && reinterpret_cast<uintptr_t>(C) % 16 == 0 &&
                (N % 4 == 0 || (c_cols_padded && ldc >= n4));
     for (int p = 0; p < peers.n; ++p) vec = vec && reinterpret_cast<uintptr_t>(peers.c[p]) % 16 == 0;
     (void)BN;

@@ -232,13 +232,21 @@ class ShardedModel:
         # 3.42 ms, P = 4 2.08 vs 2.20 ms, P = 8 1.443 vs 1.440 ms -- at P = 8
         # the 119 MB layer-1 exchange is faster fused (GEMM + exchange 0.29
         # vs 0.32 ms) and the 41 MB layer-2 one slower (0.16 vs 0.13 ms).
-        if exchange == "auto":
+        # A list gives each layer's exchange ("peer" / "nccl").
+        if isinstance(exchange, (list, tuple)):
+            if len(exchange) != len(layers) or any(x not in ("peer", "nccl") for x in exchange):
+                raise ValueError(f"exchange: one of 'peer' / 'nccl' per layer, got {exchange!r}")
+            peer_layers = [x == "peer" for x in exchange]
+            exchange = "peer" if any(peer_layers) else "nccl"
+        elif exchange == "auto":
             exchange = ("peer" if mode == "fast" and getattr(comm, "distributed", False)
                         and all(L.W.shape[1] <= 256 for L in layers) else "nccl")
             peer_layers = [exchange == "peer" and (comm.world < 8 or n * _pad4(L.W.shape[1]) * 4 >= self.BLOCK_BYTES)
                            for L in layers]
-        else:
+        elif exchange in ("peer", "nccl"):
             peer_layers = [exchange == "peer"] * len(layers)
+        else:
+            raise ValueError(f"exchange: 'auto', 'peer', 'nccl' or one of the last two per layer, got {exchange!r}")
         if exchange == "peer" and mode != "fast":
             raise ValueError("exchange='peer' runs the tensor-core GEMM: mode must be 'fast'")
         self.exchange_kind = exchange
@@ -594,10 +602,13 @@ class ShardedModel:
             # another stream are reusable only once the GPU has caught up,
             # which made the allocator grow, and synchronise, while the host
             # ran ahead).
+            # High priority: its blocks are dispatched ahead of the scale
+            # kernel's, so it is done before the GEMM (a persistent kernel
+            # holding every SM's shared memory until its last tile) starts.
             cur = torch.cuda.current_stream()
             side = self._prep_stream
             if side is None:
-                side = self._prep_stream = torch.cuda.Stream(device=self.device)
+                side = self._prep_stream = torch.cuda.Stream(device=self.device, priority=-1)
             side.wait_stream(cur)
             with torch.cuda.stream(side):
                 if As.order is None:
