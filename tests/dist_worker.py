@@ -59,11 +59,13 @@ def main() -> int:
     # three forwards use both buffer parities.
     nccl = ShardedModel(layers, n, comm, dev, mode="fast", exchange="nccl")
     peer = ShardedModel(layers, n, comm, dev, mode="fast", exchange="peer")
+    mixed = ShardedModel(layers, n, comm, dev, mode="fast", exchange=["peer"] + ["nccl"] * (len(layers) - 1))
     for step in range(3):
         a = nccl.forward(An, A, X[r0:r1].contiguous()).clone()
+        c = mixed.forward(An, A, X[r0:r1].contiguous()).clone()
         b = peer.forward(An, A, X[r0:r1].contiguous())
         torch.cuda.synchronize()
-        same = bool(torch.equal(a, b))
+        same = bool(torch.equal(a, b)) and bool(torch.equal(a, c))
         if rank == 0:
             print(f"peer exchange step {step} same={same}", flush=True)
         ok = ok and same
@@ -112,6 +114,7 @@ def main() -> int:
         m.close()
     tg.ops.take_device_error()
     peer.close()
+    mixed.close()
     if rank == 0:
         print(f"world={world} bit-identical={ok}", flush=True)
     flag = torch.tensor([1 if ok else 0], device=dev)

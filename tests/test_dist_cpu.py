@@ -150,3 +150,17 @@ def test_rank_dropout_is_detected_not_hung():
         p.join(30)
     assert ("left", "") in got
     assert any(s == "raised" for s, _ in got), got
+
+
+def test_exchange_choice_is_validated():
+    """ShardedModel's exchange: 'auto' / 'peer' / 'nccl', or one of the last two per layer."""
+    from tinygnn_b200.dist import Comm, Layer, ShardedModel
+    layers = [Layer("gcn", torch.zeros(8, 4), None, "relu"), Layer("gcn", torch.zeros(4, 2), None, None)]
+    with pytest.raises(ValueError, match="one of 'peer' / 'nccl' per layer"):
+        ShardedModel(layers, 16, Comm(1, 0), "cpu", mode="fast", exchange=["peer"])
+    with pytest.raises(ValueError, match="one of 'peer' / 'nccl' per layer"):
+        ShardedModel(layers, 16, Comm(1, 0), "cpu", mode="fast", exchange=["peer", "ring"])
+    with pytest.raises(ValueError, match="exchange: 'auto', 'peer', 'nccl'"):
+        ShardedModel(layers, 16, Comm(1, 0), "cpu", mode="fast", exchange="ring")
+    with pytest.raises(ValueError, match="mode must be 'fast'"):
+        ShardedModel(layers, 16, Comm(1, 0), "cpu", mode="exact", exchange=["nccl", "peer"])
