@@ -540,6 +540,33 @@ def run_ours(args):
     model.timing = None
     launches = tg.launches() - launches0
     layers_ms = time_steps(layers_step, args.steps, min(args.warmup, 3), world)
+    # Beside the step: the same step given the unweighted adjacency without
+    # its values array (values=None: every entry 1.0).  The FAST gcn_norm
+    # scale then takes each degree from row_ptr and the gathers read no
+    # values; the logits are checked equal to the step's, bit for bit.
+    unweighted = bool(torch.all(A_raw.values == 1.0).item())
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([1 if unweighted else 0], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        unweighted = bool(t.item())
+    bare_info = None
+    if unweighted and args.workload == "gcn" and args.mode == "fast":
+        def bare_step():
+            model.forward_model(CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind, None,
+                                    validated=A_raw.validated), X, dis_all=dis_buf)
+        bare_ms = time_steps(bare_step, args.steps, min(args.warmup, 3), world)
+        y_vals = model.forward_model(CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind, A_raw.values,
+                                         validated=A_raw.validated), X, dis_all=dis_buf).clone()
+        y_bare = model.forward_model(CSR(A_raw.n_rows, A_raw.n_cols, A_raw.row_ptr, A_raw.col_ind, None,
+                                         validated=A_raw.validated), X, dis_all=dis_buf)
+        torch.cuda.synchronize()
+        bare_info = {"ms_per_step": bare_ms / args.steps,
+                     "logits_equal_bitwise": bool(torch.equal(y_bare, y_vals)),
+                     "what": "the step on the unweighted adjacency given without its values array (values=None, "
+                             "every entry 1.0): the FAST gcn_norm scale takes degrees from row_ptr, the gathers "
+                             "read no values; TinyGNN's CSR stores the 1.0s, which the step above reads"}
+        del y_vals
     def phase_ms(key):
         evs = ev.get(key, [])
         pairs = list(zip(evs[0::2], evs[1::2]))[-args.steps:]
@@ -560,7 +587,6 @@ def run_ours(args):
     pin = lambda t: t.cpu().pin_memory()  # noqa: E731
     # An unweighted graph (every stored value 1.0, as Reddit's is) crosses as
     # its structure only; forward_from_host writes the 1.0s on the device.
-    unweighted = bool(torch.all(A_raw.values == 1.0).item())
     h_rp, h_ci, h_X = pin(A_raw.row_ptr), pin(A_raw.col_ind), pin(X)
     h_v = None if unweighted else pin(A_raw.values)
     h_out = torch.empty((rows, CLASSES), dtype=torch.float32).pin_memory()
@@ -738,6 +764,8 @@ def run_ours(args):
             "step": ("Model::forward: gcn_norm of the raw adjacency, its row schedule, both layers, log_softmax"
                      if args.workload == "gcn" else
                      "Model::forward: the raw adjacency's row schedule, both layers, log_softmax"),
+            "unweighted_csr": None if bare_info is None else dict(
+                bare_info, value=nnz_total / (bare_info["ms_per_step"] * 1e-3), unit="edges/s"),
             "layers_only": {"value": layers_value, "unit": "edges/s", "ms_per_step": layers_ms / args.steps,
                             "what": "the layers + log_softmax on a graph normalised and scheduled once"},
             "clocks": clocks, "gpu_launches": int(per_launch * args.steps),

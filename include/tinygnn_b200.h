@@ -177,7 +177,9 @@ TG_API tg_status tg_add_bias_f32(float* X, int64_t rows, int64_t cols, int64_t l
  * EXACT: one fused multiply-add chain per output element over the row's
  * entries in stored order -> bit-identical.  row_order (nullable) lists the
  * rows in the order to schedule them (e.g. tg_csr_degree_order); it changes
- * speed only.  Optional fused epilogue + bias[F], activation. */
+ * speed only.  Optional fused epilogue + bias[F], activation.  values ==
+ * NULL: an unweighted CSR, every entry 1.0 (each update then adds the row
+ * with one rounding, as the FMA with 1.0 does) -- no values are read. */
 TG_API tg_status tg_spmm_f32(int64_t M, int64_t K, int64_t nnz, const int32_t* row_ptr,
                              const int32_t* col_ind, const float* values, const float* B,
                              int64_t F, int64_t ldb, float* C, int64_t ldc, const float* bias,
@@ -350,6 +352,9 @@ TG_API tg_status tg_csr_validate(int64_t rows, int64_t cols, int64_t nnz,
  *
  * tg_gcn_norm_scale_f32: dis_out[rows] for a block of raw rows (values read
  *   in any order; nnz = row_ptr[rows] - row_ptr[0] entries).
+ * values == NULL in both: an unweighted CSR (every a_ij = 1.0); d_i is then
+ *   the row length + 1 from row_ptr alone, and the aggregate reads no
+ *   values -- bit-identical to passing an array of ones.
  * tg_gcn_aggregate_f32: out_i = act(dis[i] * (sum_j a_ij Hs[j] + Hs_self[i])
  *   + bias) for the M rows of a block (global columns < K; Hs K x F, ld
  *   ldh; Hs_self / dis this block's rows), the sum one fused multiply-add

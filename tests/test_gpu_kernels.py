@@ -426,3 +426,33 @@ def test_sage_max_aggregate_vs_oracle(tg):
         H = rng.standard_normal((4000, F)).astype(np.float32)
         assert_bits_equal(host(tg.sage_max_aggregate(csr(tg, rp, ci, v), dev(H))),
                           P.sage_max_aggregate(rp, ci, v, H), f"sage_max F={F}")
+
+
+def test_unweighted_csr_equals_explicit_ones(tg):
+    """values=None (an unweighted CSR: no values array, every entry 1.0) gives the
+    bits an explicit array of ones gives: spmm (hub rows included, any schedule),
+    the FAST gcn_norm scale and aggregate, and the FAST GCN forward."""
+    from tinygnn_b200.dist import Comm, Layer, ShardedModel
+    rng = np.random.default_rng(7)
+    n = 20000
+    rp, ci, _ = powerlaw_csr(rng, n, 30, weighted=False, diag=False)
+    assert int(np.diff(rp).max()) >= 1023, "the graph should have hub rows for the heavy-row kernel"
+    ones = csr(tg, rp, ci, np.ones(ci.size, np.float32))
+    bare = tg.CSR(n, n, ones.row_ptr, ones.col_ind, None)
+    B = dev(rng.standard_normal((n, 64)).astype(np.float32))
+    for order in (None, tg.degree_order(ones)):
+        assert_bits_equal(host(tg.spmm(bare, B, row_order=order)), host(tg.spmm(ones, B, row_order=order)), "spmm")
+    d1, d0 = tg.ops.gcn_norm_scale(ones), tg.ops.gcn_norm_scale(bare)
+    assert_bits_equal(host(d0), host(d1), "gcn_norm_scale")
+    Hs = dev(rng.standard_normal((n, 44)).astype(np.float32))[:, :41]
+    g1 = tg.ops.gcn_aggregate(ones, Hs, Hs, d1, act="relu")
+    g0 = tg.ops.gcn_aggregate(bare, Hs, Hs, d0, act="relu")
+    assert_bits_equal(host(g0), host(g1), "gcn_aggregate")
+    W1 = dev((rng.standard_normal((32, 16)) * 0.2).astype(np.float32))
+    W2 = dev((rng.standard_normal((16, 7)) * 0.2).astype(np.float32))
+    X = dev(rng.standard_normal((n, 32)).astype(np.float32))
+    m = ShardedModel([Layer("gcn", W1, None, "relu"), Layer("gcn", W2, None, None)], n, Comm(1, 0), "cuda",
+                     mode="fast")
+    y1 = m.forward_model(tg.CSR(n, n, ones.row_ptr, ones.col_ind, ones.values), X).clone()
+    y0 = m.forward_model(tg.CSR(n, n, ones.row_ptr, ones.col_ind, None), X).clone()
+    assert_bits_equal(host(y0), host(y1), "FAST GCN forward")

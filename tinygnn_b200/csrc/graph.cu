@@ -396,20 +396,29 @@ __global__ void self_loop_fill_kernel(int64_t N, int64_t off, const int32_t* rp,
 
 // FAST gcn_norm scale: dis[i] = 1/sqrt(sum of row i's values + 1), the sum in
 // any order (a warp tree; exact for integer rows within 2^24).
+// v == nullptr: an unweighted CSR (every entry 1.0).  Below 2^24 entries
+// every partial sum of ones is an exact integer, so the row sum is the row
+// length whatever the order -- taken from row_ptr without reading entries;
+// longer rows run the same tree over ones.
 __global__ void gcn_scale_rows_kernel(int64_t N, const int32_t* rp, const float* v, float* dis) {
     const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     if (row >= N) return;
     const int lane = threadIdx.x & 31;
     const int32_t s = rp[row], e = rp[row + 1];
     float part = 0.0f;
-    for (int32_t b = s; b < e; b += 32 * kSlChunks) {
-        float x[kSlChunks];
+    if (v == nullptr && e - s < (1 << 24)) {
+        part = static_cast<float>(e - s);
+    } else {
+        for (int32_t b = s; b < e; b += 32 * kSlChunks) {
+            float x[kSlChunks];
 #pragma unroll
-        for (int u = 0; u < kSlChunks; ++u) x[u] = (b + 32 * u + lane < e) ? v[b + 32 * u + lane] : 0.0f;
+            for (int u = 0; u < kSlChunks; ++u)
+                x[u] = (b + 32 * u + lane < e) ? (v ? v[b + 32 * u + lane] : 1.0f) : 0.0f;
 #pragma unroll
-        for (int u = 0; u < kSlChunks; ++u) part = __fadd_rn(part, x[u]);
+            for (int u = 0; u < kSlChunks; ++u) part = __fadd_rn(part, x[u]);
+        }
+        for (int k = 16; k > 0; k >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, k));
     }
-    for (int k = 16; k > 0; k >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, k));
     const float d = __fadd_rn(part, 1.0f);
     if (lane == 0) dis[row] = d > 0.0f ? __fdiv_rn(1.0f, __fsqrt_rn(d)) : 0.0f;
 }
@@ -771,7 +780,7 @@ TG_API tg_status tg_gcn_norm_scale_f32(int64_t rows, int64_t nnz, const int32_t*
         if (rows < 0 || nnz < 0) invalid("gcn_norm: negative size");
         if (rows == 0) return;
         check_ptr("gcn_norm", "row_ptr/dis_out", row_ptr && dis_out ? row_ptr : nullptr, true);
-        check_ptr("gcn_norm", "values", values, nnz > 0);
+        // values == NULL: an unweighted CSR (every entry 1.0)
         check_csr_input(rows, -1, -1, row_ptr, nullptr, as_stream(stream));  // values read by row only
         launch("gcn_scale_rows", gcn_scale_rows_kernel, dim3(warp_rows_grid(rows)), dim3(256), 0, as_stream(stream),
                rows, row_ptr, values, dis_out);

@@ -357,7 +357,7 @@ TG_API tg_status tg_spmm_f32(int64_t M, int64_t K, int64_t nnz, const int32_t* r
         check_ld("spmm", "B", ldb, F);
         check_ld("spmm", "C", ldc, F);
         check_ptr("spmm", "row_ptr", row_ptr, M > 0);
-        check_ptr("spmm", "col_ind/values", col_ind && values ? col_ind : nullptr, nnz > 0);
+        check_ptr("spmm", "col_ind", col_ind, nnz > 0);  // values == NULL: every entry 1.0
         check_ptr("spmm", "B", B, nnz > 0 && F > 0);
         check_ptr("spmm", "C", C, M > 0 && F > 0);
         check_csr_input(M, K, nnz, row_ptr, col_ind, as_stream(stream), row_order);
@@ -462,7 +462,7 @@ TG_API tg_status tg_gcn_aggregate_f32(int64_t M, int64_t K, int64_t nnz, const i
         check_ld("gcn_aggregate", "out", ldo, F);
         check_ptr("gcn_aggregate", "row_ptr/Hs_self/dis/out", row_ptr && Hs_self && dis && out ? row_ptr : nullptr,
                   M > 0 && F > 0);
-        check_ptr("gcn_aggregate", "col_ind/values/Hs", col_ind && values && Hs ? col_ind : nullptr, nnz > 0 && F > 0);
+        check_ptr("gcn_aggregate", "col_ind/Hs", col_ind && Hs ? col_ind : nullptr, nnz > 0 && F > 0);  // values may be NULL
         if ((seg_begin == nullptr) != (seg_end == nullptr)) invalid("gcn_aggregate: seg_begin and seg_end go together");
         // with segments the CSR may be a row-offset view: its entry count is row_ptr[M]
         check_csr_input(M, K, seg_begin ? -1 : nnz, row_ptr, col_ind, as_stream(stream), row_order);

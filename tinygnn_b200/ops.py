@@ -58,13 +58,18 @@ def _vec(t: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
 
 @dataclass
 class CSR:
-    """Device CSR matrix: int32 row_ptr[n_rows+1], col_ind[nnz], float32 values[nnz]."""
+    """Device CSR matrix: int32 row_ptr[n_rows+1], col_ind[nnz], float32 values[nnz].
+
+    values may be None: an unweighted CSR (every entry 1.0, no array), which
+    spmm / spmm_segment, gcn_norm_scale, gcn_aggregate and the FAST GCN
+    forward take as they take an array of ones, bit for bit, without reading
+    one; every other operation needs the values array."""
 
     n_rows: int
     n_cols: int
     row_ptr: torch.Tensor
     col_ind: torch.Tensor
-    values: torch.Tensor
+    values: Optional[torch.Tensor]
     # Optional row schedule (int32 permutation, longest rows first) reused by
     # every gather over this matrix; without it large gathers compute one.
     order: Optional[torch.Tensor] = None
@@ -94,7 +99,8 @@ class CSR:
         return cls(n, n if n_cols is None else int(n_cols), rp, ci, v)
 
     def numpy(self):
-        return (self.row_ptr.cpu().numpy(), self.col_ind.cpu().numpy(), self.values.cpu().numpy())
+        v = (np.ones(self.nnz, np.float32) if self.values is None else self.values.cpu().numpy())
+        return (self.row_ptr.cpu().numpy(), self.col_ind.cpu().numpy(), v)
 
 
 def _csr_call(csrs, fn, *args) -> None:
