@@ -82,6 +82,13 @@ typedef enum tg_mode { TG_MODE_EXACT = 0, TG_MODE_FAST = 1 } tg_mode;
  * read with 16-byte loads.  Results do not change. */
 #define TG_FLAG_B_ROWS_PADDED 0x100
 
+/* OR'ed into a GEMM's `mode` (tg_gemm_f32, tg_gemm_rowscale_f32,
+ * tg_gemm_pair_f32; the `flags` of tg_gemm_peers_f32): the rows of C have
+ * room up to round_up(N, 4) columns, which may then be written (the
+ * epilogue applied to a zero product: act(0)), so FAST mode can store rows
+ * 16 bytes at a time.  Without it nothing past column N is written. */
+#define TG_FLAG_C_COLS_PADDED 0x200
+
 /* ── library ─────────────────────────────────────────────────────────────── */
 TG_API const char* tg_last_error_message(void); /* thread-local */
 TG_API const char* tg_version(void);
@@ -457,7 +464,6 @@ TG_API tg_status tg_ipc_close_handle(void* base);
  * rows of C and of its copies have room up to round_up(N, 4) columns, which
  * may then be written (with act(0)) so that rows are stored 16 bytes at a
  * time. */
-#define TG_FLAG_C_COLS_PADDED 0x200
 TG_API tg_status tg_gemm_peers_f32(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                                    const float* B, int64_t ldb, float* C, int64_t ldc,
                                    const float* bias, int32_t act, float alpha,

@@ -10,6 +10,7 @@ import pytest
 import torch
 
 import oracle
+from tests.helpers import assert_bits_equal
 
 pytestmark = pytest.mark.gpu
 P = oracle.port
@@ -45,7 +46,8 @@ def check(got, A, B, what, bias=None):
 
 
 @pytest.mark.parametrize("shape", [(128, 32, 16), (1, 8, 7), (130, 70, 41), (300, 602, 128), (257, 256, 64),
-                                   (1000, 128, 41), (4099, 602, 256), (64, 1433, 16), (513, 33, 48), (200, 4, 1)])
+                                   (1000, 128, 41), (4099, 602, 256), (64, 1433, 16), (513, 33, 48), (200, 4, 1),
+                                   (700, 128, 82), (300, 602, 96), (129, 40, 65)])
 def test_tc_gemm_vs_oracle(tg, shape):
     M, K, N = shape
     rng = np.random.default_rng(M * 7 + K + N)
@@ -55,6 +57,25 @@ def test_tc_gemm_vs_oracle(tg, shape):
     torch.cuda.synchronize()
     tg.ops.take_device_error()
     check(out.cpu().numpy(), A, B, f"tc {shape}")
+
+
+@pytest.mark.parametrize("N,padded_ok", [(41, False), (41, True), (44, False), (7, False)])
+def test_tc_gemm_writes_nothing_past_n(tg, N, padded_ok):
+    """An aligned output view whose rows have room past N (TMA-store epilogue):
+    columns >= N stay untouched unless the caller declares them writable
+    (cols_padded: up to round_up(N, 4), holding act(0) = 0 here)."""
+    rng = np.random.default_rng(N)
+    A = rng.standard_normal((700, 602)).astype(np.float32)
+    B = (rng.standard_normal((602, N)) * 0.05).astype(np.float32)
+    Cw = torch.full((700, 48), 5.0, device="cuda")
+    tg.ops.matmul(padded(A), torch.as_tensor(B).cuda(), out=Cw[:, :N], mode="fast", cols_padded=padded_ok)
+    torch.cuda.synchronize()
+    tg.ops.take_device_error()
+    h = Cw.cpu().numpy()
+    check(h[:, :N], A, B, f"tc N={N}")
+    n4 = (N + 3) // 4 * 4 if padded_ok else N
+    assert np.all(h[:, N:n4] == 0.0), "declared padding holds act(0)"
+    assert np.all(h[:, n4:] == 5.0), "written past the output's columns"
 
 
 def test_tc_gemm_epilogue_and_strided_out(tg):
@@ -101,9 +122,11 @@ def test_fast_layers_within_tolerance(tg):
 
 
 @pytest.mark.parametrize("M,K,N", [(1000, 602, 128), (513, 128, 41), (300, 96, 20), (129, 33, 7)])
-def test_tc_gemm_pair_vs_oracle(tg, M, K, N):
+@pytest.mark.parametrize("persistent", ["0", "1"])
+def test_tc_gemm_pair_vs_oracle(tg, M, K, N, persistent, monkeypatch):
     """C1 = A . B1, C2 = A . B2 in one tensor-core pass ([B1 | B2], columns
-    split in the epilogue into two strided outputs)."""
+    split in the epilogue into two strided outputs); both kernels."""
+    monkeypatch.setenv("TINYGNN_B200_GEMM_PERSISTENT", persistent)
     rng = np.random.default_rng(M + K + N)
     A = rng.standard_normal((M, K)).astype(np.float32)
     B1 = (rng.standard_normal((K, N)) / np.sqrt(K)).astype(np.float32)
@@ -118,6 +141,28 @@ def test_tc_gemm_pair_vs_oracle(tg, M, K, N):
     check(h[:, :N], A, B1, "pair C1")
     check(h[:, half:half + N], A, B2, "pair C2")
     assert np.all(h[:, N:half] == 7.0) and np.all(h[:, half + N:] == 7.0)
+
+
+@pytest.mark.parametrize("N", [128, 64, 44, 41])
+def test_tc_gemm_pair_persistent_matches_per_tile(tg, N, monkeypatch):
+    """More tiles than SMs (each persistent CTA walks several, alternating its
+    two accumulators), K > 256: the split outputs of both kernels bit-identical."""
+    rng = np.random.default_rng(N)
+    M, K = 40000, 300
+    A = padded(rng.standard_normal((M, K)).astype(np.float32))
+    B1 = torch.as_tensor((rng.standard_normal((K, N)) / np.sqrt(K)).astype(np.float32)).cuda()
+    B2 = torch.as_tensor((rng.standard_normal((K, N)) / np.sqrt(K)).astype(np.float32)).cuda()
+    half = (N + 3) // 4 * 4
+    got = {}
+    for persistent in ("0", "1"):
+        monkeypatch.setenv("TINYGNN_B200_GEMM_PERSISTENT", persistent)
+        T = torch.full((M, 2 * half), 7.0, device="cuda")
+        tg.ops.gemm_pair(A, B1, B2, T[:, :N], T[:, half:half + N])
+        torch.cuda.synchronize()
+        got[persistent] = T.cpu().numpy()
+    tg.ops.take_device_error()
+    assert_bits_equal(got["1"], got["0"], "persistent vs per-tile (both outputs, padding untouched)")
+    assert np.all(got["1"][:, N:half] == 7.0) and np.all(got["1"][:, half + N:] == 7.0)
 
 
 @pytest.mark.parametrize("M,K1,K2,N", [(1000, 128, 128, 128), (700, 40, 602, 41), (300, 33, 70, 64), (129, 8, 8, 7)])

@@ -182,7 +182,8 @@ Tensor GCNLayer::forward(const Tensor& A_norm, const Tensor& H) const {
     check(tg_gemm_f32(static_cast<int64_t>(N), static_cast<int64_t>(out_features_), static_cast<int64_t>(in_features_),
                       H.device_data(), static_cast<int64_t>(H.device_ld()), weight_.device_data(),
                       static_cast<int64_t>(weight_.device_ld()), HW.mutable_device_data(),
-                      static_cast<int64_t>(HW.device_ld()), nullptr, TG_ACT_NONE, 0.0f, detail::mode(), stream()));
+                      static_cast<int64_t>(HW.device_ld()), nullptr, TG_ACT_NONE, 0.0f,
+                      detail::mode() | TG_FLAG_C_COLS_PADDED, stream()));
     const detail::TrustedCsr trusted_csr;
     check(tg_spmm_f32(static_cast<int64_t>(N), static_cast<int64_t>(N), static_cast<int64_t>(A_norm.nnz()),
                       A_norm.device_row_ptr(), A_norm.device_col_ind(), A_norm.device_data(), HW.device_data(),
@@ -242,8 +243,8 @@ Tensor SAGELayer::forward(const Tensor& A, const Tensor& H) const {
         check(tg_gemm_pair_f32(static_cast<int64_t>(N), static_cast<int64_t>(Fo), static_cast<int64_t>(Fi),
                                H.device_data(), static_cast<int64_t>(H.device_ld()), w.wn, w.ws,
                                static_cast<int64_t>(Fo), Tn.mutable_device_data(), static_cast<int64_t>(Tn.device_ld()),
-                               Ts.mutable_device_data(), static_cast<int64_t>(Ts.device_ld()), TG_MODE_FAST,
-                               stream()));
+                               Ts.mutable_device_data(), static_cast<int64_t>(Ts.device_ld()),
+                               TG_MODE_FAST | TG_FLAG_C_COLS_PADDED, stream()));
         // The combine gathers Tn rows in a longest-first schedule, in column
         // passes when Tn is larger than kPassBytes (each pass's slice stays
         // in L2; the passes carry each output element's chain through out).

@@ -231,8 +231,8 @@ Tensor gcn_forward_scaled(const GCNLayer& L, ScaledGraph& g, const Tensor& H) {
                                static_cast<int64_t>(L.in_features()), H.device_data(),
                                static_cast<int64_t>(H.device_ld()), L.weight().device_data(),
                                static_cast<int64_t>(L.weight().device_ld()), Hs.mutable_device_data(),
-                               static_cast<int64_t>(Hs.device_ld()), g.dis.p, nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST,
-                               stream()));
+                               static_cast<int64_t>(Hs.device_ld()), g.dis.p, nullptr, TG_ACT_NONE, 0.0f,
+                               TG_MODE_FAST | TG_FLAG_C_COLS_PADDED, stream()));
     const int passes = static_cast<int>(
         std::max<std::size_t>(1, (N * Hs.device_ld() * sizeof(float) + kPassBytes - 1) / kPassBytes));
     const int32_t* sp = passes > 1 ? g.split_points(passes) : nullptr;
@@ -617,7 +617,7 @@ void Model::forward_host(std::size_t n, std::size_t nnz, const int32_t* row_ptr,
                                            static_cast<int64_t>(ldx), L.weight().device_data(),
                                            static_cast<int64_t>(L.weight().device_ld()),
                                            Hs.mutable_device_data() + a * ldh, static_cast<int64_t>(ldh), g.sg->dis.p + a,
-                                           nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST, stream()));
+                                           nullptr, TG_ACT_NONE, 0.0f, TG_MODE_FAST | TG_FLAG_C_COLS_PADDED, stream()));
             check(tg_gcn_aggregate_f32(
                 static_cast<int64_t>(n), static_cast<int64_t>(n), static_cast<int64_t>(nnz), A.device_row_ptr(),
                 A.device_col_ind(), A.device_data(), Hs.device_data(), static_cast<int64_t>(Fo),
@@ -662,8 +662,8 @@ void Model::forward_host(std::size_t n, std::size_t nnz, const int32_t* row_ptr,
                                        static_cast<int64_t>(feature_cols), X.device_data() + a * ldx,
                                        static_cast<int64_t>(ldx), w.wn, w.ws, static_cast<int64_t>(Fo),
                                        Tn.mutable_device_data() + a * ldn, static_cast<int64_t>(ldn),
-                                       Ts.mutable_device_data() + a * lds, static_cast<int64_t>(lds), TG_MODE_FAST,
-                                       stream()));
+                                       Ts.mutable_device_data() + a * lds, static_cast<int64_t>(lds),
+                                       TG_MODE_FAST | TG_FLAG_C_COLS_PADDED, stream()));
             if (sp)
                 check(tg_sage_mean_combine_segment_f32(
                     static_cast<int64_t>(n), static_cast<int64_t>(n), A.device_row_ptr(), A.device_col_ind(),

@@ -199,7 +199,8 @@ void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const
              bool c_cols_padded = false, const float* row_scale = nullptr);
 
 void gemm_tc_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B1, const float* B2,
-                  int64_t ldb, float* C1, int64_t ldc1, float* C2, int64_t ldc2, cudaStream_t s);
+                  int64_t ldb, float* C1, int64_t ldc1, float* C2, int64_t ldc2, cudaStream_t s,
+                  bool c_cols_padded);
 void gemm_tc_cat(int64_t M, int64_t N, int64_t K1, const float* A1, int64_t lda1, int64_t K2, const float* A2,
                  int64_t lda2, const float* B1, int64_t ldb1, const float* B2, int64_t ldb2, float* C, int64_t ldc,
                  const float* bias, int act, float alpha, cudaStream_t s);
@@ -209,7 +210,7 @@ void gemm_tc_cat(int64_t M, int64_t N, int64_t K1, const float* A1, int64_t lda1
 void gemm(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
           int64_t ldc, const float* bias, int act, float alpha, int mode, cudaStream_t s) {
     if ((mode & 0xff) == TG_MODE_FAST && gemm_tc_supported(N, K, A, lda))
-        gemm_tc(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, s);
+        gemm_tc(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, s, PeerOut{}, (mode & TG_FLAG_C_COLS_PADDED) != 0);
     else
         gemm_exact(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, s);
 }
@@ -235,7 +236,8 @@ void gemm_rowscale(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                    cudaStream_t s) {
     if (M == 0 || N == 0) return;
     if ((mode & 0xff) == TG_MODE_FAST && gemm_tc_supported(N, K, A, lda)) {
-        gemm_tc(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, s, PeerOut{}, false, rs);
+        gemm_tc(M, N, K, A, lda, B, ldb, C, ldc, bias, act, alpha, s, PeerOut{}, (mode & TG_FLAG_C_COLS_PADDED) != 0,
+                rs);
         return;
     }
     gemm_exact(M, N, K, A, lda, B, ldb, C, ldc, nullptr, TG_ACT_NONE, 0.0f, s);
@@ -250,7 +252,7 @@ void gemm_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, con
                int64_t ldb, float* C1, int64_t ldc1, float* C2, int64_t ldc2, int mode, cudaStream_t s) {
     if (M == 0 || N == 0) return;
     if ((mode & 0xff) == TG_MODE_FAST && gemm_tc_supported(2 * N, K, A, lda)) {
-        gemm_tc_pair(M, N, K, A, lda, B1, B2, ldb, C1, ldc1, C2, ldc2, s);
+        gemm_tc_pair(M, N, K, A, lda, B1, B2, ldb, C1, ldc1, C2, ldc2, s, (mode & TG_FLAG_C_COLS_PADDED) != 0);
         return;
     }
     gemm(M, N, K, A, lda, B1, ldb, C1, ldc1, nullptr, TG_ACT_NONE, 0.0f, mode, s);

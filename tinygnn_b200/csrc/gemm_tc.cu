@@ -135,6 +135,12 @@ struct TcArgs {
     // The epilogue stores through tmC / tmC2 (TMA, 32 x 32 boxes, 128-byte
     // swizzle): C rows 16-byte aligned, and nsplit a multiple of 32.
     int tma_store;
+    // Column split with a gap: product columns [gap_lo, nsplit) are zero
+    // padding stored nowhere (C holds gap_lo columns); 0 = no gap.
+    int64_t gap_lo = 0;
+    // The caller's rows have room up to round_up(width, 4) columns of each
+    // output, which the epilogue may write (the epilogue of a zero product).
+    int pad_ok = 0;
 };
 
 // PEERS: the epilogue also stores to peer copies (and may use 16-byte
@@ -472,6 +478,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
                                 g.C2[row * g.ldc2 + (col - g.nsplit)] = v;
                                 continue;
                             }
+                            if (!PEERS && g.gap_lo && col >= g.gap_lo) continue;  // the split's padding gap
                             g.C[off + col] = v;
                             if (PEERS)
                                 for (int p = 0; p < peers.n; ++p) peers.c[p][off + col] = v;
@@ -677,6 +684,7 @@ __global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant_
         const int q = warp & 3;  // this warp's TMEM lane quarter = its 32 rows of a tile
         float* buf = s.out[warp - 6];
         const bool vec = g.vec != 0, has_rs = g.rs != nullptr, has_bias = g.bias != nullptr;
+        const bool split = g.nsplit < g.N;  // columns [nsplit, N) go to C2 (local output only)
         const int act = g.act;
         const float alpha = g.alpha;
         int lt = 0;
@@ -745,6 +753,11 @@ __global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant_
                             }
                             act_v<4>(x, act, alpha);
                             const float4 v = make_float4(x[0], x[1], x[2], x[3]);
+                            if (split && col >= g.nsplit) {  // a vector never straddles nsplit (% 4 == 0)
+                                *reinterpret_cast<float4*>(g.C2 + (r0 + rr) * g.ldc2 + (col - g.nsplit)) = v;
+                                continue;
+                            }
+                            if (split && g.gap_lo && col >= g.gap_lo) continue;  // the gap (gap_lo % 4 == 0)
                             const int64_t off = (r0 + rr) * g.ldc + col;
                             *reinterpret_cast<float4*>(g.C + off) = v;
                             for (int p = 0; p < peers.n; ++p) *reinterpret_cast<float4*>(peers.c[p] + off) = v;
@@ -765,6 +778,11 @@ __global__ void __launch_bounds__(320, 1) gemm_tcp_kernel(const __grid_constant_
                             if (has_bias) x[0] = __fadd_rn(x[0], bv);
                             act_v<1>(x, act, alpha);
                             const float v = x[0];
+                            if (split && col >= g.nsplit) {
+                                g.C2[(r0 + rr) * g.ldc2 + (col - g.nsplit)] = v;
+                                continue;
+                            }
+                            if (split && g.gap_lo && col >= g.gap_lo) continue;
                             const int64_t off = (r0 + rr) * g.ldc + col;
                             g.C[off] = v;
                             for (int p = 0; p < peers.n; ++p) peers.c[p][off] = v;
@@ -908,7 +926,12 @@ void launch_tc(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& b
     else launch_tc_s<BN, stages_for(BN)>(a, a2, bh, bl, c, c2, g, peers, s);
 }
 
-int tile_n(int64_t N) { return N <= 16 ? 16 : N <= 32 ? 32 : N <= 48 ? 48 : N <= 64 ? 64 : N <= 128 ? 128 : 256; }
+// Output tile width.  96 (for 65..96 columns, e.g. a pair product of two
+// 41-wide weights) keeps a short-K two-stage ring small enough for two CTAs
+// per SM, which a 128-wide tile is not.
+int tile_n(int64_t N) {
+    return N <= 16 ? 16 : N <= 32 ? 32 : N <= 48 ? 48 : N <= 64 ? 64 : N <= 96 ? 96 : N <= 128 ? 128 : 256;
+}
 
 // Runs the kernel for a prepared B^T (hi at bt, lo at bt + N * ldt) and
 // A maps; g's N, K (and C2 / nsplit / kb1) describe the product.
@@ -924,18 +947,24 @@ void run_tc(const CUtensorMap& ma, const CUtensorMap& ma2, const float* bt, int6
     g.tma_store = 0;
     // (Measured in the GCN forward on B200, same build: layer-1 GEMM 0.46 ->
     // 0.385 ms, layer-2 0.132 -> 0.091 ms against the per-row stores.)
-    if (peers.n == 0 && g.M <= INT32_MAX && aligned16(g.C, g.ldc) &&
-        (g.nsplit >= g.N || (g.nsplit % 32 == 0 && aligned16(g.C2, g.ldc2)))) {
-        mc = make_map(g.C, std::min(g.N, g.nsplit), g.M, g.ldc, 32);
-        if (g.nsplit < g.N) mc2 = make_map(g.C2, g.N - g.nsplit, g.M, g.ldc2, 32);
+    // A TMA store writes whole 16-byte pieces of a row, also where the box
+    // is clipped at the tensor's width: each stored width must be a multiple
+    // of 4 floats -- its own, or rounded up where the caller's rows have room.
+    const auto w4 = [&](int64_t w) { return g.pad_ok ? (w + 3) / 4 * 4 : w; };
+    const int64_t w1 = w4(g.gap_lo ? g.gap_lo : std::min(g.N, g.nsplit)), w2 = w4(g.N - g.nsplit);
+    if (peers.n == 0 && g.M <= INT32_MAX && aligned16(g.C, g.ldc) && w1 % 4 == 0 &&
+        (g.nsplit >= g.N || (g.nsplit % 32 == 0 && aligned16(g.C2, g.ldc2) && w2 % 4 == 0))) {
+        mc = make_map(g.C, w1, g.M, g.ldc, 32);  // boxes clip at C's (stored) width
+        if (g.nsplit < g.N) mc2 = make_map(g.C2, w2, g.M, g.ldc2, 32);
         g.tma_store = 1;
     }
-    if (use_persistent(g.vec != 0, g.K, ceil_div(g.M, BM)) && g.kb1 * BK >= g.K && g.nsplit >= g.N) {
+    if (use_persistent(g.vec != 0, g.K, ceil_div(g.M, BM)) && g.kb1 * BK >= g.K) {
         switch (BN) {
             case 16: launch_tcp<16>(ma, mh, ml, g, peers, s); break;
             case 32: launch_tcp<32>(ma, mh, ml, g, peers, s); break;
             case 48: launch_tcp<48>(ma, mh, ml, g, peers, s); break;
             case 64: launch_tcp<64>(ma, mh, ml, g, peers, s); break;
+            case 96: launch_tcp<96>(ma, mh, ml, g, peers, s); break;
             case 128: launch_tcp<128>(ma, mh, ml, g, peers, s); break;
             default: launch_tcp<256>(ma, mh, ml, g, peers, s); break;
         }
@@ -946,6 +975,7 @@ void run_tc(const CUtensorMap& ma, const CUtensorMap& ma2, const float* bt, int6
         case 32: launch_tc<32>(ma, ma2, mh, ml, mc, mc2, g, peers, s); break;
         case 48: launch_tc<48>(ma, ma2, mh, ml, mc, mc2, g, peers, s); break;
         case 64: launch_tc<64>(ma, ma2, mh, ml, mc, mc2, g, peers, s); break;
+        case 96: launch_tc<96>(ma, ma2, mh, ml, mc, mc2, g, peers, s); break;
         case 128: launch_tc<128>(ma, ma2, mh, ml, mc, mc2, g, peers, s); break;
         default: launch_tc<256>(ma, ma2, mh, ml, mc, mc2, g, peers, s); break;
     }
@@ -975,25 +1005,45 @@ void gemm_tc(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const
                (N % 4 == 0 || (c_cols_padded && ldc >= n4));
     for (int p = 0; p < peers.n; ++p) vec = vec && reinterpret_cast<uintptr_t>(peers.c[p]) % 16 == 0;
     (void)BN;
-    const TcArgs g{C, ldc, M, N, K, bias, act, alpha, vec ? n4 : N, vec ? 1 : 0, row_scale, nullptr, 0, N,
-                   static_cast<int>(ceil_div(K, BK)), 0};
+    TcArgs g{C, ldc, M, N, K, bias, act, alpha, vec ? n4 : N, vec ? 1 : 0, row_scale, nullptr, 0, N,
+             static_cast<int>(ceil_div(K, BK)), 0};
+    g.pad_ok = c_cols_padded && ldc >= n4;
     run_tc(ma, ma, bt.p, Kp, g, peers, s);
 }
 
 // C1 = A . B1 and C2 = A . B2 (K x N each) in one pass over A: the product
 // with [B1 | B2] (2N <= 256 columns), its columns split in the epilogue.
 void gemm_tc_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B1, const float* B2,
-                  int64_t ldb, float* C1, int64_t ldc1, float* C2, int64_t ldc2, cudaStream_t s) {
+                  int64_t ldb, float* C1, int64_t ldc1, float* C2, int64_t ldc2, cudaStream_t s,
+                  bool c_cols_padded) {
     if (M == 0 || N == 0) return;
-    const int64_t Kp = (K + 3) / 4 * 4, N2 = 2 * N;
+    // B2 starts at product column Ns.  Ns = N, unless N is not a multiple of
+    // 32 and both outputs can take TMA stores: then Ns = round_up(N, 32),
+    // columns [N, Ns) a zero gap, so the split falls on a 32-column box and
+    // both outputs are stored by TMA boxes clipped at their widths (per-row
+    // stores had taken the 232,965 x 128 x (41 + 41) product 0.26 ms).
+    const bool aligned = aligned16(C1, ldc1) && aligned16(C2, ldc2);
+    const int64_t N32 = (N + 31) / 32 * 32, n4 = (N + 3) / 4 * 4;
+    const bool pad_ok = c_cols_padded && ldc1 >= n4 && ldc2 >= n4;
+    const bool gap = N % 32 != 0 && aligned && (N % 4 == 0 || pad_ok) && M <= INT32_MAX && N32 + N <= 256;
+    const int64_t Kp = (K + 3) / 4 * 4, Ns = gap ? N32 : N, N2 = Ns + N;
     Scratch<float> bt(static_cast<size_t>(2 * N2 * Kp), s);
     float* hi = bt.p;
     float* lo = bt.p + N2 * Kp;
-    split_bt(B1, ldb, K, N, Kp, Kp, hi, lo, s);                   // rows [0, N) of B^T
-    split_bt(B2, ldb, K, N, Kp, Kp, hi + N * Kp, lo + N * Kp, s); // rows [N, 2N)
+    split_bt(B1, ldb, K, N, Kp, Kp, hi, lo, s);                     // rows [0, N) of B^T
+    if (gap) {                                                      // rows [N, Ns): zero
+        TG_CUDA(cudaMemsetAsync(hi + N * Kp, 0, static_cast<size_t>((Ns - N) * Kp) * sizeof(float), s));
+        TG_CUDA(cudaMemsetAsync(lo + N * Kp, 0, static_cast<size_t>((Ns - N) * Kp) * sizeof(float), s));
+    }
+    split_bt(B2, ldb, K, N, Kp, Kp, hi + Ns * Kp, lo + Ns * Kp, s);  // rows [Ns, Ns + N)
     const CUtensorMap ma = make_map(A, K, M, lda, BM);
-    const TcArgs g{C1, ldc1, M, N2, K, nullptr, TG_ACT_NONE, 0.0f, N2, 0, nullptr, C2, ldc2, N,
-                   static_cast<int>(ceil_div(K, BK)), 0};
+    // 16-byte stores (persistent kernel) when both outputs' rows are 16-byte
+    // aligned and N % 4 == 0 (no vector straddles the split or the gap)
+    const bool vec = aligned && N % 4 == 0;
+    TcArgs g{C1, ldc1, M, N2, K, nullptr, TG_ACT_NONE, 0.0f, N2, vec ? 1 : 0, nullptr, C2, ldc2, Ns,
+             static_cast<int>(ceil_div(K, BK)), 0};
+    g.gap_lo = gap ? N : 0;
+    g.pad_ok = pad_ok;
     run_tc(ma, ma, bt.p, Kp, g, PeerOut{}, s);
 }
 

@@ -43,7 +43,7 @@ void gcn_layer(int64_t N, const int32_t* rp, const int32_t* ci, const float* v, 
     if (N == 0 || F_out == 0) return;
     const int64_t ldw = pad4(F_out);
     Scratch<float> HW(static_cast<size_t>(N * ldw), s);
-    gemm(N, F_out, F_in, H, ldh, W, F_out, HW.p, ldw, nullptr, TG_ACT_NONE, 0.0f, mode, s);
+    gemm(N, F_out, F_in, H, ldh, W, F_out, HW.p, ldw, nullptr, TG_ACT_NONE, 0.0f, mode | TG_FLAG_C_COLS_PADDED, s);
     GatherArgs a;
     a.M = N; a.rp = rp; a.ci = ci; a.val = v; a.order = order;
     a.B = HW.p; a.ldb = ldw; a.b_padded = true; a.F = F_out;
@@ -79,7 +79,7 @@ void sage_layer(int64_t N, const int32_t* rp, const int32_t* ci, const float* H,
     const int64_t half = pad4(F_out);
     const int64_t ldt = 2 * half;
     Scratch<float> T(static_cast<size_t>(N * ldt), s);
-    gemm_pair(N, F_out, F_in, H, ldh, Wn, Ws, F_out, T.p, ldt, T.p + half, ldt, mode, s);
+    gemm_pair(N, F_out, F_in, H, ldh, Wn, Ws, F_out, T.p, ldt, T.p + half, ldt, mode | TG_FLAG_C_COLS_PADDED, s);
     GatherArgs a;
     a.M = N; a.rp = rp; a.ci = ci; a.order = order;
     a.B = T.p; a.ldb = ldt; a.b_padded = true; a.F = F_out;

@@ -368,12 +368,12 @@ class ShardedModel:
                            row_scale=self.scale if self._scaled(li) else None)
         elif L.kind == "sage":  # W_neigh and W_self in one pass over H (FAST: one tensor-core GEMM)
             ops.gemm_pair(H, L.W, L.W_self, self.full[li][r * self.R:r * self.R + self.rows, :fo],
-                          self.selfs[li][:, :fo], mode=self.mode)
-        else:
+                          self.selfs[li][:, :fo], mode=self.mode, cols_padded=True)
+        else:  # the gather buffer's rows are padded to 16 bytes
             ops.matmul(H, L.W, out=self.full[li][r * self.R:r * self.R + self.rows, :fo], mode=self.mode,
-                       row_scale=self.scale if self._scaled(li) else None)
+                       row_scale=self.scale if self._scaled(li) else None, cols_padded=True)
         if L.kind == "sage" and self.pex is not None and self.peer_layers[li]:
-            ops.matmul(H, L.W_self, out=self.selfs[li][:, :fo], mode=self.mode)
+            ops.matmul(H, L.W_self, out=self.selfs[li][:, :fo], mode=self.mode, cols_padded=True)
         self._mark(li, "gemm", "end")
 
     def exchange(self, li: int) -> None:
@@ -534,7 +534,7 @@ class ShardedModel:
                     if landing is not None:
                         d_X[a:b].copy_(landing[a:b])
                     ops.matmul(d_X[a:b], L.W, out=self.full[0][a:b, :fo], mode=self.mode,
-                               row_scale=self.scale[a:b] if self._scaled(0) else None)
+                               row_scale=self.scale[a:b] if self._scaled(0) else None, cols_padded=True)
                 if self._scaled(0):
                     ops.gcn_aggregate(A_gcn, B, self._self_rows(0), self.scale, bias=L.b, act=L.act,
                                       out=self.outs[0], seg_begin=sp[q], seg_end=sp[q + 1], carry=q > 0,

@@ -123,9 +123,11 @@ def _csr_call(csrs, fn, *args) -> None:
 # ── dense ops ────────────────────────────────────────────────────────────────
 def matmul(A: torch.Tensor, B: torch.Tensor, bias=None, act=None, alpha: float = 0.0,
            out: Optional[torch.Tensor] = None, mode: str = "exact",
-           row_scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+           row_scale: Optional[torch.Tensor] = None, cols_padded: bool = False) -> torch.Tensor:
     """C = act(A . B + bias)  (TinyGNN matmul, src/ops.cpp:70); with
-    ``row_scale``, C = act(diag(row_scale) . (A . B) + bias)."""
+    ``row_scale``, C = act(diag(row_scale) . (A . B) + bias).  ``cols_padded``:
+    out's rows have room up to round_up(N, 4) columns, which FAST mode may
+    write (act(0)) to store rows 16 bytes at a time."""
     A, B = _dense(A, "A"), _dense(B, "B")
     if A.shape[1] != B.shape[0]:
         raise _lib.InvalidArgument(
@@ -139,21 +141,23 @@ def matmul(A: torch.Tensor, B: torch.Tensor, bias=None, act=None, alpha: float =
     b = _vec(bias)
     if row_scale is not None:
         check(lib.tg_gemm_rowscale_f32(M, N, K, _p(A), _ld(A), _p(B), _ld(B), _p(out), _ld(out), _p(row_scale),
-                                       _p(b), ACT[act], alpha, MODE[mode], _stream()))
+                                       _p(b), ACT[act], alpha, MODE[mode] | (FLAG_C_COLS_PADDED if cols_padded else 0),
+                                       _stream()))
         return out
     check(lib.tg_gemm_f32(M, N, K, _p(A), _ld(A), _p(B), _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha,
-                          MODE[mode], _stream()))
+                          MODE[mode] | (FLAG_C_COLS_PADDED if cols_padded else 0), _stream()))
     return out
 
 
 def gemm_pair(A: torch.Tensor, B1: torch.Tensor, B2: torch.Tensor, out1: torch.Tensor, out2: torch.Tensor,
-              mode: str = "fast"):
-    """out1 = A . B1, out2 = A . B2 (one tensor-core pass over A in FAST mode)."""
+              mode: str = "fast", cols_padded: bool = False):
+    """out1 = A . B1, out2 = A . B2 (one tensor-core pass over A in FAST mode);
+    ``cols_padded`` as in matmul, for both outputs."""
     A, B1, B2 = _dense(A, "A"), _dense(B1, "B1").contiguous(), _dense(B2, "B2").contiguous()
     M, K = A.shape
     N = B1.shape[1]
     check(lib.tg_gemm_pair_f32(M, N, K, _p(A), _ld(A), _p(B1), _p(B2), N, _p(out1), _ld(out1), _p(out2), _ld(out2),
-                               MODE[mode], _stream()))
+                               MODE[mode] | (FLAG_C_COLS_PADDED if cols_padded else 0), _stream()))
     return out1, out2
 
 
@@ -241,6 +245,7 @@ def add_bias_(X: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
 
 # ── sparse ops ───────────────────────────────────────────────────────────────
 FLAG_B_ROWS_PADDED = 0x100
+FLAG_C_COLS_PADDED = 0x200
 
 
 def _padded(t: torch.Tensor) -> bool:
@@ -579,7 +584,7 @@ def gemm_peers(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, peer_out, pe
     pf = (C.c_void_p * max(1, n))(*peer_flags)
     b = _vec(bias)
     check(lib.tg_gemm_peers_f32(M, N, K, _p(A), _ld(A), _p(B), _ld(B), _p(out), _ld(out), _p(b), ACT[act], alpha,
-                                _p(row_scale), n, pc, pf, 0x200 if cols_padded else 0, _stream()))
+                                _p(row_scale), n, pc, pf, FLAG_C_COLS_PADDED if cols_padded else 0, _stream()))
     return out
 
 
