@@ -15,6 +15,12 @@
 //    warps 2-5   split each A tile into Ah (in place) / Al in shared memory,
 //                then run the epilogue: TMEM -> registers, + bias,
 //                activation, store.
+//  The persistent form (gemm_tcp_kernel, further down) walks several tiles
+//  per CTA with two TMEM accumulators, so a tile's epilogue -- including its
+//  stores to peer GPUs' copies -- overlaps the next tile's main loop; it is
+//  chosen for long K with 16-byte-aligned outputs (use_persistent).
+//  Nothing is written past an output's N columns unless the caller declares
+//  row padding writable (a TMA store writes whole 16-byte pieces of a row).
 //  Every mbarrier wait is bounded; a wait that runs out records a code in
 //  a device error word, the CTA drains its copies, frees TMEM and returns.
 //  A is read once from HBM (the tile's B^T comes from L2): the kernel is
